@@ -1,0 +1,311 @@
+"""Generate the golden fixtures in this directory from the reference itself.
+
+Runs the reference llm-compressor (imported through ``ref_shim``) on CPU over
+seeded synthetic inputs and stores inputs and outputs as ``.npz`` files:
+
+* ``modelfree_<scheme>.npz`` -- the model-free per-tensor path
+  (``S/entrypoints/model_free/lifecycle.py:38-60`` then
+  ``CT/compressors/base.py:145`` ``compress_module``): bf16 weight in,
+  compressed-tensors state dict out (packed codes, scales, global scale).
+* ``observer_<case>.npz`` -- memoryless min-max statistics and
+  ``calculate_qparams`` output (``S/observers/min_max.py:106-110``,
+  ``S/observers/base.py:99-123``).
+* ``hessian.npz`` -- ``accumulate_hessian`` over several calls
+  (``S/modifiers/gptq/gptq_quantize.py:63-97``).
+* ``gptq_<case>.npz`` -- ``quantize_weight``
+  (``S/modifiers/gptq/gptq_quantize.py:100-296``) on a Hessian built from
+  seeded activations.
+
+bf16 tensors are stored as ``uint16`` bit patterns, fp8 as ``uint8``.
+Only run in a container that holds the reference checkout:
+``python tests/golden/make_golden.py``.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import ref_shim  # noqa: E402
+
+ref_shim.install()
+
+from compressed_tensors.compressors import compress_module  # noqa: E402
+from compressed_tensors.quantization import (  # noqa: E402
+    QuantizationArgs,
+    QuantizationScheme,
+    initialize_module_for_quantization,
+)
+from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme  # noqa: E402
+
+from llmcompressor.modifiers.gptq.gptq_quantize import (  # noqa: E402
+    accumulate_hessian,
+    make_empty_hessian,
+    quantize_weight,
+)
+from llmcompressor.modifiers.quantization.calibration import (  # noqa: E402
+    apply_calibration_status,
+    freeze_module_quantization,
+    initialize_observer,
+    observe,
+    update_qparams,
+)
+from llmcompressor.observers import Observer  # noqa: E402
+from llmcompressor.observers.helpers import fuse_weight_observers  # noqa: E402
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.uint16).numpy().astype(np.uint16)
+    if t.dtype == torch.float8_e4m3fn:
+        return t.view(torch.uint8).numpy()
+    return t.numpy()
+
+
+def make_weight(rows: int, cols: int, seed: int, kind: str = "normal") -> torch.Tensor:
+    """Seeded bf16 weights with the value features the casts must handle."""
+    g = torch.Generator().manual_seed(seed)
+    if kind == "student_t":
+        # Student-t(nu=4) rows scaled by 0.02: heavy tails
+        z = torch.randn(rows, cols, generator=g)
+        chi = torch.distributions.Chi2(torch.tensor(4.0)).sample((rows, 1))
+        w = 0.02 * z / torch.sqrt(chi / 4.0)
+    else:
+        w = 0.02 * torch.randn(rows, cols, generator=g)
+        mask = torch.rand(rows, cols, generator=g) < 0.001
+        w = torch.where(mask, w * 50.0, w)
+    # edge cases: an all-zero row, an all-positive row, a row of tiny values
+    if rows >= 4:
+        w[0, :] = 0.0
+        w[1, :] = w[1, :].abs()
+        w[2, :] = w[2, :] * 1e-6
+        w[3, : cols // 2] = -w[3, : cols // 2].abs()
+    return w.to(torch.bfloat16)
+
+
+# --------------------------------------------------------------------------
+# model-free path
+# --------------------------------------------------------------------------
+
+
+def modelfree_one(weight: torch.Tensor, scheme: QuantizationScheme) -> dict:
+    """``initialize_quantized_linear`` + ``calibrate_weight`` + ``compress_module``.
+
+    Version-skew notes for the installed compressed-tensors 0.15.0.1:
+
+    * NVFP4: the scale is held in fp32 until ``compress_module``; the installed
+      version rejects fp8/fp32 promotion in ``scale / global_scale``.  The fp32
+      scale is already fp8-rounded by ``calculate_qparams``, so no value changes.
+    * MXFP4: the scale is held in the weight dtype (compressed-tensors' own
+      default scale dtype) until ``compress_module``, which encodes it as E8M0.
+      Casting it to uint8 before calibration (``lifecycle.py:48-50``) would
+      truncate the power-of-two scales through ``copy_``.
+    """
+    out_f, in_f = weight.shape
+    module = torch.nn.Linear(in_f, out_f, bias=False, dtype=weight.dtype)
+    module.weight.data.copy_(weight)
+    initialize_module_for_quantization(module, scheme, force_zero_point=False)
+    sd = scheme.weights.scale_dtype
+    is_fp4 = scheme.weights.num_bits == 4 and scheme.weights.type == "float"
+    if sd is not None and hasattr(module, "weight_scale") and not is_fp4:
+        module.weight_scale.data = module.weight_scale.data.to(sd)
+    if is_fp4 and scheme.weights.group_size == 16:
+        module.weight_scale.data = module.weight_scale.data.to(torch.float32)
+    initialize_observer(module, "weight")
+    apply_calibration_status(module)
+    observe(module, base_name="weight")
+    update_qparams(module, base_name="weight")
+    freeze_module_quantization(module)
+    compress_module(module)
+    return {k: v for k, v in module.state_dict().items()}
+
+
+def gen_modelfree():
+    cases = [
+        ("W4A16", 64, 512, "normal"),
+        ("W4A16_ASYM", 64, 512, "normal"),
+        ("W8A16", 64, 256, "normal"),
+        ("FP8_DYNAMIC", 64, 256, "student_t"),
+        ("FP8", 64, 256, "normal"),
+        ("FP8_BLOCK", 200, 300, "student_t"),
+        ("MXFP4A16", 64, 256, "student_t"),
+        ("NVFP4A16", 64, 256, "normal"),
+    ]
+    for i, (name, r, c, kind) in enumerate(cases):
+        w = make_weight(r, c, seed=100 + i, kind=kind)
+        scheme = preset_name_to_scheme(name, ["Linear"])
+        sd = modelfree_one(w, scheme)
+        arrays = {"weight": to_np(w)}
+        for k, v in sd.items():
+            arrays["out_" + k] = to_np(v)
+        np.savez_compressed(os.path.join(HERE, f"modelfree_{name}.npz"), **arrays)
+        print("modelfree", name, {k: (v.shape, v.dtype) for k, v in arrays.items()})
+
+
+def gen_nvfp4_fused():
+    """NVFP4 with q/k/v sharing one global scale (``S/observers/helpers.py:161-216``)."""
+
+    class Attn(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.q_proj = torch.nn.Linear(256, 128, bias=False, dtype=torch.bfloat16)
+            self.k_proj = torch.nn.Linear(256, 64, bias=False, dtype=torch.bfloat16)
+            self.v_proj = torch.nn.Linear(256, 64, bias=False, dtype=torch.bfloat16)
+
+    m = Attn()
+    ws = {}
+    for j, n in enumerate(("q_proj", "k_proj", "v_proj")):
+        w = make_weight(getattr(m, n).out_features, 256, seed=200 + j)
+        if n == "k_proj":
+            w[5, 7] = 3.0  # the fused absmax lives in k_proj
+        getattr(m, n).weight.data.copy_(w)
+        ws[n] = w
+    scheme = preset_name_to_scheme("NVFP4A16", ["Linear"])
+    for n in ("q_proj", "k_proj", "v_proj"):
+        mod = getattr(m, n)
+        initialize_module_for_quantization(mod, scheme, force_zero_point=False)
+        mod.weight_scale.data = mod.weight_scale.data.to(torch.float32)
+        initialize_observer(mod, "weight")
+        apply_calibration_status(mod)
+    fuse_weight_observers(m)
+    arrays = {}
+    for n in ("q_proj", "k_proj", "v_proj"):
+        mod = getattr(m, n)
+        observe(mod, base_name="weight")
+        update_qparams(mod, base_name="weight")
+    for n in ("q_proj", "k_proj", "v_proj"):
+        mod = getattr(m, n)
+        freeze_module_quantization(mod)
+        compress_module(mod)
+        arrays[f"{n}_weight"] = to_np(ws[n])
+        for k, v in mod.state_dict().items():
+            arrays[f"{n}_out_{k}"] = to_np(v)
+    np.savez_compressed(os.path.join(HERE, "modelfree_NVFP4A16_fused_qkv.npz"), **arrays)
+    print("nvfp4 fused", sorted(arrays))
+
+
+# --------------------------------------------------------------------------
+# observers
+# --------------------------------------------------------------------------
+
+
+def gen_observers():
+    cases = {
+        "int4_sym_group128": QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=128),
+        "int4_asym_group128": QuantizationArgs(num_bits=4, type="int", symmetric=False, strategy="group", group_size=128),
+        "int8_sym_channel": QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="channel"),
+        "int4_sym_tensor": QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="tensor"),
+        "fp8_block_128": QuantizationArgs(num_bits=8, type="float", symmetric=True, strategy="block", block_structure=[128, 128]),
+        "int8_asym_channel": QuantizationArgs(num_bits=8, type="int", symmetric=False, strategy="channel"),
+    }
+    for i, (name, args) in enumerate(cases.items()):
+        r, c = (200, 300) if "block" in name else (96, 512)
+        w = make_weight(r, c, seed=300 + i)
+        obs = Observer.load_from_registry("memoryless_minmax", base_name="weight", args=args)
+        obs(w)
+        mn, mx = obs.min_vals.clone(), obs.max_vals.clone()
+        qp = obs.get_qparams()
+        np.savez_compressed(
+            os.path.join(HERE, f"observer_{name}.npz"),
+            weight=to_np(w),
+            min_vals=to_np(mn),
+            max_vals=to_np(mx),
+            scale=to_np(qp["scale"]),
+            zero_point=to_np(qp["zero_point"]),
+        )
+        print("observer", name, tuple(mn.shape), qp["scale"].dtype, qp["zero_point"].dtype)
+
+
+# --------------------------------------------------------------------------
+# Hessian + GPTQ
+# --------------------------------------------------------------------------
+
+
+def gen_hessian():
+    g = torch.Generator().manual_seed(7)
+    d = 192
+    lin = torch.nn.Linear(d, 64, bias=False, dtype=torch.bfloat16)
+    H = make_empty_hessian(lin)
+    n = torch.zeros(())
+    xs = []
+    for s in range(3):
+        x = torch.randn(1, 80 + 16 * s, d, generator=g).to(torch.bfloat16)
+        xs.append(to_np(x[0]))
+        H, n = accumulate_hessian(x, lin, H, n)
+    arrays = {f"x{i}": x for i, x in enumerate(xs)}
+    arrays.update(H=to_np(H), num_samples=to_np(n))
+    np.savez_compressed(os.path.join(HERE, "hessian.npz"), **arrays)
+    print("hessian", H.shape, float(n))
+
+
+def gptq_case(name, rows, cols, args, dead_cols=(), seed=11, tokens=512):
+    g = torch.Generator().manual_seed(seed)
+    w = make_weight(rows, cols, seed=seed + 1)
+    lin = torch.nn.Linear(cols, rows, bias=False, dtype=torch.bfloat16)
+    lin.weight.data.copy_(w)
+    # correlated activations: x = z @ M with a random mixing matrix
+    mix = torch.randn(cols, cols, generator=g) / cols**0.5 + torch.eye(cols)
+    H = make_empty_hessian(lin)
+    n = torch.zeros(())
+    xs = []
+    for s in range(4):
+        x = (torch.randn(tokens // 4, cols, generator=g) @ mix).to(torch.bfloat16)
+        for dc in dead_cols:
+            x[:, dc] = 0
+        xs.append(to_np(x))
+        H, n = accumulate_hessian(x.unsqueeze(0), lin, H, n)
+    Hn = H / n
+    scheme = QuantizationScheme(targets=["Linear"], weights=args)
+    initialize_module_for_quantization(lin, scheme, force_zero_point=False)
+    initialize_observer(lin, "weight")
+    observe(lin, base_name="weight")
+    loss, qd = quantize_weight(lin, args, Hn.clone(), blocksize=128, percdamp=0.01)
+    arrays = {
+        "weight": to_np(w),
+        "x": np.stack(xs),
+        "hessian": to_np(Hn),
+        "loss": np.array(loss, dtype=np.float64),
+        "out_weight": to_np(qd["weight"]),
+        "out_scale": to_np(qd["weight_scale"]),
+        "out_zero_point": to_np(qd["weight_zero_point"]),
+    }
+    np.savez_compressed(os.path.join(HERE, f"gptq_{name}.npz"), **arrays)
+    print("gptq", name, loss)
+
+
+def gen_gptq():
+    gptq_case(
+        "int4_group128",
+        128,
+        384,
+        QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=128, actorder=None),
+    )
+    gptq_case(
+        "int4_channel_dead",
+        96,
+        256,
+        QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="channel", actorder=None),
+        dead_cols=(3, 100, 255),
+        seed=21,
+    )
+    gptq_case(
+        "int8_group64_asym",
+        64,
+        320,
+        QuantizationArgs(num_bits=8, type="int", symmetric=False, strategy="group", group_size=64, actorder=None),
+        seed=31,
+    )
+
+
+if __name__ == "__main__":
+    torch.manual_seed(0)
+    gen_observers()
+    gen_modelfree()
+    gen_nvfp4_fused()
+    gen_hessian()
+    gen_gptq()

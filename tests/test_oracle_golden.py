@@ -1,0 +1,177 @@
+"""Pin the CPU oracle to the reference: every oracle function against the
+golden fixtures made by running the reference itself (tests/golden/make_golden.py),
+plus the reference's own known-answer tests.  CPU only."""
+import numpy as np
+import pytest
+
+from oracle import casts, gptq, numerics, observers
+from oracle.observers import QArgs
+from golden_io import bf16, load
+
+OBS_CASES = {
+    "int4_sym_group128": QArgs(4, "int", True, "group", 128),
+    "int4_asym_group128": QArgs(4, "int", False, "group", 128),
+    "int8_sym_channel": QArgs(8, "int", True, "channel", None),
+    "int4_sym_tensor": QArgs(4, "int", True, "tensor", None),
+    "fp8_block_128": QArgs(8, "float", True, "block", None, (128, 128), zp_dtype="fp8"),
+    "int8_asym_channel": QArgs(8, "int", False, "channel", None),
+}
+
+
+@pytest.mark.parametrize("case", sorted(OBS_CASES))
+def test_observer_qparams_bit_exact(case):
+    g = load(f"observer_{case}")
+    args = OBS_CASES[case]
+    w = bf16(g["weight"])
+    mn, mx = observers.minmax(w, args)
+    np.testing.assert_array_equal(numerics.f32_to_bf16_bits(mn), g["min_vals"].reshape(mn.shape))
+    np.testing.assert_array_equal(numerics.f32_to_bf16_bits(mx), g["max_vals"].reshape(mx.shape))
+    scale, zp = observers.calculate_qparams(mn, mx, args)
+    np.testing.assert_array_equal(numerics.f32_to_bf16_bits(scale), g["scale"].reshape(scale.shape))
+    if args.zp_dtype == "int8":
+        np.testing.assert_array_equal(zp, g["zero_point"].reshape(zp.shape))
+
+
+@pytest.mark.parametrize("scheme", ["W4A16", "W4A16_ASYM", "W8A16", "FP8_DYNAMIC", "FP8", "FP8_BLOCK", "MXFP4A16", "NVFP4A16"])
+def test_modelfree_bit_exact(scheme):
+    g = load(f"modelfree_{scheme}")
+    w = bf16(g["weight"])
+    out = casts.modelfree_tensor(w, scheme)
+    for k, v in out.items():
+        ref = g["out_" + k]
+        if k == "weight_scale" and v.dtype == np.float32:
+            v = numerics.f32_to_bf16_bits(v)
+        np.testing.assert_array_equal(np.asarray(v).reshape(ref.shape), ref, err_msg=f"{scheme}:{k}")
+    assert set("out_" + k for k in out) <= set(g)
+
+
+def test_nvfp4_fused_global_scale_bit_exact():
+    g = load("modelfree_NVFP4A16_fused_qkv")
+    names = ("q_proj", "k_proj", "v_proj")
+    ws = [bf16(g[f"{n}_weight"]) for n in names]
+    gs = casts.nvfp4_global_scale(ws)
+    for n, w in zip(names, ws):
+        out = casts.modelfree_tensor(w, "NVFP4A16", global_scale=gs)
+        for k, v in out.items():
+            np.testing.assert_array_equal(np.asarray(v).reshape(g[f"{n}_out_{k}"].shape), g[f"{n}_out_{k}"], err_msg=f"{n}:{k}")
+
+
+def test_hessian_matches_reference():
+    g = load("hessian")
+    d = g["H"].shape[0]
+    H = np.zeros((d, d), np.float32)
+    n = 0
+    for i in range(3):
+        H, n = gptq.accumulate_hessian(bf16(g[f"x{i}"]), H, n)
+    assert n == float(g["num_samples"])
+    rel = np.linalg.norm(H - g["H"]) / np.linalg.norm(g["H"])
+    assert rel <= 1e-5, rel
+
+
+GPTQ_CASES = {
+    "int4_group128": QArgs(4, "int", True, "group", 128),
+    "int4_channel_dead": QArgs(4, "int", True, "channel", None),
+    "int8_group64_asym": QArgs(8, "int", False, "group", 64),
+}
+
+
+@pytest.mark.parametrize("case", sorted(GPTQ_CASES))
+def test_gptq_oracle_matches_reference(case):
+    g = load(f"gptq_{case}")
+    args = GPTQ_CASES[case]
+    w = bf16(g["weight"])
+    loss, wq, scale, zp, ok = gptq.quantize_weight(w, g["hessian"], args)
+    assert ok
+    np.testing.assert_array_equal(numerics.f32_to_bf16_bits(scale), g["out_scale"].reshape(scale.shape))
+    ref_wq = bf16(g["out_weight"])
+    codes = gptq.codes_from_weight(wq, scale, zp, args)
+    ref_codes = gptq.codes_from_weight(ref_wq, scale, zp, args)
+    agree = float(np.mean(codes == ref_codes))
+    assert agree >= 0.99, agree
+    assert abs(loss - float(g["loss"])) <= 0.01 * abs(float(g["loss"]))
+    x = bf16(g["x"])
+    e_ref = gptq.layer_output_error(w, ref_wq, x)
+    e_new = gptq.layer_output_error(w, wq, x)
+    assert abs(e_new - e_ref) <= 0.01 * e_ref, (e_new, e_ref)
+
+
+# --- known-answer tests of the reference's own suite -------------------------
+# T/llmcompressor/modifiers/calibration/test_lifecycle.py:16-121: weight = arange(24) as 4x6 bf16
+LIFECYCLE = [
+    (QArgs(4, "int", True, "tensor", None), [0.0], [23.0],
+     [[0.0, 0.0, 3.0625, 3.0625, 3.0625, 6.125], [6.125, 6.125, 9.1875, 9.1875, 9.1875, 12.25],
+      [12.25, 12.25, 15.3125, 15.3125, 15.3125, 18.375], [18.375, 18.375, 21.5, 21.5, 21.5, 21.5]]),
+    (QArgs(4, "int", True, "channel", None), [[0], [6], [12], [18]], [[5], [11], [17], [23]],
+     [[0.0, 1.3359, 2.0, 2.6719, 4.0, 4.6875], [5.875, 7.3438, 7.3438, 8.8125, 10.25, 10.25],
+      [11.3125, 13.625, 13.625, 15.875, 15.875, 15.875], [18.375, 18.375, 21.5, 21.5, 21.5, 21.5]]),
+    (QArgs(4, "int", True, "group", 3), [[0, 3], [6, 9], [12, 15], [18, 21]], [[2, 5], [8, 11], [14, 17], [20, 23]],
+     [[0.0, 1.0703, 1.875, 2.6719, 4.0, 4.6875], [6.4375, 7.5, 7.5, 8.8125, 10.25, 10.25],
+      [11.1875, 13.0625, 13.0625, 15.875, 15.875, 15.875], [18.75, 18.75, 18.75, 21.5, 21.5, 21.5]]),
+    (QArgs(4, "float", True, "tensor_group", 3, scale_dtype="fp8", zp_dtype="fp8"),
+     [[0, 3], [6, 9], [12, 15], [18, 21]], [[2, 5], [8, 11], [14, 17], [20, 23]],
+     [[0.0, 1.0234, 2.0469, 3.2812, 3.2812, 4.9375], [5.4688, 8.1875, 8.1875, 10.6875, 10.6875, 10.6875],
+      [9.875, 14.75, 14.75, 16.375, 16.375, 16.375], [19.75, 19.75, 19.75, 23.0, 23.0, 23.0]]),
+    (QArgs(4, "int", True, "block", None, (2, 3)), [[0, 3], [12, 15]], [[8, 11], [20, 23]],
+     [[0.0, 1.0703, 2.1406, 2.9375, 4.4062, 4.4062], [6.4375, 7.5, 7.5, 8.8125, 10.25, 10.25],
+      [10.6875, 13.375, 13.375, 15.3125, 15.3125, 18.375], [18.75, 18.75, 18.75, 21.5, 21.5, 21.5]]),
+]
+
+
+def _fake_quant_weight(w, args):
+    """Weight fake-quant of a bf16 weight (forward_quantize on the weight)."""
+    mn, mx = observers.minmax(w, args)
+    gsc = None
+    if args.strategy == "tensor_group":
+        gsc = observers.generate_gparam(observers.fused_absmax([(mn, mx)]))
+    scale, zp = observers.calculate_qparams(mn, mx, args, global_scale=gsc)
+    s = casts.expand_scale(scale, args, w.shape)
+    lo, hi = observers.calculate_range(args)
+    if args.type == "float":
+        eff = (s / np.float32(gsc)).astype(np.float32)
+        q = numerics.cast_to_fp4(np.clip((w / eff).astype(np.float32), lo, hi))
+        return mn, mx, numerics.rb((q * eff).astype(np.float32))
+    q = np.rint(np.clip(numerics.rb(w / s), lo, hi)).astype(np.float32)
+    return mn, mx, numerics.rb(q * s)
+
+
+@pytest.mark.parametrize("idx", range(len(LIFECYCLE)))
+def test_reference_lifecycle_known_answers(idx):
+    args, exp_min, exp_max, exp_q = LIFECYCLE[idx]
+    w = np.arange(24, dtype=np.float32).reshape(4, 6)
+    mn, mx, fq = _fake_quant_weight(w, args)
+    np.testing.assert_array_equal(mn.reshape(-1), np.asarray(exp_min, np.float32).reshape(-1))
+    np.testing.assert_array_equal(mx.reshape(-1), np.asarray(exp_max, np.float32).reshape(-1))
+    # the reference compares with torch.allclose (rtol 1e-5, atol 1e-8) against 4-5 digit values
+    np.testing.assert_allclose(fq, np.asarray(exp_q, np.float32), rtol=1e-3, atol=1e-3)
+
+
+def test_reference_min_max_known_answers():
+    """T/llmcompressor/observers/test_min_max.py:8-29: int8 on [1,1,1,1,1]."""
+    x = np.ones((1, 5), np.float32)
+    for sym, exp_s, exp_zp in ((True, 0.0078, 0), (False, 0.0039, -128)):
+        args = QArgs(8, "int", sym, "tensor", None)
+        mn, mx = observers.minmax(x, args)
+        s, zp = observers.calculate_qparams(mn, mx, args, dtype="f32")
+        assert round(float(s[0]), 4) == exp_s and int(zp[0]) == exp_zp
+
+
+def test_fp8_rounding_exhaustive_against_torch():
+    """The fp8 restatement against torch's own float -> e4m3fn cast for every bf16 value."""
+    import torch
+
+    u = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    x = bf16(u)
+    x = x[np.isfinite(x)]
+    x = np.clip(x, -448, 448)
+    ours = numerics.fp8_e4m3_bits(numerics.round_fp8_e4m3(x))
+    ref = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(ours, ref)
+
+
+def test_bf16_rounding_against_torch():
+    import torch
+
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(200000) * np.exp(rng.uniform(-30, 30, 200000))).astype(np.float32)
+    ref = torch.from_numpy(x).to(torch.bfloat16).view(torch.uint16).numpy()
+    np.testing.assert_array_equal(numerics.f32_to_bf16_bits(x), ref)
