@@ -1,0 +1,134 @@
+/*
+ * llmc_b200.h -- C ABI of the B200 (sm_100a) kernels for llm-compressor's
+ * post-training-quantization hot path.
+ *
+ * Conventions
+ *  - Every entry point is `extern "C"`, takes plain device pointers, int64
+ *    sizes and a `cudaStream_t` passed as `void*`, and returns an LlmcStatus.
+ *    Nothing here allocates memory visible to the caller; scratch space is a
+ *    caller-provided workspace whose size a *_workspace_size() call reports.
+ *  - Nothing synchronises the stream.  Errors detected on the device (a
+ *    non-positive-definite Hessian, a bounded wait that ran out) are written
+ *    to a caller-provided device status word, never raised as a trap.
+ *  - Tensors are row-major and contiguous unless a leading dimension is given.
+ *  - bf16 values travel as uint16 bit patterns, fp8 as uint8.
+ *
+ * Each declaration names the reference interface it replaces
+ * (S/ = llm-compressor src/llmcompressor/, CT/ = compressed-tensors).
+ */
+#ifndef LLMC_B200_H
+#define LLMC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum LlmcStatus {
+  LLMC_OK = 0,
+  LLMC_EINVAL_SHAPE = 1, /* maps to ValueError (shape / divisibility)          */
+  LLMC_EINVAL_DTYPE = 2, /* maps to ValueError (dtype)                          */
+  LLMC_ENOT_PD = 3,      /* Hessian not positive definite -> RTN fallback        */
+  LLMC_ETIMEOUT = 4,     /* a bounded device-side wait ran out                   */
+  LLMC_ECUDA = 5,        /* a CUDA runtime call failed                           */
+  LLMC_EINVAL_ARG = 6,   /* bad argument (null pointer, unsupported option)      */
+  LLMC_ENOSUPPORT = 7    /* combination not supported by this build -> NotImplementedError */
+} LlmcStatus;
+
+/* QuantizationStrategy (CT/quantization/quant_args.py QuantizationStrategy) */
+enum { LLMC_STRAT_TENSOR = 0, LLMC_STRAT_CHANNEL = 1, LLMC_STRAT_GROUP = 2,
+       LLMC_STRAT_TENSOR_GROUP = 3, LLMC_STRAT_BLOCK = 4 };
+/* scale storage dtype (QuantizationArgs.scale_dtype; NONE = the weight dtype, bf16) */
+enum { LLMC_SCALE_NONE = 0, LLMC_SCALE_FP8 = 1, LLMC_SCALE_U8 = 2, LLMC_SCALE_F32 = 3 };
+/* zero-point dtype (QuantizationArgs.zp_dtype) */
+enum { LLMC_ZP_INT8 = 0, LLMC_ZP_FP8 = 1, LLMC_ZP_UINT8 = 2 };
+
+/* The QuantizationArgs fields the hot path reads (CT/quantization/quant_args.py). */
+typedef struct LlmcQuantArgs {
+  int32_t num_bits;    /* 4 or 8                                   */
+  int32_t type;        /* 0 = int, 1 = float                       */
+  int32_t symmetric;   /* 1 = symmetric                            */
+  int32_t strategy;    /* LLMC_STRAT_*                              */
+  int64_t group_size;  /* GROUP / TENSOR_GROUP                      */
+  int64_t block_rows;  /* BLOCK: block_structure[0]                 */
+  int64_t block_cols;  /* BLOCK: block_structure[1]                 */
+  int32_t scale_dtype; /* LLMC_SCALE_*                              */
+  int32_t zp_dtype;    /* LLMC_ZP_*                                 */
+} LlmcQuantArgs;
+
+/* Output formats of the compressors (CT/compressors/*). */
+enum { LLMC_FMT_PACK_INT32 = 0, /* pack_quantized: int codes, 32/num_bits per int32 */
+       LLMC_FMT_FP8 = 1,        /* naive/float_quantized: float8_e4m3fn weight       */
+       LLMC_FMT_NVFP4 = 2,      /* nvfp4_pack_quantized: E2M1 pairs + fp8 scales     */
+       LLMC_FMT_MXFP4 = 3,      /* mxfp4_pack_quantized: E2M1 pairs + E8M0 scales    */
+       LLMC_FMT_INT8 = 4 };     /* int8 codes, unpacked                               */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int llmc_version(void);
+/* Static description of a status code. */
+const char* llmc_status_string(int status);
+
+/* ---------------------------------------------------------------- observers
+ * Memoryless min-max statistics of a bf16 weight (rows x cols):
+ * S/observers/min_max.py:16-25,106-110 (`_get_min_max` over the view built by
+ * `_flatten_weight`, S/observers/helpers.py:63-102).  Outputs are bf16 with
+ * shapes: TENSOR (1), CHANNEL (rows,1), GROUP/TENSOR_GROUP (rows, cols/group),
+ * BLOCK (ceil(rows/bh), ceil(cols/bw)) -- blocks zero-padded as
+ * `maybe_pad_tensor_for_block_quant`. */
+int llmc_observe_minmax(const void* w_bf16, int64_t rows, int64_t cols, const LlmcQuantArgs* args,
+                        void* min_bf16, void* max_bf16, void* stream);
+
+/* Absolute maximum of `n` bf16 values, max-accumulated into *absmax_f32
+ * (initialise it to 0).  Used for fused-set NVFP4 global scales:
+ * `Observer.get_global_scale`, S/observers/base.py:78-96. */
+int llmc_absmax_accumulate(const void* w_bf16, int64_t n, float* absmax_f32, void* stream);
+
+/* generate_gparam (CT/quantization/utils/helpers.py:309-338) from an absmax:
+ * writes the float32 global scale. */
+int llmc_global_scale(const float* absmax_f32, float* global_scale_f32, void* stream);
+
+/* calculate_qparams (CT/quantization/utils/helpers.py:50-137) over `n`
+ * groups from bf16 min/max.  scale_out dtype: float32 when a global scale
+ * is given, else bf16 (the statistics' dtype; values on the fp8 grid for
+ * scale_dtype FP8, power-of-two values for MX).  zp_out: int8 for
+ * LLMC_ZP_INT8, uint8 for UINT8, float32 zeros for FP8.  global_scale may be
+ * NULL. */
+int llmc_calculate_qparams(const void* min_bf16, const void* max_bf16, int64_t n, const LlmcQuantArgs* args,
+                           const float* global_scale, void* scale_out, void* zp_out, void* stream);
+
+/* ---------------------------------------------------------------- casts
+ * Quantize a bf16 weight with given parameters and pack it in a
+ * compressed-tensors format: `compress` of PackedQuantizationCompressor
+ * (CT/compressors/pack_quantized/base.py:29-78), NaiveQuantizationCompressor
+ * (CT/compressors/naive_quantized/base.py), NVFP4PackedCompressor
+ * (CT/compressors/nvfp4/base.py:23-73) and MXFP4PackedCompressor
+ * (CT/compressors/mxfp4/base.py:20-34).
+ *   scale: bf16 (scale_is_f32 = 0) or float32 (scale_is_f32 = 1), laid out as
+ *          llmc_observe_minmax's statistics; zp: int8 or NULL (symmetric);
+ *   global_scale: float32 scalar or NULL (NVFP4).
+ *   out: PACK_INT32 -> int32 (rows, ceil(cols*bits/32)); FP8 -> uint8 (rows, cols);
+ *        NVFP4/MXFP4 -> uint8 (rows, cols/2); INT8 -> int8 (rows, cols). */
+int llmc_quantize_pack(const void* w_bf16, int64_t rows, int64_t cols, const LlmcQuantArgs* args,
+                       const void* scale, int scale_is_f32, const void* zp_int8, const float* global_scale,
+                       int out_format, void* out, void* stream);
+
+/* Model-free fused path: observe + calculate_qparams + quantize + pack in one
+ * streaming pass over the bf16 weight (S/entrypoints/model_free/lifecycle.py:38-60
+ * then `compress_module`, CT/compressors/base.py:145-166).
+ *   scale_out: bf16 (INT/FP8 schemes), fp8 bytes (NVFP4), E8M0 bytes (MXFP4);
+ *   zp_out: int8 (rows, groups) for asymmetric INT, else NULL;
+ *   global_scale: float32 device scalar, required for TENSOR_GROUP (NVFP4). */
+int llmc_modelfree_quantize(const void* w_bf16, int64_t rows, int64_t cols, const LlmcQuantArgs* args,
+                            const float* global_scale, int out_format, void* packed_out, void* scale_out,
+                            void* zp_out, void* stream);
+
+/* pack_to_int32(zero_point, num_bits, packed_dim=0)
+ * (CT/compressors/pack_quantized/helpers.py:20-89): int8 (rows, groups) ->
+ * int32 (ceil(rows*bits/32), groups). */
+int llmc_pack_zero_point(const int8_t* zp, int64_t rows, int64_t groups, int num_bits, int32_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LLMC_B200_H */

@@ -1,0 +1,11 @@
+"""B200-native (sm_100a) kernels behind llm-compressor's PTQ hot-path API.
+
+The host side mirrors the reference's Python interfaces (``accumulate_hessian``,
+``quantize_weight``, the observer registry, the compressed-tensors compressors,
+``model_free_ptq``); the arithmetic runs in ``libllmc_b200.so`` (C ABI in
+``include/llmc_b200.h``).  There is no CPU fallback: without the library or a
+CUDA device the entry points raise.
+"""
+from . import _lib, ops  # noqa: F401
+
+__version__ = "0.1.0"

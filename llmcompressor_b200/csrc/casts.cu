@@ -1,0 +1,607 @@
+// Observers, qparams, casts and packers of the PTQ hot path (sm_100a).
+//
+// Two kernel shapes cover every strategy:
+//  * k_group_vec   -- GROUP / TENSOR_GROUP with a power-of-two group of 8..256
+//                     columns: one thread per 16-byte chunk (8 bf16), a group
+//                     is 1..32 adjacent lanes reduced with shuffles; single
+//                     pass over HBM (W4A16 g128, NVFP4 g16, MXFP4 g32).
+//  * k_paramgroup  -- one CTA per quantization-parameter group (a row for
+//                     CHANNEL, a 128x128 tile for BLOCK, the whole tensor for
+//                     TENSOR, any odd group): pass 1 reduces min/max, pass 2
+//                     re-reads the group (an L2 hit for rows and tiles) and
+//                     quantizes.
+// Both run in three modes: FUSED (observe + qparams + quantize + pack),
+// STATS (min/max only) and GIVEN (quantize + pack with stored qparams).
+#include "llmc_common.cuh"
+
+#include <algorithm>
+
+namespace llmc {
+
+enum Mode { MODE_FUSED = 0, MODE_STATS = 1, MODE_GIVEN = 2 };
+
+struct CastParams {
+  const uint16_t* w;
+  int64_t rows, cols;
+  QArgs a;
+  int mode;
+  int fmt;
+  // GIVEN inputs
+  const void* scale_in;
+  int scale_in_f32;
+  const int8_t* zp_in;
+  const float* gs;  // global scale (device scalar) or null
+  // outputs
+  void* out;          // packed codes
+  void* scale_out;    // FUSED: bf16 / fp8 byte / e8m0 byte
+  int8_t* zp_out;     // FUSED asymmetric int
+  uint16_t* min_out;  // STATS
+  uint16_t* max_out;
+};
+
+// Per-group quantization state shared by the element routine.
+struct ElemQ {
+  float s;     // scale the element divides by (effective scale for NVFP4)
+  float r;     // RN(1/s)
+  bool fast;   // reciprocal path valid
+  float zp;    // zero point (float) -- only used when has_zp
+  bool has_zp;
+  bool f32q;   // quotient stays float32 (float32 scale) instead of bf16
+  float qmin, qmax;
+};
+
+// Quantized code of one bf16 value as compressed-tensors' quantize() does it.
+//   INT formats: signed integer code; FP8: e4m3 byte; FP4: E2M1 nibble code.
+template <int FMT>
+__device__ __forceinline__ uint32_t quant_code(float x, const ElemQ& e) {
+  if (FMT == LLMC_FMT_NVFP4) {
+    float q = f32_quotient_for_fp4(x, e.s, e.r, e.fast);
+    q = fminf(fmaxf(q, -6.0f), 6.0f);
+    return e2m1_code(q);
+  }
+  float q;
+  if (e.f32q) {
+    q = __fdiv_rn(x, e.s);
+    if (e.has_zp) q = q + e.zp;
+  } else {
+    q = bf16_quotient(x, e.s, e.r, e.fast);
+    if (e.has_zp) q = rbf(q + e.zp);
+  }
+  q = fminf(fmaxf(q, e.qmin), e.qmax);
+  if (FMT == LLMC_FMT_MXFP4) return e2m1_code(q);
+  if (FMT == LLMC_FMT_FP8) return (uint32_t)f_to_e4m3(q);
+  return (uint32_t)(int32_t)rintf(q);  // INT8 / PACK_INT32: signed code
+}
+
+// Per-group qparams -> ElemQ (+ the stored scale bits) in FUSED mode.
+template <int FMT>
+__device__ __forceinline__ ElemQ make_elemq_fused(const CastParams& p, float mn, float mx, float* s_store,
+                                                   float* zp_store) {
+  ElemQ e;
+  bool has_gs = (FMT == LLMC_FMT_NVFP4);
+  float gs = has_gs ? *p.gs : 0.0f;
+  float zp;
+  float s = group_qparams(mn, mx, p.a, has_gs, gs, &zp);
+  *s_store = s;
+  *zp_store = zp;
+  e.s = (FMT == LLMC_FMT_NVFP4) ? __fdiv_rn(s, gs) : s;
+  e.r = scale_recip(e.s, &e.fast);
+  e.zp = zp;
+  e.has_zp = !p.a.symmetric;
+  e.f32q = false;
+  e.qmin = p.a.qmin();
+  e.qmax = p.a.qmax();
+  return e;
+}
+
+template <int FMT>
+__device__ __forceinline__ ElemQ make_elemq_given(const CastParams& p, int64_t gi) {
+  ElemQ e;
+  float s = p.scale_in_f32 ? ((const float*)p.scale_in)[gi] : bf16_to_f(((const uint16_t*)p.scale_in)[gi]);
+  if (FMT == LLMC_FMT_NVFP4) {
+    e.s = __fdiv_rn(s, *p.gs);  // scale / global_scale in float32
+    e.f32q = true;
+  } else {
+    e.s = s;
+    e.f32q = p.scale_in_f32 != 0;  // bf16 / float32 -> float32 quotient
+  }
+  e.r = scale_recip(e.s, &e.fast);
+  e.has_zp = p.zp_in != nullptr;
+  e.zp = e.has_zp ? (float)p.zp_in[gi] : 0.0f;
+  e.qmin = p.a.qmin();
+  e.qmax = p.a.qmax();
+  return e;
+}
+
+template <int FMT>
+__device__ __forceinline__ void store_scale(const CastParams& p, int64_t gi, float s, float zp) {
+  if (FMT == LLMC_FMT_NVFP4) ((uint8_t*)p.scale_out)[gi] = f_to_e4m3(s);
+  else if (FMT == LLMC_FMT_MXFP4) {
+    // compress_mx_scale: 127 + floor(log2(scale)); scale is 2^(e-127)
+    uint32_t b = __float_as_uint(s);
+    uint32_t ex = (b >> 23) & 0xFF;
+    // normal: floor(log2) = ex - 127; subnormal: the top mantissa bit's weight
+    uint32_t e8 = ex ? ex : (uint32_t)((31 - __clz(b & 0x7FFFFF)) - 149 + 127);
+    ((uint8_t*)p.scale_out)[gi] = (uint8_t)e8;
+  } else {
+    ((uint16_t*)p.scale_out)[gi] = f_to_bf16(s);
+  }
+  if (p.zp_out) p.zp_out[gi] = (int8_t)(int32_t)zp;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& v, float* x) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(w[i] << 16);
+    x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Store 8 codes starting at element index `elem` (a multiple of 8).
+template <int FMT>
+__device__ __forceinline__ void store8(const CastParams& p, int64_t elem, const uint32_t* c) {
+  if (FMT == LLMC_FMT_PACK_INT32) {
+    if (p.a.bits == 4) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) word |= ((c[j] + 8u) & 0xFu) << (4 * j);
+      __stcs((uint32_t*)p.out + elem / 8, word);
+    } else {
+      uint2 w2;
+      w2.x = ((c[0] + 128u) & 0xFFu) | (((c[1] + 128u) & 0xFFu) << 8) | (((c[2] + 128u) & 0xFFu) << 16) |
+             (((c[3] + 128u) & 0xFFu) << 24);
+      w2.y = ((c[4] + 128u) & 0xFFu) | (((c[5] + 128u) & 0xFFu) << 8) | (((c[6] + 128u) & 0xFFu) << 16) |
+             (((c[7] + 128u) & 0xFFu) << 24);
+      __stcs((uint2*)p.out + elem / 8, w2);
+    }
+  } else if (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) word |= (c[j] & 0xFu) << (4 * j);
+    __stcs((uint32_t*)((uint8_t*)p.out + elem / 2), word);
+  } else {  // FP8 / INT8 bytes
+    uint2 w2;
+    w2.x = (c[0] & 0xFFu) | ((c[1] & 0xFFu) << 8) | ((c[2] & 0xFFu) << 16) | ((c[3] & 0xFFu) << 24);
+    w2.y = (c[4] & 0xFFu) | ((c[5] & 0xFFu) << 8) | ((c[6] & 0xFFu) << 16) | ((c[7] & 0xFFu) << 24);
+    __stcs((uint2*)((uint8_t*)p.out + elem), w2);
+  }
+}
+
+// ------------------------------------------------------------------------
+// k_group_vec: power-of-two groups of 8..256 columns, cols % group == 0.
+// ------------------------------------------------------------------------
+constexpr int VEC_UNROLL = 4;
+
+template <int FMT, int TPG>
+__global__ void __launch_bounds__(256) k_group_vec(CastParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t total = p.rows * p.cols / 8;  // chunks
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t base = warp * 32 * VEC_UNROLL; base < total; base += nwarps * 32 * VEC_UNROLL) {
+    uint4 v[VEC_UNROLL];
+#pragma unroll
+    for (int u = 0; u < VEC_UNROLL; ++u) {
+      int64_t ch = base + u * 32 + lane;
+      if (ch < total) v[u] = __ldcs((const uint4*)p.w + ch);
+      else v[u] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < VEC_UNROLL; ++u) {
+      int64_t ch = base + u * 32 + lane;
+      bool valid = ch < total;  // a whole group is valid or not (total % TPG == 0)
+      float x[8];
+      unpack8(v[u], x);
+      int64_t gi = ch / TPG;
+      ElemQ e;
+      float s_store = 0.f, zp_store = 0.f;
+      if (p.mode != MODE_GIVEN) {
+        float mn = x[0], mx = x[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) { mn = fminf(mn, x[j]); mx = fmaxf(mx, x[j]); }
+#pragma unroll
+        for (int o = 1; o < TPG; o <<= 1) {
+          mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        if (p.mode == MODE_STATS) {
+          if (valid && (lane % TPG) == 0) { p.min_out[gi] = f_to_bf16(mn); p.max_out[gi] = f_to_bf16(mx); }
+          continue;
+        }
+        e = make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
+      } else {
+        if (!valid) continue;
+        e = make_elemq_given<FMT>(p, gi);
+      }
+      if (!valid) continue;
+      uint32_t c[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) c[j] = quant_code<FMT>(x[j], e);
+      store8<FMT>(p, ch * 8, c);
+      if (p.mode == MODE_FUSED && (lane % TPG) == 0) store_scale<FMT>(p, gi, s_store, zp_store);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------
+// k_paramgroup: one CTA per parameter group.
+// ------------------------------------------------------------------------
+struct Rect { int64_t r0, r1, c0, c1; };
+
+__device__ __forceinline__ Rect group_rect(const CastParams& p, int64_t gi) {
+  Rect R;
+  const QArgs& a = p.a;
+  if (a.strategy == LLMC_STRAT_TENSOR) { R.r0 = 0; R.r1 = p.rows; R.c0 = 0; R.c1 = p.cols; }
+  else if (a.strategy == LLMC_STRAT_CHANNEL) { R.r0 = gi; R.r1 = gi + 1; R.c0 = 0; R.c1 = p.cols; }
+  else if (a.strategy == LLMC_STRAT_BLOCK) {
+    int64_t bc_n = (p.cols + a.bw - 1) / a.bw;
+    int64_t br = gi / bc_n, bc = gi % bc_n;
+    R.r0 = br * a.bh; R.r1 = min(p.rows, R.r0 + a.bh);
+    R.c0 = bc * a.bw; R.c1 = min(p.cols, R.c0 + a.bw);
+  } else {
+    int64_t G = p.cols / a.group;
+    R.r0 = gi / G; R.r1 = R.r0 + 1;
+    R.c0 = (gi % G) * a.group; R.c1 = R.c0 + a.group;
+  }
+  return R;
+}
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* sh) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, t) : fminf(v, t);
+  }
+  __syncthreads();
+  if (lane == 0) sh[wid] = v;
+  __syncthreads();
+  int nw = blockDim.x >> 5;
+  v = sh[0];
+  for (int i = 1; i < nw; ++i) v = is_max ? fmaxf(v, sh[i]) : fminf(v, sh[i]);
+  return v;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) k_paramgroup(CastParams p) {
+  __shared__ float sh[32];
+  const int64_t gi = blockIdx.x;
+  const Rect R = group_rect(p, gi);
+  const int64_t w = R.c1 - R.c0, h = R.r1 - R.r0;
+  const bool vec = ((w & 7) == 0) && ((R.c0 & 7) == 0) && ((p.cols & 7) == 0);
+  ElemQ e;
+  float s_store = 0.f, zp_store = 0.f;
+  if (p.mode != MODE_GIVEN) {
+    float mn = INFINITY, mx = -INFINITY;
+    if (vec) {
+      const int64_t wc = w / 8, n = h * wc;
+      for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        int64_t r = R.r0 + i / wc, c = R.c0 + (i % wc) * 8;
+        uint4 v = __ldg((const uint4*)(p.w + r * p.cols + c));
+        float x[8];
+        unpack8(v, x);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { mn = fminf(mn, x[j]); mx = fmaxf(mx, x[j]); }
+      }
+    } else {
+      const int64_t n = h * w;
+      for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        int64_t r = R.r0 + i / w, c = R.c0 + i % w;
+        float x = bf16_to_f(p.w[r * p.cols + c]);
+        mn = fminf(mn, x); mx = fmaxf(mx, x);
+      }
+    }
+    // zero padding of partial blocks joins the statistics (maybe_pad_tensor_for_block_quant)
+    if (p.a.strategy == LLMC_STRAT_BLOCK && (h < p.a.bh || w < p.a.bw)) { mn = fminf(mn, 0.f); mx = fmaxf(mx, 0.f); }
+    mn = block_reduce(mn, false, sh);
+    mx = block_reduce(mx, true, sh);
+    if (p.mode == MODE_STATS) {
+      if (threadIdx.x == 0) { p.min_out[gi] = f_to_bf16(mn); p.max_out[gi] = f_to_bf16(mx); }
+      return;
+    }
+    e = make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
+    if (threadIdx.x == 0) store_scale<FMT>(p, gi, s_store, zp_store);
+  } else {
+    e = make_elemq_given<FMT>(p, gi);
+  }
+  // pass 2: quantize + pack
+  if (vec && !(FMT == LLMC_FMT_PACK_INT32 && p.a.bits == 4 && (p.cols & 7))) {
+    const int64_t wc = w / 8, n = h * wc;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+      int64_t r = R.r0 + i / wc, c = R.c0 + (i % wc) * 8;
+      uint4 v = __ldg((const uint4*)(p.w + r * p.cols + c));
+      float x[8];
+      unpack8(v, x);
+      uint32_t cd[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cd[j] = quant_code<FMT>(x[j], e);
+      if (FMT == LLMC_FMT_PACK_INT32) {
+        // row-wise packing: element (r, c) -> word r * ceil(cols/pf) + c/pf
+        const int pf = 32 / p.a.bits;
+        const int64_t wpr = (p.cols + pf - 1) / pf;
+        if (p.a.bits == 4) {
+          uint32_t word = 0;
+          for (int j = 0; j < 8; ++j) word |= ((cd[j] + 8u) & 0xFu) << (4 * j);
+          ((uint32_t*)p.out)[r * wpr + c / 8] = word;
+        } else {
+          for (int k = 0; k < 2; ++k) {
+            uint32_t word = 0;
+            for (int j = 0; j < 4; ++j) word |= ((cd[4 * k + j] + 128u) & 0xFFu) << (8 * j);
+            ((uint32_t*)p.out)[r * wpr + c / 4 + k] = word;
+          }
+        }
+      } else if (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) {
+        uint32_t word = 0;
+        for (int j = 0; j < 8; ++j) word |= (cd[j] & 0xFu) << (4 * j);
+        *(uint32_t*)((uint8_t*)p.out + (r * p.cols + c) / 2) = word;
+      } else {
+        uint2 w2;
+        w2.x = (cd[0] & 0xFFu) | ((cd[1] & 0xFFu) << 8) | ((cd[2] & 0xFFu) << 16) | ((cd[3] & 0xFFu) << 24);
+        w2.y = (cd[4] & 0xFFu) | ((cd[5] & 0xFFu) << 8) | ((cd[6] & 0xFFu) << 16) | ((cd[7] & 0xFFu) << 24);
+        *(uint2*)((uint8_t*)p.out + r * p.cols + c) = w2;
+      }
+    }
+  } else {
+    // scalar path: one output word per iteration
+    int pf = 1;
+    if (FMT == LLMC_FMT_PACK_INT32) pf = 32 / p.a.bits;
+    else if (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) pf = 2;
+    const int64_t c0w = R.c0 / pf;
+    const int64_t c1w = (R.c1 + pf - 1) / pf;
+    const int64_t ww = c1w - c0w, n = h * ww;
+    const int64_t wpr = (p.cols + pf - 1) / pf;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+      int64_t r = R.r0 + i / ww, wc = c0w + i % ww;
+      uint32_t word = 0;
+      for (int j = 0; j < pf; ++j) {
+        int64_t c = wc * pf + j;
+        if (c >= p.cols) break;  // padding of the last int32 word stays 0
+        uint32_t cd = quant_code<FMT>(bf16_to_f(p.w[r * p.cols + c]), e);
+        if (FMT == LLMC_FMT_PACK_INT32) word |= ((cd + (1u << (p.a.bits - 1))) & ((1u << p.a.bits) - 1)) << (p.a.bits * j);
+        else if (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) word |= (cd & 0xFu) << (4 * j);
+        else word = cd & 0xFFu;
+      }
+      if (FMT == LLMC_FMT_PACK_INT32) ((uint32_t*)p.out)[r * wpr + wc] = word;
+      else ((uint8_t*)p.out)[r * wpr + wc] = (uint8_t)word;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------
+// small kernels
+// ------------------------------------------------------------------------
+__global__ void k_absmax(const uint16_t* w, int64_t n, float* out) {
+  float m = 0.0f;
+  const int64_t n8 = n / 8;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, st = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = tid; i < n8; i += st) {
+    uint4 v = __ldcs((const uint4*)w + i);
+    float x[8];
+    unpack8(v, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(x[j]));
+  }
+  for (int64_t i = n8 * 8 + tid; i < n; i += st) m = fmaxf(m, fabsf(bf16_to_f(w[i])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax((unsigned int*)out, __float_as_uint(m));  // m >= 0: uint order == float order
+}
+
+__global__ void k_global_scale(const float* absmax, float* gs) { *gs = global_scale_from_absmax(*absmax); }
+
+__global__ void k_qparams(const uint16_t* mn, const uint16_t* mx, int64_t n, QArgs a, const float* gs,
+                          void* scale_out, void* zp_out) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float zp;
+  bool has_gs = gs != nullptr;
+  float s = group_qparams(bf16_to_f(mn[i]), bf16_to_f(mx[i]), a, has_gs, has_gs ? *gs : 0.f, &zp);
+  bool f32out = has_gs;  // otherwise the statistics' dtype (bf16), as round_to_quantized_type_dtype casts back
+  if (f32out) ((float*)scale_out)[i] = s;
+  else ((uint16_t*)scale_out)[i] = f_to_bf16(s);
+  if (zp_out) {
+    if (a.zp_dtype == LLMC_ZP_INT8) ((int8_t*)zp_out)[i] = (int8_t)(int32_t)zp;
+    else if (a.zp_dtype == LLMC_ZP_UINT8) ((uint8_t*)zp_out)[i] = (uint8_t)(int32_t)zp;
+    else ((float*)zp_out)[i] = 0.0f;
+  }
+}
+
+__global__ void k_pack_zp(const int8_t* zp, int64_t rows, int64_t groups, int bits, int32_t* out) {
+  // packed along dim 0: out[(r/pf), g] holds rows r..r+pf-1 of column g
+  const int pf = 32 / bits;
+  const int64_t prow = (rows + pf - 1) / pf;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= prow * groups) return;
+  int64_t pr = i / groups, g = i % groups;
+  uint32_t word = 0;
+  for (int j = 0; j < pf; ++j) {
+    int64_t r = pr * pf + j;
+    if (r >= rows) break;
+    uint32_t v = ((uint32_t)((int32_t)zp[r * groups + g] + (1 << (bits - 1)))) & ((1u << bits) - 1);
+    word |= v << (bits * j);
+  }
+  out[i] = (int32_t)word;
+}
+
+// ------------------------------------------------------------------------
+// host-side dispatch
+// ------------------------------------------------------------------------
+static int n_groups(const CastParams& p) {
+  const QArgs& a = p.a;
+  switch (a.strategy) {
+    case LLMC_STRAT_TENSOR: return 1;
+    case LLMC_STRAT_CHANNEL: return (int)p.rows;
+    case LLMC_STRAT_BLOCK: return (int)(((p.rows + a.bh - 1) / a.bh) * ((p.cols + a.bw - 1) / a.bw));
+    default: return (int)(p.rows * (p.cols / a.group));
+  }
+}
+
+static int validate(const CastParams& p) {
+  const QArgs& a = p.a;
+  if (!p.w || p.rows < 0 || p.cols < 0) return LLMC_EINVAL_ARG;
+  if (a.bits != 4 && a.bits != 8) return LLMC_ENOSUPPORT;
+  if (a.strategy < 0 || a.strategy > LLMC_STRAT_BLOCK) return LLMC_EINVAL_ARG;
+  if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
+    if (a.group <= 0) return LLMC_EINVAL_ARG;
+    if (p.cols % a.group) return LLMC_EINVAL_SHAPE;  // strategy_cdiv(strict=True)
+  }
+  if (a.strategy == LLMC_STRAT_BLOCK && (a.bh <= 0 || a.bw <= 0)) return LLMC_EINVAL_ARG;
+  if (a.is_float && !a.symmetric && a.bits == 4) return LLMC_ENOSUPPORT;  // asymmetric FP4
+  if (p.mode != MODE_STATS) {
+    // a packed word must not straddle two parameter groups
+    int pf = (p.fmt == LLMC_FMT_PACK_INT32) ? 32 / a.bits : (p.fmt == LLMC_FMT_NVFP4 || p.fmt == LLMC_FMT_MXFP4) ? 2 : 1;
+    if ((a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) && (a.group % pf)) return LLMC_ENOSUPPORT;
+    if (a.strategy == LLMC_STRAT_BLOCK && (a.bw % pf) && a.bw < p.cols) return LLMC_ENOSUPPORT;
+  }
+  return LLMC_OK;
+}
+
+template <int FMT>
+static int launch_fmt(const CastParams& p, cudaStream_t st) {
+  const QArgs& a = p.a;
+  bool grp = (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP);
+  int64_t tpg = grp ? a.group / 8 : 0;
+  bool pow2 = grp && (a.group % 8 == 0) && tpg >= 1 && tpg <= 32 && ((tpg & (tpg - 1)) == 0);
+  if (FMT == LLMC_FMT_PACK_INT32 && grp && (a.group * a.bits) % 32) pow2 = false;
+  if (p.rows * p.cols == 0) return LLMC_OK;
+  if (pow2) {
+    int64_t chunks = p.rows * p.cols / 8;
+    int64_t blocks = std::min<int64_t>((chunks + 256 * VEC_UNROLL - 1) / (256 * VEC_UNROLL), 148 * 16);
+    dim3 g((unsigned)std::max<int64_t>(blocks, 1)), b(256);
+    switch (tpg) {
+      case 1: k_group_vec<FMT, 1><<<g, b, 0, st>>>(p); break;
+      case 2: k_group_vec<FMT, 2><<<g, b, 0, st>>>(p); break;
+      case 4: k_group_vec<FMT, 4><<<g, b, 0, st>>>(p); break;
+      case 8: k_group_vec<FMT, 8><<<g, b, 0, st>>>(p); break;
+      case 16: k_group_vec<FMT, 16><<<g, b, 0, st>>>(p); break;
+      default: k_group_vec<FMT, 32><<<g, b, 0, st>>>(p); break;
+    }
+  } else {
+    int ng = n_groups(p);
+    if (ng > 0) k_paramgroup<FMT><<<ng, 256, 0, st>>>(p);
+  }
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+static int launch(const CastParams& p, cudaStream_t st) {
+  switch (p.fmt) {
+    case LLMC_FMT_PACK_INT32: return launch_fmt<LLMC_FMT_PACK_INT32>(p, st);
+    case LLMC_FMT_FP8: return launch_fmt<LLMC_FMT_FP8>(p, st);
+    case LLMC_FMT_NVFP4: return launch_fmt<LLMC_FMT_NVFP4>(p, st);
+    case LLMC_FMT_MXFP4: return launch_fmt<LLMC_FMT_MXFP4>(p, st);
+    case LLMC_FMT_INT8: return launch_fmt<LLMC_FMT_INT8>(p, st);
+    default: return LLMC_EINVAL_ARG;
+  }
+}
+
+static int check_fmt(const QArgs& a, int fmt) {
+  switch (fmt) {
+    case LLMC_FMT_PACK_INT32:
+    case LLMC_FMT_INT8: return a.is_float ? LLMC_EINVAL_DTYPE : LLMC_OK;
+    case LLMC_FMT_FP8: return (a.is_float && a.bits == 8) ? LLMC_OK : LLMC_EINVAL_DTYPE;
+    case LLMC_FMT_NVFP4: return (a.is_float && a.bits == 4 && a.strategy == LLMC_STRAT_TENSOR_GROUP) ? LLMC_OK : LLMC_EINVAL_DTYPE;
+    case LLMC_FMT_MXFP4: return (a.is_float && a.bits == 4 && a.is_mx()) ? LLMC_OK : LLMC_EINVAL_DTYPE;
+    default: return LLMC_EINVAL_ARG;
+  }
+}
+
+}  // namespace llmc
+
+using namespace llmc;
+
+extern "C" {
+
+int llmc_version(void) { return 100; }
+
+const char* llmc_status_string(int s) {
+  switch (s) {
+    case LLMC_OK: return "ok";
+    case LLMC_EINVAL_SHAPE: return "invalid shape";
+    case LLMC_EINVAL_DTYPE: return "invalid dtype";
+    case LLMC_ENOT_PD: return "matrix not positive definite";
+    case LLMC_ETIMEOUT: return "device wait timed out";
+    case LLMC_ECUDA: return "CUDA error";
+    case LLMC_EINVAL_ARG: return "invalid argument";
+    case LLMC_ENOSUPPORT: return "not supported";
+    default: return "unknown status";
+  }
+}
+
+int llmc_observe_minmax(const void* w, int64_t rows, int64_t cols, const LlmcQuantArgs* args, void* mn, void* mx,
+                        void* stream) {
+  if (!args || !mn || !mx) return LLMC_EINVAL_ARG;
+  CastParams p = {};
+  p.w = (const uint16_t*)w; p.rows = rows; p.cols = cols; p.a = to_qargs(*args);
+  p.mode = MODE_STATS; p.fmt = LLMC_FMT_INT8;
+  p.min_out = (uint16_t*)mn; p.max_out = (uint16_t*)mx;
+  int v = validate(p);
+  if (v) return v;
+  return launch_fmt<LLMC_FMT_INT8>(p, (cudaStream_t)stream);
+}
+
+int llmc_absmax_accumulate(const void* w, int64_t n, float* absmax, void* stream) {
+  if (!w || !absmax || n < 0) return LLMC_EINVAL_ARG;
+  if (n == 0) return LLMC_OK;
+  int64_t blocks = std::min<int64_t>((n / 8 + 255) / 256 + 1, 148 * 8);
+  k_absmax<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)w, n, absmax);
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_global_scale(const float* absmax, float* gs, void* stream) {
+  if (!absmax || !gs) return LLMC_EINVAL_ARG;
+  k_global_scale<<<1, 1, 0, (cudaStream_t)stream>>>(absmax, gs);
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_calculate_qparams(const void* mn, const void* mx, int64_t n, const LlmcQuantArgs* args, const float* gs,
+                           void* scale_out, void* zp_out, void* stream) {
+  if (!mn || !mx || !args || !scale_out || n < 0) return LLMC_EINVAL_ARG;
+  QArgs a = to_qargs(*args);
+  if (a.is_float && !a.symmetric && a.bits == 4) return LLMC_ENOSUPPORT;
+  if (n == 0) return LLMC_OK;
+  k_qparams<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint16_t*)mn, (const uint16_t*)mx,
+                                                                            n, a, gs, scale_out, zp_out);
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_quantize_pack(const void* w, int64_t rows, int64_t cols, const LlmcQuantArgs* args, const void* scale,
+                       int scale_is_f32, const void* zp, const float* gs, int fmt, void* out, void* stream) {
+  if (!args || !scale || !out) return LLMC_EINVAL_ARG;
+  CastParams p = {};
+  p.w = (const uint16_t*)w; p.rows = rows; p.cols = cols; p.a = to_qargs(*args);
+  p.mode = MODE_GIVEN; p.fmt = fmt; p.scale_in = scale; p.scale_in_f32 = scale_is_f32;
+  p.zp_in = (const int8_t*)zp; p.gs = gs; p.out = out;
+  int v = validate(p);
+  if (v) return v;
+  if ((v = check_fmt(p.a, fmt))) return v;
+  if (fmt == LLMC_FMT_NVFP4 && !gs) return LLMC_EINVAL_ARG;
+  if ((fmt == LLMC_FMT_NVFP4 || fmt == LLMC_FMT_MXFP4) && (cols & 1)) return LLMC_EINVAL_SHAPE;
+  return launch(p, (cudaStream_t)stream);
+}
+
+int llmc_modelfree_quantize(const void* w, int64_t rows, int64_t cols, const LlmcQuantArgs* args, const float* gs,
+                            int fmt, void* out, void* scale_out, void* zp_out, void* stream) {
+  if (!args || !out || !scale_out) return LLMC_EINVAL_ARG;
+  CastParams p = {};
+  p.w = (const uint16_t*)w; p.rows = rows; p.cols = cols; p.a = to_qargs(*args);
+  p.mode = MODE_FUSED; p.fmt = fmt; p.gs = gs; p.out = out; p.scale_out = scale_out;
+  p.zp_out = p.a.symmetric ? nullptr : (int8_t*)zp_out;
+  int v = validate(p);
+  if (v) return v;
+  if ((v = check_fmt(p.a, fmt))) return v;
+  if (fmt == LLMC_FMT_NVFP4 && !gs) return LLMC_EINVAL_ARG;
+  if (!p.a.symmetric && !zp_out) return LLMC_EINVAL_ARG;
+  if ((fmt == LLMC_FMT_NVFP4 || fmt == LLMC_FMT_MXFP4) && (cols & 1)) return LLMC_EINVAL_SHAPE;
+  return launch(p, (cudaStream_t)stream);
+}
+
+int llmc_pack_zero_point(const int8_t* zp, int64_t rows, int64_t groups, int bits, int32_t* out, void* stream) {
+  if (!zp || !out || (bits != 4 && bits != 8)) return LLMC_EINVAL_ARG;
+  int64_t n = ((rows + 32 / bits - 1) / (32 / bits)) * groups;
+  if (n == 0) return LLMC_OK;
+  k_pack_zp<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(zp, rows, groups, bits, out);
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,218 @@
+"""torch-facing wrappers of the observer / qparams / cast kernels.
+
+Each function validates devices, dtypes and shapes, allocates its outputs
+with torch (the C side never allocates caller-visible memory), and launches
+on the current CUDA stream without synchronising.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import check, lib, ptr, qargs_struct, require_cuda, stream_ptr
+
+
+def _strategy(args) -> str:
+    return getattr(args.strategy, "value", args.strategy)
+
+
+def _type(args) -> str:
+    return getattr(args.type, "value", args.type)
+
+
+def stats_shape(rows: int, cols: int, args) -> tuple[int, ...]:
+    """Shape of min/max/scale for a (rows, cols) weight (S/observers/helpers.py:63-102)."""
+    s = _strategy(args)
+    if s == "tensor":
+        return (1,)
+    if s == "channel":
+        return (rows, 1)
+    if s in ("group", "tensor_group"):
+        if cols % args.group_size:
+            raise ValueError(
+                f"group quantization strategy requires strict division of weight/activation "
+                f"size {cols} and group/block size {args.group_size}"
+            )
+        return (rows, cols // args.group_size)
+    if s == "block":
+        bh, bw = args.block_structure
+        return (-(-rows // bh), -(-cols // bw))
+    raise ValueError(f"Unknown strategy {s}")
+
+
+def _check_weight(w: torch.Tensor) -> torch.Tensor:
+    require_cuda(w)
+    if w.dtype != torch.bfloat16:
+        raise NotImplementedError(f"weights of dtype {w.dtype}: the kernels take bf16 weights")
+    if w.ndim != 2:
+        raise ValueError(f"expected 2D linear weight, but got shape {tuple(w.shape)}")
+    return w.contiguous()
+
+
+def observe_minmax(w: torch.Tensor, args) -> tuple[torch.Tensor, torch.Tensor]:
+    """Memoryless min-max statistics (S/observers/min_max.py:16-25,106-110)."""
+    w = _check_weight(w)
+    shape = stats_shape(w.shape[0], w.shape[1], args)
+    mn = torch.empty(shape, dtype=torch.bfloat16, device=w.device)
+    mx = torch.empty(shape, dtype=torch.bfloat16, device=w.device)
+    qa = qargs_struct(args)
+    check(lib().llmc_observe_minmax(ptr(w), w.shape[0], w.shape[1], ctypes.byref(qa), ptr(mn), ptr(mx),
+                                    stream_ptr(w.device)), "observe_minmax")
+    return mn, mx
+
+
+def absmax_(w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """Max-accumulate |w| into the float32 scalar ``out`` (initialise to 0)."""
+    require_cuda(w, out)
+    if w.dtype != torch.bfloat16:
+        raise NotImplementedError(f"dtype {w.dtype}")
+    w = w.contiguous()
+    check(lib().llmc_absmax_accumulate(ptr(w), w.numel(), ptr(out), stream_ptr(w.device)), "absmax")
+    return out
+
+
+def global_scale_from_absmax(absmax: torch.Tensor) -> torch.Tensor:
+    """generate_gparam (CT/quantization/utils/helpers.py:309-338): float32 (1,)."""
+    gs = torch.empty(1, dtype=torch.float32, device=absmax.device)
+    check(lib().llmc_global_scale(ptr(absmax), ptr(gs), stream_ptr(absmax.device)), "global_scale")
+    return gs
+
+
+def fused_global_scale(weights: list[torch.Tensor]) -> torch.Tensor:
+    """Shared TENSOR_GROUP global scale of a fused set (q/k/v, gate/up): one
+    absmax over all members, then generate_gparam (S/observers/base.py:78-96)."""
+    acc = torch.zeros(1, dtype=torch.float32, device=weights[0].device)
+    for w in weights:
+        absmax_(w, acc)
+    return global_scale_from_absmax(acc)
+
+
+def calculate_qparams(mn: torch.Tensor, mx: torch.Tensor, args, global_scale: torch.Tensor | None = None):
+    """calculate_qparams (CT/quantization/utils/helpers.py:50-137) on the GPU."""
+    require_cuda(mn, mx)
+    if mn.dtype != torch.bfloat16 or mx.dtype != torch.bfloat16:
+        raise NotImplementedError("statistics must be bf16 (the observed weight's dtype)")
+    mn, mx = mn.contiguous(), mx.contiguous()
+    qa = qargs_struct(args)
+    if global_scale is not None:
+        global_scale = global_scale.to(torch.float32).contiguous()
+    scale = torch.empty(mn.shape, dtype=torch.float32 if global_scale is not None else torch.bfloat16,
+                        device=mn.device)
+    zp_dtype = args.zp_dtype if getattr(args, "zp_dtype", None) is not None else torch.int8
+    if zp_dtype == torch.float8_e4m3fn:
+        zp = torch.zeros(mn.shape, dtype=zp_dtype, device=mn.device)
+        zp_out = None
+    else:
+        zp = torch.empty(mn.shape, dtype=zp_dtype, device=mn.device)
+        zp_out = zp
+    check(lib().llmc_calculate_qparams(ptr(mn), ptr(mx), mn.numel(), ctypes.byref(qa), ptr(global_scale),
+                                       ptr(scale), ptr(zp_out), stream_ptr(mn.device)), "calculate_qparams")
+    if scale.ndim == 0:
+        scale, zp = scale.reshape(1), zp.reshape(1)
+    return scale, zp
+
+
+def format_of(args) -> int:
+    """compressed-tensors format for weight-only args (CT/compressors/format.py:16-25)."""
+    if _type(args) == "float":
+        if args.num_bits == 4:
+            return _lib.FMT_MXFP4 if args.group_size == 32 else _lib.FMT_NVFP4
+        return _lib.FMT_FP8
+    return _lib.FMT_PACK_INT32
+
+
+def packed_shape(rows: int, cols: int, args, fmt: int) -> tuple[tuple[int, ...], torch.dtype]:
+    if fmt == _lib.FMT_PACK_INT32:
+        pf = 32 // args.num_bits
+        return (rows, -(-cols // pf)), torch.int32
+    if fmt in (_lib.FMT_NVFP4, _lib.FMT_MXFP4):
+        return (rows, cols // 2), torch.uint8
+    if fmt == _lib.FMT_FP8:
+        return (rows, cols), torch.float8_e4m3fn
+    return (rows, cols), torch.int8
+
+
+def quantize_pack(w: torch.Tensor, args, scale: torch.Tensor, zero_point: torch.Tensor | None = None,
+                  global_scale: torch.Tensor | None = None, fmt: int | None = None) -> torch.Tensor:
+    """``quantize`` + the compressor's packing with stored qparams
+    (CT/compressors/{pack_quantized,naive_quantized,nvfp4,mxfp4}/base.py)."""
+    w = _check_weight(w)
+    fmt = format_of(args) if fmt is None else fmt
+    rows, cols = w.shape
+    stats_shape(rows, cols, args)
+    require_cuda(scale)
+    if scale.dtype == torch.float8_e4m3fn:
+        scale = scale.to(torch.float32)
+    if scale.dtype not in (torch.bfloat16, torch.float32):
+        raise NotImplementedError(f"scale dtype {scale.dtype}")
+    scale = scale.contiguous()
+    zp = None
+    if zero_point is not None and not args.symmetric:
+        zp = zero_point.to(torch.int8).contiguous()
+    if global_scale is not None:
+        global_scale = global_scale.to(torch.float32).reshape(1).contiguous()
+    shape, dtype = packed_shape(rows, cols, args, fmt)
+    out = torch.empty(shape, dtype=dtype, device=w.device)
+    qa = qargs_struct(args)
+    check(lib().llmc_quantize_pack(ptr(w), rows, cols, ctypes.byref(qa), ptr(scale),
+                                   1 if scale.dtype == torch.float32 else 0, ptr(zp), ptr(global_scale), fmt,
+                                   ptr(out), stream_ptr(w.device)), "quantize_pack")
+    return out
+
+
+def pack_zero_point(zp: torch.Tensor, num_bits: int) -> torch.Tensor:
+    """pack_to_int32(zero_point, num_bits, packed_dim=0)."""
+    require_cuda(zp)
+    zp = zp.to(torch.int8).contiguous()
+    rows, groups = zp.shape
+    pf = 32 // num_bits
+    out = torch.empty((-(-rows // pf), groups), dtype=torch.int32, device=zp.device)
+    check(lib().llmc_pack_zero_point(ptr(zp), rows, groups, num_bits, ptr(out), stream_ptr(zp.device)),
+          "pack_zero_point")
+    return out
+
+
+def modelfree_quantize(w: torch.Tensor, args, global_scale: torch.Tensor | None = None) -> dict:
+    """One weight through observe -> qparams -> quantize -> pack in a single
+    pass; returns the compressed-tensors state dict entries for it.
+
+    Keys and dtypes follow the compressors: ``weight_packed`` (int32 or uint8)
+    or ``weight`` (fp8), ``weight_scale`` (bf16 / fp8 / uint8 E8M0),
+    ``weight_global_scale`` (NVFP4), ``weight_shape`` (pack_quantized),
+    ``weight_zero_point`` (asymmetric pack_quantized, packed along rows).
+    """
+    w = _check_weight(w)
+    rows, cols = w.shape
+    fmt = format_of(args)
+    sshape = stats_shape(rows, cols, args)
+    shape, dtype = packed_shape(rows, cols, args, fmt)
+    out = torch.empty(shape, dtype=dtype, device=w.device)
+    if fmt == _lib.FMT_NVFP4:
+        if global_scale is None:
+            global_scale = fused_global_scale([w])
+        global_scale = global_scale.to(torch.float32).reshape(1).contiguous()
+        scale = torch.empty(sshape, dtype=torch.float8_e4m3fn, device=w.device)
+    elif fmt == _lib.FMT_MXFP4:
+        scale = torch.empty(sshape, dtype=torch.uint8, device=w.device)
+    else:
+        scale = torch.empty(sshape, dtype=torch.bfloat16, device=w.device)
+    zp = None if args.symmetric else torch.empty(sshape, dtype=torch.int8, device=w.device)
+    qa = qargs_struct(args)
+    check(lib().llmc_modelfree_quantize(ptr(w), rows, cols, ctypes.byref(qa), ptr(global_scale), fmt, ptr(out),
+                                        ptr(scale), ptr(zp), stream_ptr(w.device)), "modelfree_quantize")
+    res: dict[str, torch.Tensor] = {}
+    if fmt == _lib.FMT_FP8:
+        res["weight"] = out
+        res["weight_scale"] = scale
+        return res
+    res["weight_packed"] = out
+    res["weight_scale"] = scale
+    if fmt == _lib.FMT_NVFP4:
+        res["weight_global_scale"] = global_scale
+    if fmt == _lib.FMT_PACK_INT32:
+        res["weight_shape"] = torch.tensor([rows, cols], dtype=torch.int64)
+        if zp is not None:
+            res["weight_zero_point"] = pack_zero_point(zp, args.num_bits)
+    return res

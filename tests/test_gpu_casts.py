@@ -1,0 +1,189 @@
+"""GPU parity of the observer / qparams / cast kernels (called through the C ABI).
+
+Bar: bit-exact against the golden fixtures produced by the reference itself
+and against the CPU oracle on larger seeded inputs."""
+import numpy as np
+import pytest
+import torch
+from compressed_tensors.quantization import QuantizationArgs
+from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
+
+from golden_io import bf16, load
+from gpu_util import bits, np_f32, rand_bf16, to_dev_bf16
+from llmcompressor_b200 import _lib, ops
+from oracle import casts as ocasts
+from oracle import numerics as onum
+from oracle import observers as oobs
+
+pytestmark = pytest.mark.gpu
+
+SCHEMES = ["W4A16", "W4A16_ASYM", "W8A16", "FP8_DYNAMIC", "FP8", "FP8_BLOCK", "MXFP4A16", "NVFP4A16"]
+
+
+def _weights_args(name):
+    return preset_name_to_scheme(name, ["Linear"]).weights
+
+
+def _cmp_state(out: dict, ref: dict, prefix: str, tag: str):
+    for k, v in out.items():
+        key = prefix + k
+        assert key in ref, f"{tag}: unexpected key {k}"
+        r = ref[key]
+        got = bits(v).reshape(r.shape)
+        np.testing.assert_array_equal(got, r, err_msg=f"{tag}:{k}")
+    produced = {prefix + k for k in out}
+    expected = {k for k in ref if k.startswith(prefix) and not k.endswith("input_scale")}
+    assert expected <= produced, f"{tag}: missing {expected - produced}"
+
+
+@pytest.mark.parametrize("scheme", SCHEMES)
+def test_modelfree_golden_bit_exact(scheme):
+    g = load(f"modelfree_{scheme}")
+    w = to_dev_bf16(g["weight"])
+    out = ops.modelfree_quantize(w, _weights_args(scheme))
+    torch.cuda.synchronize()
+    _cmp_state(out, {k: v for k, v in g.items() if k != "weight"}, "out_", scheme)
+
+
+def test_nvfp4_fused_qkv_golden_bit_exact():
+    g = load("modelfree_NVFP4A16_fused_qkv")
+    names = ("q_proj", "k_proj", "v_proj")
+    ws = [to_dev_bf16(g[f"{n}_weight"]) for n in names]
+    gs = ops.fused_global_scale(ws)
+    args = _weights_args("NVFP4A16")
+    for n, w in zip(names, ws):
+        out = ops.modelfree_quantize(w, args, global_scale=gs)
+        _cmp_state(out, g, f"{n}_out_", n)
+
+
+OBS = {
+    "int4_sym_group128": QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=128),
+    "int4_asym_group128": QuantizationArgs(num_bits=4, type="int", symmetric=False, strategy="group", group_size=128),
+    "int8_sym_channel": QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="channel"),
+    "int4_sym_tensor": QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="tensor"),
+    "fp8_block_128": QuantizationArgs(num_bits=8, type="float", symmetric=True, strategy="block", block_structure=[128, 128]),
+    "int8_asym_channel": QuantizationArgs(num_bits=8, type="int", symmetric=False, strategy="channel"),
+}
+
+
+@pytest.mark.parametrize("case", sorted(OBS))
+def test_observer_and_qparams_golden_bit_exact(case):
+    g = load(f"observer_{case}")
+    args = OBS[case]
+    w = to_dev_bf16(g["weight"])
+    mn, mx = ops.observe_minmax(w, args)
+    np.testing.assert_array_equal(bits(mn).reshape(g["min_vals"].shape), g["min_vals"])
+    np.testing.assert_array_equal(bits(mx).reshape(g["max_vals"].shape), g["max_vals"])
+    scale, zp = ops.calculate_qparams(mn, mx, args)
+    np.testing.assert_array_equal(bits(scale).reshape(g["scale"].shape), g["scale"])
+    np.testing.assert_array_equal(bits(zp).reshape(g["zero_point"].shape), g["zero_point"])
+
+
+LARGE = [
+    ("W4A16", 1024, 4096, "normal"),
+    ("W4A16_ASYM", 512, 2048, "normal"),
+    ("W8A16", 384, 3072, "normal"),
+    ("FP8_DYNAMIC", 256, 7168, "student_t"),
+    ("FP8_BLOCK", 576, 7168, "student_t"),  # 576 rows: padded last block row
+    ("FP8_BLOCK", 300, 1000, "student_t"),  # ragged in both dims, cols % 8 != 0
+    ("MXFP4A16", 1024, 2048, "student_t"),
+    ("NVFP4A16", 1024, 4096, "normal"),
+    ("FP8", 128, 4096, "normal"),
+]
+
+
+@pytest.mark.parametrize("scheme,rows,cols,kind", LARGE)
+def test_modelfree_vs_oracle_bit_exact(scheme, rows, cols, kind):
+    wt = rand_bf16(rows, cols, seed=rows * 7 + cols, kind=kind)
+    w = wt.cuda()
+    out = ops.modelfree_quantize(w, _weights_args(scheme))
+    ref = ocasts.modelfree_tensor(np_f32(wt), scheme)
+    for k, v in ref.items():
+        got = bits(out[k])
+        if v.dtype == np.float32 and k == "weight_scale":
+            v = onum.f32_to_bf16_bits(v)
+        np.testing.assert_array_equal(got.reshape(v.shape), v, err_msg=f"{scheme}:{k}")
+
+
+@pytest.mark.parametrize("scheme", ["W4A16", "W8A16", "FP8_DYNAMIC", "FP8_BLOCK", "MXFP4A16", "NVFP4A16", "W4A16_ASYM"])
+def test_quantize_pack_given_qparams_matches_fused(scheme):
+    """The compressor path (observer -> qparams -> quantize_pack) equals the fused pass."""
+    args = _weights_args(scheme)
+    w = rand_bf16(256, 1024, seed=5).cuda()
+    fused = ops.modelfree_quantize(w, args)
+    mn, mx = ops.observe_minmax(w, args)
+    gs = ops.fused_global_scale([w]) if scheme == "NVFP4A16" else None
+    scale, zp = ops.calculate_qparams(mn, mx, args, global_scale=gs)
+    packed = ops.quantize_pack(w, args, scale, zp, global_scale=gs)
+    key = "weight" if scheme.startswith("FP8") else "weight_packed"
+    np.testing.assert_array_equal(bits(packed), bits(fused[key]))
+
+
+def test_fp8_cast_every_bf16_value_matches_torch():
+    """All finite bf16 values through the FP8 cast with scale 1 vs torch's own cast."""
+    u = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    x = bf16(u)
+    x = np.where(np.isfinite(x), x, 0).astype(np.float32)
+    wt = torch.from_numpy(x).to(torch.bfloat16).reshape(256, 256)
+    args = QuantizationArgs(num_bits=8, type="float", symmetric=True, strategy="tensor")
+    out = ops.quantize_pack(wt.cuda(), args, torch.ones(1, dtype=torch.bfloat16, device="cuda"))
+    ref = torch.clamp(wt.float(), -448, 448).to(torch.float8_e4m3fn)
+    np.testing.assert_array_equal(bits(out), bits(ref))
+
+
+def test_int8_quotient_rounding_random_scales():
+    """bf16 quotient + round at 8-bit resolution with random per-group scales vs the oracle:
+    exercises the reciprocal fast path and its exact fallback."""
+    rows, cols, gsz = 512, 4096, 64
+    g = torch.Generator().manual_seed(3)
+    wt = (torch.randn(rows, cols, generator=g) * 3).to(torch.bfloat16)
+    st = (torch.rand(rows, cols // gsz, generator=g) * 0.05 + 1e-3).to(torch.bfloat16)
+    args = QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="group", group_size=gsz)
+    out = ops.quantize_pack(wt.cuda(), args, st.cuda(), fmt=_lib.FMT_INT8)
+    qa = oobs.QArgs(8, "int", True, "group", gsz)
+    ref = ocasts.quantize_int(np_f32(wt), np_f32(st), None, qa)
+    np.testing.assert_array_equal(bits(out), ref)
+
+
+def test_known_answer_lifecycle_stats_on_gpu():
+    """T/llmcompressor/modifiers/calibration/test_lifecycle.py:16-121 statistics
+    (arange(24) as 4x6 bf16) through the kernels, for every strategy there."""
+    w = torch.arange(24, dtype=torch.bfloat16).reshape(4, 6).cuda()
+    cases = [
+        (QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="tensor"), [0.0], [23.0]),
+        (QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="channel"), [0, 6, 12, 18], [5, 11, 17, 23]),
+        (QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=3),
+         [0, 3, 6, 9, 12, 15, 18, 21], [2, 5, 8, 11, 14, 17, 20, 23]),
+        (QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="block", block_structure=[2, 3]),
+         [0, 3, 12, 15], [8, 11, 20, 23]),
+    ]
+    for args, emn, emx in cases:
+        mn, mx = ops.observe_minmax(w, args)
+        assert mn.float().cpu().reshape(-1).tolist() == [float(v) for v in emn]
+        assert mx.float().cpu().reshape(-1).tolist() == [float(v) for v in emx]
+        scale, _ = ops.calculate_qparams(mn, mx, args)
+        qa = oobs.QArgs(4, "int", True, getattr(args.strategy, "value", args.strategy), args.group_size,
+                        tuple(args.block_structure) if args.block_structure else None)
+        omn, omx = oobs.minmax(np.arange(24, dtype=np.float32).reshape(4, 6), qa)
+        osc, _ = oobs.calculate_qparams(omn, omx, qa)
+        np.testing.assert_array_equal(bits(scale).reshape(-1), onum.f32_to_bf16_bits(osc).reshape(-1))
+
+
+def test_edge_cases_and_errors():
+    args = QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=128)
+    empty = torch.empty(0, 256, dtype=torch.bfloat16, device="cuda")
+    out = ops.modelfree_quantize(empty, args)
+    assert out["weight_packed"].shape == (0, 32)
+    with pytest.raises(ValueError):
+        ops.modelfree_quantize(torch.zeros(4, 100, dtype=torch.bfloat16, device="cuda"), args)
+    g3 = QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=3)
+    with pytest.raises(NotImplementedError):
+        ops.modelfree_quantize(torch.zeros(4, 6, dtype=torch.bfloat16, device="cuda"), g3)
+    with pytest.raises(NotImplementedError):
+        ops.modelfree_quantize(torch.zeros(4, 256, dtype=torch.float16, device="cuda"), args)
+    with pytest.raises(ValueError):
+        ops.modelfree_quantize(torch.zeros(4, 4, 256, dtype=torch.bfloat16, device="cuda"), args)
+    # all-zero weight: eps scales, zero codes
+    z = ops.modelfree_quantize(torch.zeros(8, 256, dtype=torch.bfloat16, device="cuda"), args)
+    assert torch.all(z["weight_scale"].float() == 2.0**-7)
+    assert torch.all(z["weight_packed"] == 0x88888888 - 2**32)
