@@ -128,6 +128,23 @@ int llmc_modelfree_quantize(const void* w_bf16, int64_t rows, int64_t cols, cons
  * int32 (ceil(rows*bits/32), groups). */
 int llmc_pack_zero_point(const int8_t* zp, int64_t rows, int64_t groups, int num_bits, int32_t* out, void* stream);
 
+/* ---------------------------------------------------------------- GPTQ Hessian
+ * H += alpha * X^T X over X (n_tokens, d) bf16 with row stride ld; H is a
+ * float32 (d, d) row-major matrix kept fully symmetric.  Replaces
+ * `accumulate_hessian` / `_hessian_update` (S/modifiers/gptq/gptq_quantize.py:22-32,
+ * 63-97; alpha = 2 reproduces the sqrt(2) input scaling).  Tensor cores
+ * (tcgen05, TMEM accumulators, TMA) when d and ld are multiples of 8; a
+ * CUDA-core kernel otherwise.  If num_samples is non-NULL, *num_samples +=
+ * num_add on the device in the same stream (the reference's batch count,
+ * `:70-73,91`).  status (optional device int) receives LLMC_ETIMEOUT if a
+ * bounded wait in the kernel ran out. */
+int llmc_hessian_accumulate(const void* x_bf16, int64_t n_tokens, int64_t d, int64_t ld, float* H, float alpha,
+                            float* num_samples, float num_add, int* status, void* stream);
+
+/* Number of 128x256 output tiles the tensor-core Hessian computes for size d
+ * (tiles touching the lower triangle). */
+int llmc_hessian_tiles(int64_t d);
+
 #ifdef __cplusplus
 }
 #endif

@@ -439,7 +439,7 @@ static int n_groups(const CastParams& p) {
 
 static int validate(const CastParams& p) {
   const QArgs& a = p.a;
-  if (!p.w || p.rows < 0 || p.cols < 0) return LLMC_EINVAL_ARG;
+  if ((!p.w && p.rows * p.cols > 0) || p.rows < 0 || p.cols < 0) return LLMC_EINVAL_ARG;
   if (a.bits != 4 && a.bits != 8) return LLMC_ENOSUPPORT;
   if (a.strategy < 0 || a.strategy > LLMC_STRAT_BLOCK) return LLMC_EINVAL_ARG;
   if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
@@ -567,7 +567,7 @@ int llmc_calculate_qparams(const void* mn, const void* mx, int64_t n, const Llmc
 
 int llmc_quantize_pack(const void* w, int64_t rows, int64_t cols, const LlmcQuantArgs* args, const void* scale,
                        int scale_is_f32, const void* zp, const float* gs, int fmt, void* out, void* stream) {
-  if (!args || !scale || !out) return LLMC_EINVAL_ARG;
+  if (!args || ((!scale || !out) && rows * cols > 0)) return LLMC_EINVAL_ARG;
   CastParams p = {};
   p.w = (const uint16_t*)w; p.rows = rows; p.cols = cols; p.a = to_qargs(*args);
   p.mode = MODE_GIVEN; p.fmt = fmt; p.scale_in = scale; p.scale_in_f32 = scale_is_f32;
@@ -582,7 +582,7 @@ int llmc_quantize_pack(const void* w, int64_t rows, int64_t cols, const LlmcQuan
 
 int llmc_modelfree_quantize(const void* w, int64_t rows, int64_t cols, const LlmcQuantArgs* args, const float* gs,
                             int fmt, void* out, void* scale_out, void* zp_out, void* stream) {
-  if (!args || !out || !scale_out) return LLMC_EINVAL_ARG;
+  if (!args || ((!out || !scale_out) && rows * cols > 0)) return LLMC_EINVAL_ARG;
   CastParams p = {};
   p.w = (const uint16_t*)w; p.rows = rows; p.cols = cols; p.a = to_qargs(*args);
   p.mode = MODE_FUSED; p.fmt = fmt; p.gs = gs; p.out = out; p.scale_out = scale_out;
@@ -591,7 +591,7 @@ int llmc_modelfree_quantize(const void* w, int64_t rows, int64_t cols, const Llm
   if (v) return v;
   if ((v = check_fmt(p.a, fmt))) return v;
   if (fmt == LLMC_FMT_NVFP4 && !gs) return LLMC_EINVAL_ARG;
-  if (!p.a.symmetric && !zp_out) return LLMC_EINVAL_ARG;
+  if (!p.a.symmetric && !zp_out && rows * cols > 0) return LLMC_EINVAL_ARG;
   if ((fmt == LLMC_FMT_NVFP4 || fmt == LLMC_FMT_MXFP4) && (cols & 1)) return LLMC_EINVAL_SHAPE;
   return launch(p, (cudaStream_t)stream);
 }
