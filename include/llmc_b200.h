@@ -145,6 +145,32 @@ int llmc_hessian_accumulate(const void* x_bf16, int64_t n_tokens, int64_t d, int
  * (tiles touching the lower triangle). */
 int llmc_hessian_tiles(int64_t d);
 
+/* ---------------------------------------------------------------- GPTQ solve
+ * Replaces `quantize_weight` (S/modifiers/gptq/gptq_quantize.py:100-296) in
+ * three steps so that modules sharing one Hessian (q/k/v, gate/up) factor it
+ * once:
+ *   1. llmc_gptq_prepare_hessian: `_mask_dead_hessian` (:35-38) -- diag == 0 ->
+ *      1, dead[i] = 1 -- then damp = percdamp * mean(diag), diag += damp
+ *      (:181-185).  H (d x d float32) is modified in place.
+ *   2. llmc_gptq_hinv: Hinv = upper Cholesky factor of H^-1 (:185-188), in
+ *      float32; a non-positive pivot sets *status = LLMC_ENOT_PD (the
+ *      reference's LinAlgError) and later steps then use the identity
+ *      (:189-196, round-to-nearest fallback).  workspace: see
+ *      llmc_gptq_hinv_workspace_size.
+ *   3. llmc_gptq_quantize: the blockwise column loop (:199-277) for one weight
+ *      (rows x cols bf16) with stored bf16 scales / int8 zero points (TENSOR,
+ *      CHANNEL or GROUP; blocksize 128), writing the fake-quantized bf16
+ *      weight and the summed loss (float32 scalar).  Dead columns are zeroed
+ *      first (:38).  workspace: see llmc_gptq_quantize_workspace_size.
+ * Nothing synchronises; *status is read by the caller when it needs it. */
+int llmc_gptq_prepare_hessian(float* H, int64_t d, float percdamp, uint8_t* dead, void* stream);
+int llmc_gptq_hinv_workspace_size(int64_t d, int64_t* bytes);
+int llmc_gptq_hinv(const float* H, int64_t d, float* Hinv, void* workspace, int* status, void* stream);
+int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes);
+int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const uint8_t* dead,
+                       const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp, int64_t blocksize,
+                       void* wq_bf16, float* loss, void* workspace, const int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -6,6 +6,6 @@ The host side mirrors the reference's Python interfaces (``accumulate_hessian``,
 ``include/llmc_b200.h``).  There is no CPU fallback: without the library or a
 CUDA device the entry points raise.
 """
-from . import _lib, ops  # noqa: F401
+from . import _lib, ops, gptq  # noqa: F401
 
 __version__ = "0.1.0"

@@ -1,0 +1,585 @@
+// GPTQ solve on sm_100a: damping + dead-column mask, the upper Cholesky
+// factor of the inverse Hessian, and the blockwise quantize / error-propagate
+// loop.  Reference: quantize_weight, S/modifiers/gptq/gptq_quantize.py:100-296.
+//
+// Inverse factor.  The reference computes U = chol(chol_inverse(chol(A)), upper)
+// with A = H + damp*I.  Here A is factored from the bottom-right corner
+// instead: with J the reversal permutation, JAJ = L L^T (lower Cholesky), so
+// A = R R^T with R = J L J upper, and A^-1 = (R^-1)^T R^-1.  R^-1 is upper
+// with a positive diagonal, hence it *is* U.  So U = J L^-1 J: one Cholesky
+// (d^3/3) plus one triangular inverse (d^3/3) instead of the reference's
+// Cholesky + cholesky_inverse + Cholesky.  Same matrix, float32 throughout.
+//
+// Both factorisations are blocked (128): a one-CTA kernel factors and inverts
+// each diagonal block in shared memory; panels and trailing updates are
+// float32 GEMMs (k_sgemm).  A non-positive pivot sets LLMC_ENOT_PD in the
+// caller's status word; the quantize kernels then use the identity (the
+// reference's round-to-nearest fallback) without a host round trip.
+//
+// Block loop.  Rows of W are independent, so one thread owns one row; a CTA
+// stages its rows' 128-column block and the 128x128 block of U in shared
+// memory.  Within a 32-column sub-block the per-column update follows the
+// reference exactly (float32 product, then subtraction, column by column);
+// across sub-blocks and across 128-column blocks the update is the lazy
+// batched form W -= Err * U (the reference's `Err1.matmul(Hinv[i1:i2, i2:])`).
+#include "llmc_common.cuh"
+
+#include <algorithm>
+
+namespace llmc {
+namespace gq {
+
+// ---------------------------------------------------------------------------
+// float32 GEMM: C (m x n, ldc) {=, -=, = -} A * op(B)
+//   A: !TA row-major (m x k, lda);  TA: stored k-major (k x m, lda)
+//   B: !TB row-major (k x n, ldb);  TB: stored n-major (n x k, ldb)
+//   tri:     only output tiles that touch the lower triangle (row >= col)
+//   b_lower: B is lower triangular -> for an output column tile starting at
+//            n0 only k >= n0 contributes
+//   skip:    optional device flag; the kernel does nothing when it is set
+// ---------------------------------------------------------------------------
+struct GemmArgs {
+  int m, n, k;
+  const float* A;
+  int64_t lda;
+  const float* B;
+  int64_t ldb;
+  float* C;
+  int64_t ldc;
+  int mode;  // 0: C = AB, 1: C = C - AB, 2: C = -AB
+  int tri, b_lower;
+  const int* skip;
+};
+
+constexpr int GBM = 128, GBN = 128, GBK = 8;
+
+template <bool TA, bool TB>
+__global__ void __launch_bounds__(256) k_sgemm(GemmArgs g) {
+  if (g.skip && *g.skip) return;
+  const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
+  if (g.tri && n0 > m0 + GBM - 1) return;
+  __shared__ __align__(16) float As[2][GBK][GBM + 4];
+  __shared__ __align__(16) float Bs[2][GBK][GBN + 4];
+  const int t = threadIdx.x;
+  const int tx = t & 15, ty = t >> 4;
+  int kbeg = 0;
+  if (g.b_lower) kbeg = (n0 / GBK) * GBK;
+  const int kend = g.k;
+
+  float a_ld[4], b_ld[4];
+  auto load_tiles = [&](int k0) {
+    // A
+    if (!TA) {
+      const int mm = t >> 1, kq = (t & 1) * 4;
+      const int gm = m0 + mm;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int gk = k0 + kq + i;
+        a_ld[i] = (gm < g.m && gk < kend) ? g.A[(int64_t)gm * g.lda + gk] : 0.f;
+      }
+    } else {
+      const int kk = t >> 5, mq = (t & 31) * 4;
+      const int gk = k0 + kk;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int gm = m0 + mq + i;
+        a_ld[i] = (gm < g.m && gk < kend) ? g.A[(int64_t)gk * g.lda + gm] : 0.f;
+      }
+    }
+    // B
+    if (TB) {
+      const int nn = t >> 1, kq = (t & 1) * 4;
+      const int gn = n0 + nn;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int gk = k0 + kq + i;
+        b_ld[i] = (gn < g.n && gk < kend) ? g.B[(int64_t)gn * g.ldb + gk] : 0.f;
+      }
+    } else {
+      const int kk = t >> 5, nq = (t & 31) * 4;
+      const int gk = k0 + kk;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int gn = n0 + nq + i;
+        b_ld[i] = (gn < g.n && gk < kend) ? g.B[(int64_t)gk * g.ldb + gn] : 0.f;
+      }
+    }
+  };
+  auto store_tiles = [&](int buf) {
+    if (!TA) {
+      const int mm = t >> 1, kq = (t & 1) * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) As[buf][kq + i][mm] = a_ld[i];
+    } else {
+      const int kk = t >> 5, mq = (t & 31) * 4;
+      *(float4*)&As[buf][kk][mq] = make_float4(a_ld[0], a_ld[1], a_ld[2], a_ld[3]);
+    }
+    if (TB) {
+      const int nn = t >> 1, kq = (t & 1) * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) Bs[buf][kq + i][nn] = b_ld[i];
+    } else {
+      const int kk = t >> 5, nq = (t & 31) * 4;
+      *(float4*)&Bs[buf][kk][nq] = make_float4(b_ld[0], b_ld[1], b_ld[2], b_ld[3]);
+    }
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  int buf = 0;
+  if (kbeg < kend) {
+    load_tiles(kbeg);
+    store_tiles(0);
+    __syncthreads();
+    for (int k0 = kbeg; k0 < kend; k0 += GBK) {
+      const bool more = k0 + GBK < kend;
+      if (more) load_tiles(k0 + GBK);
+#pragma unroll
+      for (int kk = 0; kk < GBK; ++kk) {
+        float4 a0 = *(const float4*)&As[buf][kk][ty * 4];
+        float4 a1 = *(const float4*)&As[buf][kk][64 + ty * 4];
+        float4 b0 = *(const float4*)&Bs[buf][kk][tx * 4];
+        float4 b1 = *(const float4*)&Bs[buf][kk][64 + tx * 4];
+        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      }
+      if (more) {
+        store_tiles(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (gm >= g.m) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+      if (gn >= g.n) continue;
+      float* c = g.C + (int64_t)gm * g.ldc + gn;
+      if (g.mode == 0) *c = acc[i][j];
+      else if (g.mode == 1) *c = *c - acc[i][j];
+      else *c = -acc[i][j];
+    }
+  }
+}
+
+static int launch_gemm(bool ta, bool tb, const GemmArgs& g, cudaStream_t st) {
+  if (g.m <= 0 || g.n <= 0) return LLMC_OK;
+  dim3 grid((g.n + GBN - 1) / GBN, (g.m + GBM - 1) / GBM);
+  if (!ta && !tb) k_sgemm<false, false><<<grid, 256, 0, st>>>(g);
+  else if (!ta && tb) k_sgemm<false, true><<<grid, 256, 0, st>>>(g);
+  else if (ta && !tb) k_sgemm<true, false><<<grid, 256, 0, st>>>(g);
+  else k_sgemm<true, true><<<grid, 256, 0, st>>>(g);
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Hessian preparation: dead columns (diag == 0 -> 1, flagged), then
+// damp = percdamp * mean(diag), diag += damp  (gptq_quantize.py:35-38,178-185)
+// ---------------------------------------------------------------------------
+__global__ void k_prep_hessian(float* H, int64_t d, float percdamp, uint8_t* dead) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < d; i += blockDim.x) {
+    float v = H[i * d + i];
+    const bool dd = (v == 0.0f);
+    if (dd) { v = 1.0f; H[i * d + i] = 1.0f; }
+    dead[i] = dd ? 1 : 0;
+    s += v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float mean = __fdiv_rn(red[0], (float)d);
+  const float damp = percdamp * mean;
+  for (int64_t i = threadIdx.x; i < d; i += blockDim.x) H[i * d + i] += damp;
+}
+
+// reversed copy: B[i][j] = A[d-1-i][d-1-j]  (only the lower triangle of B is used)
+__global__ void k_reverse(const float* __restrict__ A, float* __restrict__ B, int64_t d) {
+  const int64_t i = blockIdx.y, j0 = (int64_t)blockIdx.x * blockDim.x;
+  const int64_t j = j0 + threadIdx.x;
+  if (i < d && j < d && j <= i) B[i * d + j] = A[(d - 1 - i) * d + (d - 1 - j)];
+}
+
+// U[i][j] = X[d-1-i][d-1-j] for j >= i, 0 below the diagonal
+__global__ void k_reverse_to_upper(const float* __restrict__ X, float* __restrict__ U, int64_t d) {
+  const int64_t i = blockIdx.y;
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < d && j < d) U[i * d + j] = (j >= i) ? X[(d - 1 - i) * d + (d - 1 - j)] : 0.0f;
+}
+
+// Factor one diagonal block (kb <= 128) of B in place (lower Cholesky) and
+// write its lower-triangular inverse to Linv (row stride 128).
+constexpr int PB = 128;
+__global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_t k0, int kb, float* Linv,
+                                                    int* status) {
+  extern __shared__ float sm[];
+  float* S = sm;                 // [PB][PB+1]
+  float* X = sm + PB * (PB + 1);  // [PB][PB+1]
+  __shared__ int bad;
+  const int t = threadIdx.x, nt = blockDim.x;
+  if (t == 0) bad = 0;
+  for (int e = t; e < kb * kb; e += nt) {
+    const int i = e / kb, j = e % kb;
+    S[i * (PB + 1) + j] = (j <= i) ? B[(k0 + i) * ld + k0 + j] : 0.f;
+  }
+  __syncthreads();
+  for (int j = 0; j < kb; ++j) {
+    if (t == 0) {
+      float p = S[j * (PB + 1) + j];
+      if (!(p > 0.0f)) { bad = 1; p = 1.0f; }
+      S[j * (PB + 1) + j] = sqrtf(p);
+    }
+    __syncthreads();
+    const float piv = S[j * (PB + 1) + j];
+    for (int i = j + 1 + t; i < kb; i += nt) S[i * (PB + 1) + j] = __fdiv_rn(S[i * (PB + 1) + j], piv);
+    __syncthreads();
+    // trailing rank-1 update of the lower triangle
+    const int rem = kb - j - 1;
+    for (int e = t; e < rem * rem; e += nt) {
+      const int i = j + 1 + e / rem, l = j + 1 + e % rem;
+      if (l <= i) S[i * (PB + 1) + l] -= S[i * (PB + 1) + j] * S[l * (PB + 1) + j];
+    }
+    __syncthreads();
+  }
+  if (t == 0 && bad && status) atomicExch(status, LLMC_ENOT_PD);
+  for (int e = t; e < kb * kb; e += nt) {
+    const int i = e / kb, j = e % kb;
+    if (j <= i) B[(k0 + i) * ld + k0 + j] = S[i * (PB + 1) + j];
+  }
+  // inverse by forward substitution, one column per thread
+  for (int c = t; c < kb; c += nt) {
+    for (int i = 0; i < kb; ++i) X[i * (PB + 1) + c] = 0.f;
+    for (int i = c; i < kb; ++i) {
+      float s = (i == c) ? 1.0f : 0.0f;
+      for (int l = c; l < i; ++l) s -= S[i * (PB + 1) + l] * X[l * (PB + 1) + c];
+      X[i * (PB + 1) + c] = __fdiv_rn(s, S[i * (PB + 1) + i]);
+    }
+  }
+  __syncthreads();
+  for (int e = t; e < PB * PB; e += nt) {
+    const int i = e / PB, j = e % PB;
+    Linv[i * PB + j] = (i < kb && j < kb && j <= i) ? X[i * (PB + 1) + j] : 0.f;
+  }
+}
+
+__global__ void k_copy2d(const float* __restrict__ src, int64_t lds, float* __restrict__ dst, int64_t ldd, int rows,
+                         int cols) {
+  const int r = blockIdx.y;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x)
+    if (r < rows) dst[(int64_t)r * ldd + c] = src[(int64_t)r * lds + c];
+}
+
+__global__ void k_copy_diag_inv(const float* __restrict__ Linv, float* __restrict__ X, int64_t d, int64_t k0, int kb) {
+  const int i = blockIdx.x, j = threadIdx.x;
+  if (i < kb && j < kb) X[(k0 + i) * d + k0 + j] = Linv[i * PB + j];
+}
+
+// ---------------------------------------------------------------------------
+// GPTQ column loop over one 128-column block
+// ---------------------------------------------------------------------------
+constexpr int QB = 128;     // GPTQ block size handled by the kernel
+constexpr int SUB = 32;     // sub-block held in registers
+constexpr int ROWS = 64;    // rows (threads) per CTA
+constexpr int QS_LD = QB + 1;
+
+struct BlockArgs {
+  float* W;            // r x c float32 working weight
+  int64_t r, c;
+  int i1, count;
+  const float* U;      // c x c upper factor
+  const uint16_t* scale;  // bf16 scales: tensor (1), channel (r,1), group (r, c/gs)
+  const int8_t* zp;       // optional
+  int strategy;
+  int64_t gs;
+  float qmin, qmax;
+  float* err;          // QB x r (column-major errors of this block)
+  float* loss;         // r per-row losses
+  const int* status;   // ENOT_PD -> identity
+};
+
+__device__ __forceinline__ void scale_of(const BlockArgs& a, int64_t row, int col, float& s, float& z) {
+  int64_t idx;
+  if (a.strategy == LLMC_STRAT_TENSOR) idx = 0;
+  else if (a.strategy == LLMC_STRAT_CHANNEL) idx = row;
+  else idx = row * (a.c / a.gs) + col / a.gs;
+  s = bf16_to_f(a.scale[idx]);
+  z = a.zp ? (float)a.zp[idx] : 0.0f;
+}
+
+// fake_quantize of one float32 value with a bf16 scale (CT forward_helpers.py:175-210):
+// float32 quotient, + zp, clamp, round half-even, -> bf16, - zp, * scale rounded to bf16.
+__device__ __forceinline__ float fake_quant(float w, float s, float z, float qmin, float qmax) {
+  float q = __fdiv_rn(w, s) + z;
+  q = rintf(fminf(fmaxf(q, qmin), qmax));
+  float deq = rbf(q - z);
+  return rbf(deq * s);
+}
+
+__global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
+  extern __shared__ float sm[];
+  float* U1 = sm;                // [QB][QB]
+  float* QS = sm + QB * QB;      // [ROWS][QS_LD]
+  const int t = threadIdx.x;
+  const int64_t row0 = (int64_t)blockIdx.x * ROWS;
+  const int64_t row = row0 + t;
+  const bool identity = a.status && *a.status == LLMC_ENOT_PD;
+  const int cnt = a.count;
+
+  for (int e = t; e < QB * QB; e += ROWS) {
+    const int i = e / QB, j = e % QB;
+    float v = 0.f;
+    if (i < cnt && j < cnt) v = identity ? (i == j ? 1.f : 0.f) : a.U[(int64_t)(a.i1 + i) * a.c + a.i1 + j];
+    U1[e] = v;
+  }
+  // stage this CTA's rows of the block (coalesced along columns)
+  for (int e = t; e < ROWS * QB; e += ROWS) {
+    const int rr = e / QB, j = e % QB;
+    const int64_t gr = row0 + rr;
+    QS[rr * QS_LD + j] = (gr < a.r && j < cnt) ? a.W[gr * a.c + a.i1 + j] : 0.f;
+  }
+  __syncthreads();
+
+  float loss = 0.f;
+  if (row < a.r) {
+    for (int s0 = 0; s0 < cnt; s0 += SUB) {
+      float w[SUB], e[SUB];
+#pragma unroll
+      for (int j = 0; j < SUB; ++j) { w[j] = QS[t * QS_LD + s0 + j]; e[j] = 0.f; }
+      const int n = min(SUB, cnt - s0);
+      float s = 0.f, z = 0.f;
+      int cur_g = -1;
+      for (int ii = 0; ii < n; ++ii) {
+        const int i = s0 + ii;
+        const int col = a.i1 + i;
+        const int g = (a.strategy == LLMC_STRAT_GROUP) ? (int)(col / a.gs) : 0;
+        if (g != cur_g) { scale_of(a, row, col, s, z); cur_g = g; }
+        const float wi = w[0];
+        const float d = U1[i * QB + i];
+        const float q = fake_quant(wi, s, z, a.qmin, a.qmax);
+        QS[t * QS_LD + i] = q;
+        const float diff = wi - q;
+        loss += __fdiv_rn(diff * diff, d * d);
+        const float err = __fdiv_rn(diff, d);
+        a.err[(int64_t)i * a.r + row] = err;
+        // shift the sub-block left by one column while applying this column's update
+#pragma unroll
+        for (int j = 0; j < SUB - 1; ++j) {
+          const int cj = min(i + 1 + j, QB - 1);
+          w[j] = w[j + 1] - err * U1[i * QB + cj];
+        }
+        w[SUB - 1] = 0.f;
+#pragma unroll
+        for (int j = 0; j < SUB - 1; ++j) e[j] = e[j + 1];
+        e[SUB - 1] = err;
+      }
+      // align errors when the sub-block was partial
+      for (int k = n; k < SUB; ++k) {
+#pragma unroll
+        for (int j = 0; j < SUB - 1; ++j) e[j] = e[j + 1];
+        e[SUB - 1] = 0.f;
+      }
+      // lazy update of the later columns of this block
+      for (int j = s0 + SUB; j < cnt; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int ii = 0; ii < SUB; ++ii) acc = fmaf(e[ii], U1[(s0 + ii) * QB + j], acc);
+        QS[t * QS_LD + j] -= acc;
+      }
+    }
+    a.loss[row] += loss / 2.0f;
+  }
+  __syncthreads();
+  // write the quantized block back (coalesced)
+  for (int e = t; e < ROWS * QB; e += ROWS) {
+    const int rr = e / QB, j = e % QB;
+    const int64_t gr = row0 + rr;
+    if (gr < a.r && j < cnt) a.W[gr * a.c + a.i1 + j] = QS[rr * QS_LD + j];
+  }
+}
+
+__global__ void k_init_w(const uint16_t* __restrict__ w, float* __restrict__ W, int64_t r, int64_t c,
+                         const uint8_t* dead) {
+  const int64_t n = r * c;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t col = i % c;
+    W[i] = (dead && dead[col]) ? 0.0f : bf16_to_f(w[i]);
+  }
+}
+
+__global__ void k_finish(const float* __restrict__ W, uint16_t* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = f_to_bf16(W[i]);
+}
+
+__global__ void k_sum(const float* __restrict__ x, int64_t n, float* out) {
+  __shared__ float red[32];
+  float s = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) v += red[i];
+    *out = v;
+  }
+}
+
+// cudaFuncSetAttribute is per device: remember which devices have it.
+template <typename F>
+static bool set_smem_attr(F* fn, int bytes, uint64_t* done_mask) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && (*done_mask >> dev) & 1ull) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+  if (dev < 64) *done_mask |= (1ull << dev);
+  return true;
+}
+
+static unsigned grid_for(int64_t n) { return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16)); }
+
+}  // namespace gq
+}  // namespace llmc
+
+using namespace llmc;
+using namespace llmc::gq;
+
+extern "C" {
+
+// workspace: Cholesky working copy B (d*d) + inverse X (d*d) + diag inverses (d*128) + panel (d*128)
+int llmc_gptq_hinv_workspace_size(int64_t d, int64_t* bytes) {
+  if (!bytes || d <= 0) return LLMC_EINVAL_ARG;
+  const int64_t nbp = ((d + PB - 1) / PB) * PB;
+  *bytes = (int64_t)sizeof(float) * (2 * d * d + 2 * nbp * PB) + 256;
+  return LLMC_OK;
+}
+
+int llmc_gptq_prepare_hessian(float* H, int64_t d, float percdamp, uint8_t* dead, void* stream) {
+  if (!H || !dead || d <= 0) return LLMC_EINVAL_ARG;
+  k_prep_hessian<<<1, 1024, 0, (cudaStream_t)stream>>>(H, d, percdamp, dead);
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, void* workspace, int* status, void* stream) {
+  if (!A || !Hinv || !workspace || !status || d <= 0) return LLMC_EINVAL_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t nb = (d + PB - 1) / PB;
+  float* B = (float*)workspace;
+  float* X = B + d * d;
+  float* LinvD = X + d * d;             // nb blocks of PB x PB
+  float* T = LinvD + nb * PB * PB;      // panel scratch, up to d x PB
+  static uint64_t attr_mask = 0;
+  if (!set_smem_attr(k_potrf_diag, 2 * PB * (PB + 1) * (int)sizeof(float), &attr_mask)) return LLMC_ECUDA;
+  dim3 rg((unsigned)((d + 255) / 256), (unsigned)d);
+  k_reverse<<<rg, 256, 0, st>>>(A, B, d);
+  // blocked lower Cholesky of B = J A J
+  for (int64_t kb0 = 0; kb0 < d; kb0 += PB) {
+    const int kb = (int)std::min<int64_t>(PB, d - kb0);
+    float* Ld = LinvD + (kb0 / PB) * PB * PB;
+    k_potrf_diag<<<1, 512, 2 * PB * (PB + 1) * sizeof(float), st>>>(B, d, kb0, kb, Ld, status);
+    const int rem = (int)(d - kb0 - kb);
+    if (rem > 0) {
+      // T = B[kb0+kb:, kb0:kb0+kb] * Linv_kk^T
+      GemmArgs g1 = {rem, kb, kb, B + (kb0 + kb) * d + kb0, d, Ld, PB, T, PB, 0, 0, 0, nullptr};
+      if (launch_gemm(false, true, g1, st)) return LLMC_ECUDA;
+      // B22 -= T T^T (lower tiles)
+      GemmArgs g2 = {rem, rem, kb, T, PB, T, PB, B + (kb0 + kb) * d + kb0 + kb, d, 1, 1, 0, nullptr};
+      if (launch_gemm(false, true, g2, st)) return LLMC_ECUDA;
+      // panel back into B
+      k_copy2d<<<dim3(1, rem), 128, 0, st>>>(T, PB, B + (kb0 + kb) * d + kb0, d, rem, kb);
+    }
+  }
+  // blocked inverse X = L^-1 (lower); the strictly upper part of X must be zero
+  if (cudaMemsetAsync(X, 0, sizeof(float) * d * d, st) != cudaSuccess) return LLMC_ECUDA;
+  for (int64_t i0 = 0; i0 < d; i0 += PB) {
+    const int ib = (int)std::min<int64_t>(PB, d - i0);
+    const float* Ld = LinvD + (i0 / PB) * PB * PB;
+    k_copy_diag_inv<<<ib, PB, 0, st>>>(Ld, X, d, i0, ib);
+    if (i0 == 0) continue;
+    // T2 = L[i0:i0+ib, 0:i0] * X[0:i0, 0:i0]   (X lower triangular)
+    GemmArgs g1 = {ib, (int)i0, (int)i0, B + i0 * d, d, X, d, T, d, 0, 0, 1, nullptr};
+    if (launch_gemm(false, false, g1, st)) return LLMC_ECUDA;
+    // X[i0:i0+ib, 0:i0] = -Linv_ii * T2
+    GemmArgs g2 = {ib, (int)i0, ib, Ld, PB, T, d, X + i0 * d, d, 2, 0, 0, nullptr};
+    if (launch_gemm(false, false, g2, st)) return LLMC_ECUDA;
+  }
+  k_reverse_to_upper<<<rg, 256, 0, st>>>(X, Hinv, d);
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes) {
+  if (!bytes || rows < 0 || cols < 0) return LLMC_EINVAL_ARG;
+  *bytes = (int64_t)sizeof(float) * (rows * cols + (int64_t)QB * rows + rows + 4) + 256;
+  return LLMC_OK;
+}
+
+int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const uint8_t* dead,
+                       const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp, int64_t blocksize,
+                       void* wq_bf16, float* loss_out, void* workspace, const int* status, void* stream) {
+  if (!args || !Hinv || !loss_out || !workspace || rows < 0 || cols <= 0) return LLMC_EINVAL_ARG;
+  if (blocksize != QB) return LLMC_ENOSUPPORT;
+  QArgs q = to_qargs(*args);
+  if (q.is_float) return LLMC_ENOSUPPORT;
+  if (q.strategy != LLMC_STRAT_TENSOR && q.strategy != LLMC_STRAT_CHANNEL && q.strategy != LLMC_STRAT_GROUP)
+    return LLMC_ENOSUPPORT;
+  if (q.strategy == LLMC_STRAT_GROUP && (q.group <= 0 || cols % q.group)) return LLMC_EINVAL_SHAPE;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (rows == 0) {
+    return cudaMemsetAsync(loss_out, 0, sizeof(float), st) == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+  }
+  float* W = (float*)workspace;
+  float* E = W + rows * cols;
+  float* L = E + (int64_t)QB * rows;
+  k_init_w<<<grid_for(rows * cols), 256, 0, st>>>((const uint16_t*)w_bf16, W, rows, cols, dead);
+  if (cudaMemsetAsync(L, 0, sizeof(float) * rows, st) != cudaSuccess) return LLMC_ECUDA;
+  static uint64_t attr_mask = 0;
+  const int smem = (QB * QB + ROWS * QS_LD) * (int)sizeof(float);
+  if (!set_smem_attr(k_gptq_block, smem, &attr_mask)) return LLMC_ECUDA;
+  BlockArgs ba;
+  ba.W = W; ba.r = rows; ba.c = cols; ba.U = Hinv;
+  ba.scale = (const uint16_t*)scale_bf16; ba.zp = q.symmetric ? nullptr : zp;
+  ba.strategy = q.strategy; ba.gs = q.group > 0 ? q.group : 1;
+  ba.qmin = q.qmin(); ba.qmax = q.qmax();
+  ba.err = E; ba.loss = L; ba.status = status;
+  const unsigned nblk = (unsigned)((rows + ROWS - 1) / ROWS);
+  for (int64_t i1 = 0; i1 < cols; i1 += QB) {
+    const int cnt = (int)std::min<int64_t>(QB, cols - i1);
+    ba.i1 = (int)i1; ba.count = cnt;
+    k_gptq_block<<<nblk, ROWS, smem, st>>>(ba);
+    const int64_t i2 = i1 + cnt;
+    if (i2 < cols) {
+      // W[:, i2:] -= Err1 * Hinv[i1:i2, i2:]   (Err1 stored column-major: QB x rows)
+      GemmArgs g = {(int)rows, (int)(cols - i2), cnt, E, rows, Hinv + i1 * cols + i2, cols, W + i2, cols, 1, 0, 0,
+                    status};
+      // the identity fallback has no off-diagonal Hinv: the reference's update is a no-op there
+      if (launch_gemm(true, false, g, st)) return LLMC_ECUDA;
+    }
+  }
+  k_finish<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows * cols);
+  k_sum<<<1, 1024, 0, st>>>(L, rows, loss_out);
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+}  // extern "C"

@@ -91,3 +91,150 @@ def accumulate_hessian(
     else:
         hessian_update_(H, x, 2.0, num_samples, float(num_added))
     return H, num_samples
+
+
+_I64P = ctypes.POINTER(ctypes.c_int64)
+_lib.extend_signatures(
+    {
+        "llmc_gptq_prepare_hessian": [_P, _I64, _F32, _P, _P],
+        "llmc_gptq_hinv_workspace_size": [_I64, _I64P],
+        "llmc_gptq_hinv": [_P, _I64, _P, _P, _P, _P],
+        "llmc_gptq_quantize_workspace_size": [_I64, _I64, _I64P],
+        "llmc_gptq_quantize": [_P, _I64, _I64, _P, _P, ctypes.POINTER(_lib.QuantArgs), _P, _P, _I64, _P, _P, _P, _P,
+                               _P],
+    }
+)
+
+
+def _ws_bytes(fn, *args) -> int:
+    out = ctypes.c_int64(0)
+    check(fn(*args, ctypes.byref(out)), fn.__name__)
+    return int(out.value)
+
+
+class InverseHessian:
+    """Damped, dead-masked inverse-Hessian factor shared by every module that
+    consumes the same Hessian (q/k/v, gate/up).  ``status`` stays on the
+    device; ``ok()`` reads it (one host sync)."""
+
+    def __init__(self, hinv: torch.Tensor, dead: torch.Tensor, status: torch.Tensor):
+        self.hinv, self.dead, self.status = hinv, dead, status
+
+    def ok(self) -> bool:
+        return int(self.status.item()) != _lib.ENOT_PD
+
+
+def inverse_hessian(H: torch.Tensor, percdamp: float = 0.01) -> InverseHessian:
+    """Dead-column mask, damping and the upper Cholesky factor of H^-1
+    (S/modifiers/gptq/gptq_quantize.py:35-38,177-196).  ``H`` is clobbered."""
+    require_cuda(H)
+    if H.dtype != torch.float32 or H.ndim != 2 or H.shape[0] != H.shape[1]:
+        raise ValueError("hessian must be a float32 (d, d) tensor")
+    H = H.contiguous()
+    d = H.shape[0]
+    dev = H.device
+    st = stream_ptr(dev)
+    dead = torch.empty(d, dtype=torch.uint8, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib().llmc_gptq_prepare_hessian(ptr(H), d, float(percdamp), ptr(dead), st), "gptq_prepare_hessian")
+    ws = torch.empty(_ws_bytes(lib().llmc_gptq_hinv_workspace_size, d), dtype=torch.uint8, device=dev)
+    hinv = torch.empty(d, d, dtype=torch.float32, device=dev)
+    check(lib().llmc_gptq_hinv(ptr(H), d, ptr(hinv), ptr(ws), ptr(status), st), "gptq_hinv")
+    return InverseHessian(hinv, dead, status)
+
+
+def _strategy(args) -> str:
+    return getattr(args.strategy, "value", args.strategy)
+
+
+def weight_qparams(module: torch.nn.Module, quant_args) -> tuple[torch.Tensor, torch.Tensor]:
+    """The weight observer's qparams (S/modifiers/gptq/gptq_quantize.py:168-173).
+
+    Weights are always observed memorylessly (S/modifiers/quantization/calibration.py:64-78);
+    the min-max statistics of the unmodified weight are recomputed on the GPU.
+    An attached observer's statistics are released as ``get_qparams`` does.
+    """
+    from . import ops
+
+    obs = getattr(module, "weight_observer", None)
+    if obs is not None and "mse" in type(obs).__name__.lower():
+        raise NotImplementedError("MSE weight observers are not implemented on this path")
+    mn, mx = ops.observe_minmax(module.weight, quant_args)
+    scale, zp = ops.calculate_qparams(mn, mx, quant_args)
+    if obs is not None and hasattr(obs, "delete_statistics"):
+        try:
+            obs.delete_statistics()
+        except Exception:  # an observer without statistics: nothing to release
+            pass
+    return scale, zp
+
+
+def quantize_with_inverse(weight: torch.Tensor, quant_args, hinv: InverseHessian, scale: torch.Tensor,
+                          zero_point: torch.Tensor | None, blocksize: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+    """GPTQ block loop for one bf16 weight with a prepared inverse factor.
+    Returns (fake-quantized bf16 weight, loss as a float32 device scalar)."""
+    require_cuda(weight, scale)
+    if weight.dtype != torch.bfloat16:
+        raise NotImplementedError(f"weights of dtype {weight.dtype}: the GPTQ kernels take bf16 weights")
+    w = weight.contiguous()
+    rows, cols = w.shape
+    if hinv.hinv.shape[0] != cols:
+        raise ValueError(f"Hessian size {hinv.hinv.shape[0]} != weight columns {cols}")
+    dev = w.device
+    qa = _lib.qargs_struct(quant_args)
+    zp = None
+    if not quant_args.symmetric:
+        zp = zero_point.to(torch.int8).contiguous()
+    scale_bf16 = scale.to(torch.bfloat16).contiguous()
+    ws = torch.empty(_ws_bytes(lib().llmc_gptq_quantize_workspace_size, rows, cols), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(w)
+    loss = torch.empty(1, dtype=torch.float32, device=dev)
+    check(lib().llmc_gptq_quantize(ptr(w), rows, cols, ptr(hinv.hinv), ptr(hinv.dead), ctypes.byref(qa),
+                                   ptr(scale_bf16), ptr(zp), int(blocksize), ptr(out), ptr(loss), ptr(ws),
+                                   ptr(hinv.status), stream_ptr(dev)), "gptq_quantize")
+    return out, loss
+
+
+def _warn_fallback():
+    from loguru import logger
+
+    logger.warning(
+        "Failed to invert hessian due to numerical instability. Consider "
+        "increasing GPTQModifier.dampening_frac, increasing the number "
+        "of calibration samples, or shuffling the calibration dataset. "
+        "Falling back to round-to-nearest for this module."
+    )
+
+
+def quantize_weight(
+    module: torch.nn.Module,
+    quant_args,
+    hessian: torch.Tensor,
+    blocksize: int = 128,
+    percdamp: float = 0.01,
+):
+    """``quantize_weight`` (S/modifiers/gptq/gptq_quantize.py:100-296).
+
+    :return: (loss, q_param_dict) with ``weight`` (weight dtype),
+        ``weight_scale`` (weight dtype) and ``weight_zero_point`` (zp_dtype).
+    """
+    actorder = getattr(quant_args, "actorder", None)
+    actorder = getattr(actorder, "value", actorder)
+    if actorder:
+        raise NotImplementedError("activation ordering is not implemented on this path; pass actorder=None")
+    strategy = _strategy(quant_args)
+    if strategy not in ("tensor", "channel", "group"):
+        raise ValueError(f"Quantization strategy is not supported for GPTQ: {strategy}")
+    final_dtype = module.weight.dtype
+    scale, zp = weight_qparams(module, quant_args)
+    hinv = inverse_hessian(hessian, percdamp)
+    wq, loss = quantize_with_inverse(module.weight, quant_args, hinv, scale, zp, blocksize)
+    if not hinv.ok():
+        _warn_fallback()
+    zp_dtype = getattr(quant_args, "zp_dtype", None) or torch.int8
+    q_param_dict = {
+        "weight": wq.reshape(module.weight.shape).to(final_dtype),
+        "weight_scale": scale.to(dtype=final_dtype),
+        "weight_zero_point": zp.to(dtype=zp_dtype),
+    }
+    return float(loss.item()), q_param_dict
