@@ -66,6 +66,10 @@ enum { LLMC_FMT_PACK_INT32 = 0, /* pack_quantized: int codes, 32/num_bits per in
 
 /* Library version (major*10000 + minor*100 + patch). */
 int llmc_version(void);
+/* Number of kernels this library has launched in the process so far (host
+ * counter, incremented at each launch site); lets a caller count the device
+ * work issued by a region of code.  No counterpart in the reference. */
+int64_t llmc_kernel_launches(void);
 /* Static description of a status code. */
 const char* llmc_status_string(int status);
 

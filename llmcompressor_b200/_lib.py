@@ -61,6 +61,7 @@ _QA = ctypes.POINTER(QuantArgs)
 # name -> argtypes (all return int status unless listed in _RESTYPES)
 _SIGS = {
     "llmc_version": [],
+    "llmc_kernel_launches": [],
     "llmc_status_string": [_I32],
     "llmc_observe_minmax": [_P, _I64, _I64, _QA, _P, _P, _P],
     "llmc_absmax_accumulate": [_P, _I64, _P, _P],
@@ -70,7 +71,7 @@ _SIGS = {
     "llmc_modelfree_quantize": [_P, _I64, _I64, _QA, _P, _I32, _P, _P, _P, _P],
     "llmc_pack_zero_point": [_P, _I64, _I64, _I32, _P, _P],
 }
-_RESTYPES = {"llmc_status_string": ctypes.c_char_p}
+_RESTYPES = {"llmc_status_string": ctypes.c_char_p, "llmc_kernel_launches": ctypes.c_int64}
 
 
 def _register(lib, name, argtypes, restype=ctypes.c_int):
@@ -180,3 +181,8 @@ def qargs_struct(args) -> QuantArgs:
         scale_dtype,
         zp_dtype,
     )
+
+
+def kernel_launches() -> int:
+    """Kernels launched by libllmc_b200 in this process so far."""
+    return int(lib().llmc_kernel_launches())

@@ -15,8 +15,12 @@
 #include "llmc_common.cuh"
 
 #include <algorithm>
+#include <atomic>
 
 namespace llmc {
+
+static std::atomic<long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 enum Mode { MODE_FUSED = 0, MODE_STATS = 1, MODE_GIVEN = 2 };
 
@@ -470,16 +474,16 @@ static int launch_fmt(const CastParams& p, cudaStream_t st) {
     int64_t blocks = std::min<int64_t>((chunks + 256 * VEC_UNROLL - 1) / (256 * VEC_UNROLL), 148 * 16);
     dim3 g((unsigned)std::max<int64_t>(blocks, 1)), b(256);
     switch (tpg) {
-      case 1: k_group_vec<FMT, 1><<<g, b, 0, st>>>(p); break;
-      case 2: k_group_vec<FMT, 2><<<g, b, 0, st>>>(p); break;
-      case 4: k_group_vec<FMT, 4><<<g, b, 0, st>>>(p); break;
-      case 8: k_group_vec<FMT, 8><<<g, b, 0, st>>>(p); break;
-      case 16: k_group_vec<FMT, 16><<<g, b, 0, st>>>(p); break;
-      default: k_group_vec<FMT, 32><<<g, b, 0, st>>>(p); break;
+      case 1: k_group_vec<FMT, 1><<<g, b, 0, st>>>(p); llmc::note_launch(); break;
+      case 2: k_group_vec<FMT, 2><<<g, b, 0, st>>>(p); llmc::note_launch(); break;
+      case 4: k_group_vec<FMT, 4><<<g, b, 0, st>>>(p); llmc::note_launch(); break;
+      case 8: k_group_vec<FMT, 8><<<g, b, 0, st>>>(p); llmc::note_launch(); break;
+      case 16: k_group_vec<FMT, 16><<<g, b, 0, st>>>(p); llmc::note_launch(); break;
+      default: k_group_vec<FMT, 32><<<g, b, 0, st>>>(p); llmc::note_launch(); break;
     }
   } else {
     int ng = n_groups(p);
-    if (ng > 0) k_paramgroup<FMT><<<ng, 256, 0, st>>>(p);
+    if (ng > 0) { k_paramgroup<FMT><<<ng, 256, 0, st>>>(p); llmc::note_launch(); }
   }
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
@@ -514,6 +518,8 @@ extern "C" {
 
 int llmc_version(void) { return 100; }
 
+int64_t llmc_kernel_launches(void) { return (int64_t)g_launches.load(std::memory_order_relaxed); }
+
 const char* llmc_status_string(int s) {
   switch (s) {
     case LLMC_OK: return "ok";
@@ -544,13 +550,13 @@ int llmc_absmax_accumulate(const void* w, int64_t n, float* absmax, void* stream
   if (!w || !absmax || n < 0) return LLMC_EINVAL_ARG;
   if (n == 0) return LLMC_OK;
   int64_t blocks = std::min<int64_t>((n / 8 + 255) / 256 + 1, 148 * 8);
-  k_absmax<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)w, n, absmax);
+  k_absmax<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>((const uint16_t*)w, n, absmax); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
 int llmc_global_scale(const float* absmax, float* gs, void* stream) {
   if (!absmax || !gs) return LLMC_EINVAL_ARG;
-  k_global_scale<<<1, 1, 0, (cudaStream_t)stream>>>(absmax, gs);
+  k_global_scale<<<1, 1, 0, (cudaStream_t)stream>>>(absmax, gs); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
@@ -561,7 +567,7 @@ int llmc_calculate_qparams(const void* mn, const void* mx, int64_t n, const Llmc
   if (a.is_float && !a.symmetric && a.bits == 4) return LLMC_ENOSUPPORT;
   if (n == 0) return LLMC_OK;
   k_qparams<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint16_t*)mn, (const uint16_t*)mx,
-                                                                            n, a, gs, scale_out, zp_out);
+                                                                            n, a, gs, scale_out, zp_out); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
@@ -600,7 +606,7 @@ int llmc_pack_zero_point(const int8_t* zp, int64_t rows, int64_t groups, int bit
   if (!zp || !out || (bits != 4 && bits != 8)) return LLMC_EINVAL_ARG;
   int64_t n = ((rows + 32 / bits - 1) / (32 / bits)) * groups;
   if (n == 0) return LLMC_OK;
-  k_pack_zp<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(zp, rows, groups, bits, out);
+  k_pack_zp<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(zp, rows, groups, bits, out); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 

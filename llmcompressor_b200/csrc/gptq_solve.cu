@@ -181,6 +181,7 @@ static int launch_gemm(bool ta, bool tb, const GemmArgs& g, cudaStream_t st) {
   else if (!ta && tb) k_sgemm<false, true><<<grid, 256, 0, st>>>(g);
   else if (ta && !tb) k_sgemm<true, false><<<grid, 256, 0, st>>>(g);
   else k_sgemm<true, true><<<grid, 256, 0, st>>>(g);
+  llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
@@ -478,7 +479,7 @@ int llmc_gptq_hinv_workspace_size(int64_t d, int64_t* bytes) {
 
 int llmc_gptq_prepare_hessian(float* H, int64_t d, float percdamp, uint8_t* dead, void* stream) {
   if (!H || !dead || d <= 0) return LLMC_EINVAL_ARG;
-  k_prep_hessian<<<1, 1024, 0, (cudaStream_t)stream>>>(H, d, percdamp, dead);
+  k_prep_hessian<<<1, 1024, 0, (cudaStream_t)stream>>>(H, d, percdamp, dead); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
@@ -493,12 +494,12 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, void* workspace, int*
   static uint64_t attr_mask = 0;
   if (!set_smem_attr(k_potrf_diag, 2 * PB * (PB + 1) * (int)sizeof(float), &attr_mask)) return LLMC_ECUDA;
   dim3 rg((unsigned)((d + 255) / 256), (unsigned)d);
-  k_reverse<<<rg, 256, 0, st>>>(A, B, d);
+  k_reverse<<<rg, 256, 0, st>>>(A, B, d); llmc::note_launch();
   // blocked lower Cholesky of B = J A J
   for (int64_t kb0 = 0; kb0 < d; kb0 += PB) {
     const int kb = (int)std::min<int64_t>(PB, d - kb0);
     float* Ld = LinvD + (kb0 / PB) * PB * PB;
-    k_potrf_diag<<<1, 512, 2 * PB * (PB + 1) * sizeof(float), st>>>(B, d, kb0, kb, Ld, status);
+    k_potrf_diag<<<1, 512, 2 * PB * (PB + 1) * sizeof(float), st>>>(B, d, kb0, kb, Ld, status); llmc::note_launch();
     const int rem = (int)(d - kb0 - kb);
     if (rem > 0) {
       // T = B[kb0+kb:, kb0:kb0+kb] * Linv_kk^T
@@ -508,7 +509,7 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, void* workspace, int*
       GemmArgs g2 = {rem, rem, kb, T, PB, T, PB, B + (kb0 + kb) * d + kb0 + kb, d, 1, 1, 0, nullptr};
       if (launch_gemm(false, true, g2, st)) return LLMC_ECUDA;
       // panel back into B
-      k_copy2d<<<dim3(1, rem), 128, 0, st>>>(T, PB, B + (kb0 + kb) * d + kb0, d, rem, kb);
+      k_copy2d<<<dim3(1, rem), 128, 0, st>>>(T, PB, B + (kb0 + kb) * d + kb0, d, rem, kb); llmc::note_launch();
     }
   }
   // blocked inverse X = L^-1 (lower); the strictly upper part of X must be zero
@@ -516,7 +517,7 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, void* workspace, int*
   for (int64_t i0 = 0; i0 < d; i0 += PB) {
     const int ib = (int)std::min<int64_t>(PB, d - i0);
     const float* Ld = LinvD + (i0 / PB) * PB * PB;
-    k_copy_diag_inv<<<ib, PB, 0, st>>>(Ld, X, d, i0, ib);
+    k_copy_diag_inv<<<ib, PB, 0, st>>>(Ld, X, d, i0, ib); llmc::note_launch();
     if (i0 == 0) continue;
     // T2 = L[i0:i0+ib, 0:i0] * X[0:i0, 0:i0]   (X lower triangular)
     GemmArgs g1 = {ib, (int)i0, (int)i0, B + i0 * d, d, X, d, T, d, 0, 0, 1, nullptr};
@@ -525,7 +526,7 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, void* workspace, int*
     GemmArgs g2 = {ib, (int)i0, ib, Ld, PB, T, d, X + i0 * d, d, 2, 0, 0, nullptr};
     if (launch_gemm(false, false, g2, st)) return LLMC_ECUDA;
   }
-  k_reverse_to_upper<<<rg, 256, 0, st>>>(X, Hinv, d);
+  k_reverse_to_upper<<<rg, 256, 0, st>>>(X, Hinv, d); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
@@ -552,7 +553,7 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
   float* W = (float*)workspace;
   float* E = W + rows * cols;
   float* L = E + (int64_t)QB * rows;
-  k_init_w<<<grid_for(rows * cols), 256, 0, st>>>((const uint16_t*)w_bf16, W, rows, cols, dead);
+  k_init_w<<<grid_for(rows * cols), 256, 0, st>>>((const uint16_t*)w_bf16, W, rows, cols, dead); llmc::note_launch();
   if (cudaMemsetAsync(L, 0, sizeof(float) * rows, st) != cudaSuccess) return LLMC_ECUDA;
   static uint64_t attr_mask = 0;
   const int smem = (QB * QB + ROWS * QS_LD) * (int)sizeof(float);
@@ -567,7 +568,7 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
   for (int64_t i1 = 0; i1 < cols; i1 += QB) {
     const int cnt = (int)std::min<int64_t>(QB, cols - i1);
     ba.i1 = (int)i1; ba.count = cnt;
-    k_gptq_block<<<nblk, ROWS, smem, st>>>(ba);
+    k_gptq_block<<<nblk, ROWS, smem, st>>>(ba); llmc::note_launch();
     const int64_t i2 = i1 + cnt;
     if (i2 < cols) {
       // W[:, i2:] -= Err1 * Hinv[i1:i2, i2:]   (Err1 stored column-major: QB x rows)
@@ -577,8 +578,8 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
       if (launch_gemm(true, false, g, st)) return LLMC_ECUDA;
     }
   }
-  k_finish<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows * cols);
-  k_sum<<<1, 1024, 0, st>>>(L, rows, loss_out);
+  k_finish<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows * cols); llmc::note_launch();
+  k_sum<<<1, 1024, 0, st>>>(L, rows, loss_out); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 

@@ -342,7 +342,7 @@ int llmc_hessian_accumulate(const void* x, int64_t n_tokens, int64_t d, int64_t 
   if ((!x && n_tokens > 0) || !H || d <= 0 || n_tokens < 0 || ld < d) return LLMC_EINVAL_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   if (n_tokens == 0) {
-    if (num_samples && num_add != 0.f) k_add_scalar<<<1, 1, 0, st>>>(num_samples, num_add);
+    if (num_samples && num_add != 0.f) { k_add_scalar<<<1, 1, 0, st>>>(num_samples, num_add); llmc::note_launch(); }
     return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
   }
   const bool tma_ok = (d % 8 == 0) && (ld % 8 == 0) && (((uintptr_t)x & 15) == 0) && (((uintptr_t)H & 15) == 0) &&
@@ -350,7 +350,7 @@ int llmc_hessian_accumulate(const void* x, int64_t n_tokens, int64_t d, int64_t 
   if (!tma_ok) {
     int64_t nt = (d + 63) / 64;
     k_hessian_simt<<<dim3((unsigned)nt, (unsigned)nt), dim3(16, 16), 0, st>>>((const uint16_t*)x, n_tokens, d, ld, H,
-                                                                             alpha, num_samples, num_add);
+                                                                             alpha, num_samples, num_add); llmc::note_launch();
     return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
   }
   CUtensorMap xmap, hmap;
@@ -384,7 +384,7 @@ int llmc_hessian_accumulate(const void* x, int64_t n_tokens, int64_t d, int64_t 
     }
   }
   int grid = std::min(p.num_tiles, num_sms());
-  k_hessian_tc<<<grid, THREADS, SMEM_TOTAL, st>>>(xmap, hmap, p);
+  k_hessian_tc<<<grid, THREADS, SMEM_TOTAL, st>>>(xmap, hmap, p); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 

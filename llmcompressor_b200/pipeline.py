@@ -1,0 +1,154 @@
+"""Layer-level GPTQ on the GPU: the per-decoder-layer work of the reference's
+sequential pipeline (S/pipelines/sequential/pipeline.py:136-178) restricted
+to the hot path -- Hessian accumulation from the hooks, the solve at
+``sequential_epoch_end`` (S/modifiers/gptq/base.py:239-321) and the
+compressed-tensors pack done at save time
+(S/transformers/compression/compressed_tensors_utils.py:172-191).
+
+Differences in structure (not in results) from the reference:
+
+* one Hessian per distinct Linear input (q/k/v share ``attn_in``, gate/up
+  share ``mlp_in``) instead of one per module, fed with batches of
+  calibration tokens instead of one hook call per sample;
+* one factorisation per Hessian, shared by the modules that read it;
+* with several ranks: tokens are split across ranks, Hessians are reduced to
+  an owner, the owner broadcasts the inverse factor, and every rank solves an
+  equal slice of every module's rows (see ``distributed``).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib, gptq, ops
+from .distributed import (
+    broadcast_inverse,
+    gather_rows,
+    greedy_owners,
+    reduce_to_owners,
+    row_range,
+    solve_cost,
+    world,
+)
+
+
+@dataclass(frozen=True)
+class LinearSpec:
+    name: str
+    out_features: int
+    in_features: int
+    input_key: str
+
+
+@dataclass
+class LayerResult:
+    """Compressed-tensors state of one module (``pack-quantized``)."""
+
+    weight_packed: torch.Tensor
+    weight_scale: torch.Tensor
+    loss: torch.Tensor  # float32 device scalar (this rank's share of rows)
+    rows: tuple[int, int]
+    weight_shape: tuple[int, int] = field(default=(0, 0))
+
+
+def llama_layer_specs(hidden: int, intermediate: int, heads: int, kv_heads: int, head_dim: int) -> list[LinearSpec]:
+    """The seven Linear modules of a Llama decoder layer and the input each reads."""
+    return [
+        LinearSpec("self_attn.q_proj", heads * head_dim, hidden, "attn_in"),
+        LinearSpec("self_attn.k_proj", kv_heads * head_dim, hidden, "attn_in"),
+        LinearSpec("self_attn.v_proj", kv_heads * head_dim, hidden, "attn_in"),
+        LinearSpec("self_attn.o_proj", hidden, heads * head_dim, "o_in"),
+        LinearSpec("mlp.gate_proj", intermediate, hidden, "mlp_in"),
+        LinearSpec("mlp.up_proj", intermediate, hidden, "mlp_in"),
+        LinearSpec("mlp.down_proj", hidden, intermediate, "down_in"),
+    ]
+
+
+def input_dims(specs: list[LinearSpec]) -> dict[str, int]:
+    dims: dict[str, int] = {}
+    for s in specs:
+        dims.setdefault(s.input_key, s.in_features)
+    return dims
+
+
+class LayerHessians:
+    """Float32 Hessian buffers, one per distinct input, reused across layers."""
+
+    def __init__(self, dims: dict[str, int], device: torch.device):
+        self.dims = dict(dims)
+        self.H = {k: torch.zeros(d, d, dtype=torch.float32, device=device) for k, d in dims.items()}
+
+    def reset(self) -> None:
+        for h in self.H.values():
+            h.zero_()
+
+    def accumulate(self, key: str, x2d: torch.Tensor, alpha: float) -> None:
+        """H[key] += alpha * x^T x (tensor cores); alpha = 2 / num_samples
+        gives the reference's averaged Hessian H / num_samples directly."""
+        gptq.hessian_update_(self.H[key], x2d, alpha)
+
+
+def solve_layer(
+    weights: dict[str, torch.Tensor],
+    specs: list[LinearSpec],
+    hessians: LayerHessians,
+    quant_args,
+    percdamp: float = 0.01,
+    blocksize: int = 128,
+    gather_to: int | None = 0,
+    pack_events: list | None = None,
+) -> dict[str, LayerResult]:
+    """GPTQ-quantize and pack every module of one layer from its (averaged)
+    Hessians.  On several ranks each rank returns its row slice; with
+    ``gather_to`` set, that rank also receives the full packed tensors."""
+    rank, ws = world()
+    dims = hessians.dims
+    rows_of: dict[str, int] = {}
+    for s in specs:
+        rows_of[s.input_key] = rows_of.get(s.input_key, 0) + s.out_features
+    owners = greedy_owners({k: solve_cost(d, rows_of[k]) for k, d in dims.items()}, ws)
+    reduce_to_owners(hessians.H, owners)
+    dev = next(iter(hessians.H.values())).device
+    inv: dict[str, gptq.InverseHessian] = {}
+    for key, d in dims.items():
+        if owners[key] == rank:
+            inv[key] = gptq.inverse_hessian(hessians.H[key], percdamp)
+        else:
+            inv[key] = gptq.InverseHessian(
+                torch.empty(d, d, dtype=torch.float32, device=dev),
+                torch.empty(d, dtype=torch.uint8, device=dev),
+                torch.empty(1, dtype=torch.int32, device=dev),
+            )
+    broadcast_inverse({k: [v.hinv, v.dead, v.status] for k, v in inv.items()}, owners)
+
+    out: dict[str, LayerResult] = {}
+    for s in specs:
+        w = weights[s.name]
+        r0, r1 = row_range(s.out_features, rank, ws)
+        wl = w[r0:r1]
+        if r1 > r0:
+            mn, mx = ops.observe_minmax(wl, quant_args)
+            scale, zp = ops.calculate_qparams(mn, mx, quant_args)
+            wq, loss = gptq.quantize_with_inverse(wl, quant_args, inv[s.input_key], scale, zp, blocksize)
+            if pack_events is not None:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+            packed = ops.quantize_pack(wq, quant_args, scale, None if quant_args.symmetric else zp,
+                                       fmt=_lib.FMT_PACK_INT32)
+            if pack_events is not None:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record()
+                pack_events.append((e0, e1, wq.numel()))
+        else:
+            pf = 32 // quant_args.num_bits
+            packed = torch.empty(0, -(-s.in_features // pf), dtype=torch.int32, device=dev)
+            scale = torch.empty(0, ops.stats_shape(1, s.in_features, quant_args)[-1], dtype=torch.bfloat16, device=dev)
+            loss = torch.zeros(1, dtype=torch.float32, device=dev)
+        if ws > 1 and gather_to is not None:
+            fp = gather_rows(packed, s.out_features, dst=gather_to)
+            fs = gather_rows(scale, s.out_features, dst=gather_to)
+            if rank == gather_to:
+                packed, scale = fp, fs
+        out[s.name] = LayerResult(packed, scale, loss, (r0, r1), (s.out_features, s.in_features))
+    return out

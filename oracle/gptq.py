@@ -27,7 +27,7 @@ def accumulate_hessian(x: np.ndarray, H: np.ndarray, num_samples: float) -> tupl
         x = x[None]
     num_samples += x.shape[0]
     xs = F32(math.sqrt(2)) * x.reshape(-1, x.shape[-1])
-    H += xs.T @ xs
+    H += np.ascontiguousarray(xs.T) @ xs
     return H, num_samples
 
 
@@ -70,8 +70,12 @@ def quantize_weight(
     args: QArgs,
     blocksize: int = 128,
     percdamp: float = 0.01,
+    hinv: np.ndarray | None = None,
 ):
     """``quantize_weight`` (S/modifiers/gptq/gptq_quantize.py:100-296), actorder off.
+
+    ``hinv`` (optional): a precomputed inverse factor for this H, so that the
+    block loop can be timed apart from the factorisation.
 
     ``w_bf16``: (rows, cols) bf16 values as float32.  ``H``: the averaged
     Hessian (H / num_samples, ``S/modifiers/gptq/base.py:594``).
@@ -98,7 +102,10 @@ def quantize_weight(
     dead = np.diag(H) == 0  # _mask_dead_hessian (:35-38)
     H[dead, dead] = 1
     W[:, dead] = 0
-    Hinv, ok = hinv_upper(H, percdamp)
+    if hinv is None:
+        Hinv, ok = hinv_upper(H, percdamp)
+    else:
+        Hinv, ok = hinv, True
 
     losses = np.zeros(r, dtype=F32)
     for i1 in range(0, c, blocksize):
