@@ -175,6 +175,32 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
                        const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp, int64_t blocksize,
                        void* wq_bf16, float* loss, void* workspace, const int* status, void* stream);
 
+/* ---------------------------------------------------------------- no-allocation variant
+ * llmc_gptq_quantize for callers that cannot allocate device memory -- code
+ * running during CUDA stream capture (where cudaMalloc is not allowed),
+ * hosts that own all device memory and expose no allocator, bare FFI
+ * bindings.  It takes the same inputs and outputs but no workspace: the
+ * scratch is a fixed array of LLMC_GPTQ_NOALLOC_SCRATCH_BYTES compiled into
+ * the library, held on every GPU that loads the library's device code until
+ * the process exits.  No counterpart in the reference.
+ *  - Size limit: returns LLMC_EINVAL_SHAPE, launching nothing, when
+ *    llmc_gptq_quantize_workspace_size(rows, cols) exceeds the array
+ *    (rows*cols*4 + rows*516 + 272 bytes > 32 MiB; e.g. 1024 x 4096 fits,
+ *    4096 x 4096 does not).
+ *  - The first call on a device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - Every call shares the one array: calls whose kernels overlap on the GPU
+ *    (other streams, other host threads) race and corrupt each other.
+ *    Calls ordered on one stream are safe; nothing from a previous call's
+ *    contents is read.
+ *  - Allocates nothing (no cudaMalloc/cudaFree). */
+#define LLMC_GPTQ_NOALLOC_SCRATCH_BYTES (32ll << 20)
+int llmc_gptq_quantize_noalloc(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv,
+                               const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16,
+                               const int8_t* zp, int64_t blocksize, void* wq_bf16, float* loss, const int* status,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif
