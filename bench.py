@@ -390,8 +390,63 @@ def cpu_sample(steps: int, warmup: int) -> dict:
     }
 
 
+def run_micro(args) -> None:
+    """One kernel on a small case (profiling captures and per-kernel timing):
+    hessian: H += alpha X^T X, X (tokens x d); gptq: factor + block loop of
+    one (rows x d) weight; cast: W4A16 model-free pass over a (rows x d) weight."""
+    from llmcompressor_b200 import gptq, ops
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    d, n, rows = args.d, args.tokens, args.rows
+    qa = w4a16_args()
+    if args.micro == "hessian":
+        x = torch.randn(n, d, device=dev, generator=g).to(torch.bfloat16)
+        H = torch.zeros(d, d, device=dev)
+        fn = lambda: gptq.hessian_update_(H, x, 2.0 / n)  # noqa: E731
+        work, unit = n * d * (d + 1) / 1e12, "TFLOP/s"
+    elif args.micro in ("gptq", "hinv"):
+        w = (0.02 * torch.randn(rows, d, device=dev, generator=g)).to(torch.bfloat16)
+        x = torch.randn(4096, d, device=dev, generator=g).to(torch.bfloat16)
+        H0 = torch.zeros(d, d, device=dev)
+        gptq.hessian_update_(H0, x, 2.0 / 4096)
+        mn, mx = ops.observe_minmax(w, qa)
+        scale, zp = ops.calculate_qparams(mn, mx, qa)
+
+        def fn():
+            inv = gptq.inverse_hessian(H0.clone(), 0.01)
+            if args.micro == "hinv":
+                return inv
+            return gptq.quantize_with_inverse(w, qa, inv, scale, zp)
+
+        work, unit = None, "ms"
+    else:
+        w = (0.02 * torch.randn(rows, d, device=dev, generator=g)).to(torch.bfloat16)
+        fn = lambda: ops.modelfree_quantize(w, qa)  # noqa: E731
+        work, unit = rows * d * (2 + 0.5 + 2 / 128) / 1e9, "GB/s"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    rate = (work / (ms * 1e-3)) if work is not None else ms
+    print(json.dumps({"micro": args.micro, "d": d, "tokens": n, "rows": rows, "ms_per_call": ms, unit: rate}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--micro", choices=["hessian", "gptq", "hinv", "cast"], default=None,
+                    help="time one kernel on a small case instead of the model benchmark")
+    ap.add_argument("--d", type=int, default=4096)
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=3)
@@ -403,6 +458,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.micro:
+        run_micro(args)
+        return
 
     if args.impl == "reference":
         if rank != 0:

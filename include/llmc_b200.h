@@ -157,7 +157,8 @@ int llmc_hessian_tiles(int64_t d);
  *      1, dead[i] = 1 -- then damp = percdamp * mean(diag), diag += damp
  *      (:181-185).  H (d x d float32) is modified in place.
  *   2. llmc_gptq_hinv: Hinv = upper Cholesky factor of H^-1 (:185-188), in
- *      float32; a non-positive pivot sets *status = LLMC_ENOT_PD (the
+ *      float32, and (if HinvT is not NULL) its transpose, which lets step 3 run
+ *      its trailing updates on the tensor cores; a non-positive pivot sets *status = LLMC_ENOT_PD (the
  *      reference's LinAlgError) and later steps then use the identity
  *      (:189-196, round-to-nearest fallback).  workspace: see
  *      llmc_gptq_hinv_workspace_size.
@@ -165,15 +166,26 @@ int llmc_hessian_tiles(int64_t d);
  *      (rows x cols bf16) with stored bf16 scales / int8 zero points (TENSOR,
  *      CHANNEL or GROUP; blocksize 128), writing the fake-quantized bf16
  *      weight and the summed loss (float32 scalar).  Dead columns are zeroed
- *      first (:38).  workspace: see llmc_gptq_quantize_workspace_size.
+ *      first (:38).  HinvT (optional) is the transposed factor from step 2.  workspace: see llmc_gptq_quantize_workspace_size.
  * Nothing synchronises; *status is read by the caller when it needs it. */
 int llmc_gptq_prepare_hessian(float* H, int64_t d, float percdamp, uint8_t* dead, void* stream);
 int llmc_gptq_hinv_workspace_size(int64_t d, int64_t* bytes);
-int llmc_gptq_hinv(const float* H, int64_t d, float* Hinv, void* workspace, int* status, void* stream);
+int llmc_gptq_hinv(const float* H, int64_t d, float* Hinv, float* HinvT, void* workspace, int* status,
+                   void* stream);
 int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes);
-int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const uint8_t* dead,
-                       const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp, int64_t blocksize,
-                       void* wq_bf16, float* loss, void* workspace, const int* status, void* stream);
+int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
+                       const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp,
+                       int64_t blocksize, void* wq_bf16, float* loss, void* workspace, const int* status,
+                       void* stream);
+
+/* Float32-accurate GEMM on the tensor cores (3xTF32 split):
+ *   C (m x n, ldc) = A*B^T (mode 0), C - A*B^T (mode 1) or -A*B^T (mode 2),
+ * A row-major m x k, B row-major n x k -- the shape of the GPTQ trailing update
+ * `W[:, i2:] -= Err1.matmul(Hinv[i1:i2, i2:])` (S/modifiers/gptq/gptq_quantize.py:276-277,
+ * with B = the transposed factor) and of the factorisation updates.
+ * Pointers 16-byte aligned and lda/ldb multiples of 4, else LLMC_ENOSUPPORT. */
+int llmc_gemm_f32_nt(int64_t m, int64_t n, int64_t k, const float* A, int64_t lda, const float* B, int64_t ldb,
+                     float* C, int64_t ldc, int mode, void* stream);
 
 /* ---------------------------------------------------------------- no-allocation variant
  * llmc_gptq_quantize for callers that cannot allocate device memory -- code
@@ -197,7 +209,7 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
  *  - Allocates nothing (no cudaMalloc/cudaFree). */
 #define LLMC_GPTQ_NOALLOC_SCRATCH_BYTES (32ll << 20)
 int llmc_gptq_quantize_noalloc(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv,
-                               const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16,
+                               const float* HinvT, const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16,
                                const int8_t* zp, int64_t blocksize, void* wq_bf16, float* loss, const int* status,
                                void* stream);
 

@@ -50,7 +50,7 @@ int scratch_address(void** out) {
 }  // namespace
 
 extern "C" int llmc_gptq_quantize_noalloc(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv,
-                                          const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16,
+                                          const float* HinvT, const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16,
                                           const int8_t* zp, int64_t blocksize, void* wq_bf16, float* loss,
                                           const int* status, void* stream) {
   int64_t need = 0;
@@ -62,6 +62,6 @@ extern "C" int llmc_gptq_quantize_noalloc(const void* w_bf16, int64_t rows, int6
   // The workspace contents left by an earlier call are never read: the
   // float32 weight copy and the block errors are written before use, and
   // llmc_gptq_quantize zeroes the per-row losses itself.
-  return llmc_gptq_quantize(w_bf16, rows, cols, Hinv, dead, args, scale_bf16, zp, blocksize, wq_bf16, loss, ws,
+  return llmc_gptq_quantize(w_bf16, rows, cols, Hinv, HinvT, dead, args, scale_bf16, zp, blocksize, wq_bf16, loss, ws,
                             status, stream);
 }

@@ -23,6 +23,7 @@
 // across sub-blocks and across 128-column blocks the update is the lazy
 // batched form W -= Err * U (the reference's `Err1.matmul(Hinv[i1:i2, i2:])`).
 #include "llmc_common.cuh"
+#include "tc32.cuh"
 
 #include <algorithm>
 
@@ -174,8 +175,23 @@ __global__ void __launch_bounds__(256) k_sgemm(GemmArgs g) {
   }
 }
 
+// The tensor-core GEMM is used by the solve once it has passed its own parity
+// test against float64 for every operand layout.
+static bool g_use_tc32 = true;
+
 static int launch_gemm(bool ta, bool tb, const GemmArgs& g, cudaStream_t st) {
   if (g.m <= 0 || g.n <= 0) return LLMC_OK;
+  // Wide updates go to the tensor cores (3xTF32, float32 accuracy); small or
+  // TMA-unaligned ones stay on the CUDA cores.
+  if (g_use_tc32 && !g.b_lower && (int64_t)g.m * g.n * g.k >= (int64_t)128 * 128 * 128) {
+    tc32::Gemm t;
+    t.m = g.m; t.n = g.n; t.k = g.k;
+    t.A = g.A; t.lda = g.lda; t.a_mn = ta;
+    t.B = g.B; t.ldb = g.ldb; t.b_mn = !tb;
+    t.C = g.C; t.ldc = g.ldc; t.mode = g.mode; t.tri = g.tri; t.skip = g.skip;
+    const int s = tc32::gemm(t, st);
+    if (s != LLMC_ENOSUPPORT) return s;
+  }
   dim3 grid((g.n + GBN - 1) / GBN, (g.m + GBM - 1) / GBM);
   if (!ta && !tb) k_sgemm<false, false><<<grid, 256, 0, st>>>(g);
   else if (!ta && tb) k_sgemm<false, true><<<grid, 256, 0, st>>>(g);
@@ -222,66 +238,89 @@ __global__ void k_reverse(const float* __restrict__ A, float* __restrict__ B, in
   if (i < d && j < d && j <= i) B[i * d + j] = A[(d - 1 - i) * d + (d - 1 - j)];
 }
 
-// U[i][j] = X[d-1-i][d-1-j] for j >= i, 0 below the diagonal
-__global__ void k_reverse_to_upper(const float* __restrict__ X, float* __restrict__ U, int64_t d) {
+// From Xt = L^-T (upper):  U = J L^-1 J = (J Xt J)^T, i.e. U[i][j] = Xt[d-1-j][d-1-i]
+// for j >= i and 0 below the diagonal.  32x32 tiles through shared memory so
+// that both the read and the write are coalesced.
+__global__ void k_xt_to_u(const float* __restrict__ Xt, float* __restrict__ U, int64_t d) {
+  __shared__ float tile[32][33];
+  const int64_t I0 = (int64_t)blockIdx.y * 32, J0 = (int64_t)blockIdx.x * 32;
+  for (int jj = threadIdx.y; jj < 32; jj += 8) {
+    const int ii = threadIdx.x;
+    const int64_t a = d - 1 - J0 - jj, b = d - 1 - I0 - ii;
+    tile[jj][ii] = (a >= 0 && b >= 0) ? Xt[a * d + b] : 0.0f;
+  }
+  __syncthreads();
+  for (int ii = threadIdx.y; ii < 32; ii += 8) {
+    const int jj = threadIdx.x;
+    const int64_t i = I0 + ii, j = J0 + jj;
+    if (i < d && j < d) U[i * d + j] = (j >= i) ? tile[jj][ii] : 0.0f;
+  }
+}
+
+// U^T (lower): Ut[i][j] = U[j][i] = Xt[d-1-i][d-1-j] for j <= i, 0 above.
+__global__ void k_xt_to_ut(const float* __restrict__ Xt, float* __restrict__ Ut, int64_t d) {
   const int64_t i = blockIdx.y;
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < d && j < d) U[i * d + j] = (j >= i) ? X[(d - 1 - i) * d + (d - 1 - j)] : 0.0f;
+  if (i < d && j < d) Ut[i * d + j] = (j <= i) ? Xt[(d - 1 - i) * d + (d - 1 - j)] : 0.0f;
 }
 
 // Factor one diagonal block (kb <= 128) of B in place (lower Cholesky) and
 // write its lower-triangular inverse to Linv (row stride 128).
 constexpr int PB = 128;
+constexpr int PLD = PB + 1;  // padded row stride of the shared-memory blocks
+// 16 warps: warp w walks rows (w, w+16, ...), its lanes walk the columns of a row.
 __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_t k0, int kb, float* Linv,
                                                     int* status) {
   extern __shared__ float sm[];
-  float* S = sm;                 // [PB][PB+1]
-  float* X = sm + PB * (PB + 1);  // [PB][PB+1]
+  float* S = sm;             // [PB][PLD]  L of this block
+  float* X = sm + PB * PLD;  // [PB][PLD]  its inverse
   __shared__ int bad;
-  const int t = threadIdx.x, nt = blockDim.x;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  constexpr int NW = 16;
   if (t == 0) bad = 0;
-  for (int e = t; e < kb * kb; e += nt) {
-    const int i = e / kb, j = e % kb;
-    S[i * (PB + 1) + j] = (j <= i) ? B[(k0 + i) * ld + k0 + j] : 0.f;
-  }
-  __syncthreads();
-  for (int j = 0; j < kb; ++j) {
-    if (t == 0) {
-      float p = S[j * (PB + 1) + j];
-      if (!(p > 0.0f)) { bad = 1; p = 1.0f; }
-      S[j * (PB + 1) + j] = sqrtf(p);
+  for (int i = warp; i < kb; i += NW)
+    for (int j = lane; j < kb; j += 32) {
+      S[i * PLD + j] = (j <= i) ? B[(k0 + i) * ld + k0 + j] : 0.f;
+      X[i * PLD + j] = (i == j) ? 1.0f : 0.f;
     }
+  __syncthreads();
+  // right-looking Cholesky, two barriers per column
+  for (int j = 0; j < kb; ++j) {
+    float p = S[j * PLD + j];
+    if (!(p > 0.0f)) { if (t == 0) bad = 1; p = 1.0f; }
+    const float piv = sqrtf(p);
+    const int i = j + 1 + t;
+    if (i < kb) S[i * PLD + j] = __fdiv_rn(S[i * PLD + j], piv);
     __syncthreads();
-    const float piv = S[j * (PB + 1) + j];
-    for (int i = j + 1 + t; i < kb; i += nt) S[i * (PB + 1) + j] = __fdiv_rn(S[i * (PB + 1) + j], piv);
-    __syncthreads();
-    // trailing rank-1 update of the lower triangle
-    const int rem = kb - j - 1;
-    for (int e = t; e < rem * rem; e += nt) {
-      const int i = j + 1 + e / rem, l = j + 1 + e % rem;
-      if (l <= i) S[i * (PB + 1) + l] -= S[i * (PB + 1) + j] * S[l * (PB + 1) + j];
+    if (t == 0) S[j * PLD + j] = piv;
+    for (int r = j + 1 + warp; r < kb; r += NW) {
+      const float srj = S[r * PLD + j];
+      for (int l = j + 1 + lane; l <= r; l += 32) S[r * PLD + l] -= srj * S[l * PLD + j];
     }
     __syncthreads();
   }
   if (t == 0 && bad && status) atomicExch(status, LLMC_ENOT_PD);
-  for (int e = t; e < kb * kb; e += nt) {
-    const int i = e / kb, j = e % kb;
-    if (j <= i) B[(k0 + i) * ld + k0 + j] = S[i * (PB + 1) + j];
-  }
-  // inverse by forward substitution, one column per thread
-  for (int c = t; c < kb; c += nt) {
-    for (int i = 0; i < kb; ++i) X[i * (PB + 1) + c] = 0.f;
-    for (int i = c; i < kb; ++i) {
-      float s = (i == c) ? 1.0f : 0.0f;
-      for (int l = c; l < i; ++l) s -= S[i * (PB + 1) + l] * X[l * (PB + 1) + c];
-      X[i * (PB + 1) + c] = __fdiv_rn(s, S[i * (PB + 1) + i]);
+  // inverse by right-looking forward substitution on X = I, two barriers per row
+  for (int l = 0; l < kb; ++l) {
+    if (t <= l) X[l * PLD + t] = __fdiv_rn(X[l * PLD + t], S[l * PLD + l]);
+    __syncthreads();
+    for (int r = l + 1 + warp; r < kb; r += NW) {
+      const float srl = S[r * PLD + l];
+      for (int c = lane; c <= l; c += 32) X[r * PLD + c] -= srl * X[l * PLD + c];
     }
+    __syncthreads();
   }
-  __syncthreads();
-  for (int e = t; e < PB * PB; e += nt) {
-    const int i = e / PB, j = e % PB;
-    Linv[i * PB + j] = (i < kb && j < kb && j <= i) ? X[i * (PB + 1) + j] : 0.f;
-  }
+  for (int i = warp; i < PB; i += NW)
+    for (int j = lane; j < PB; j += 32) {
+      const bool in = i < kb && j < kb && j <= i;
+      Linv[i * PB + j] = in ? X[i * PLD + j] : 0.f;
+      if (in) B[(k0 + i) * ld + k0 + j] = S[i * PLD + j];
+    }
+}
+
+__global__ void k_eye(float* X, int64_t d) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < d) X[i * d + i] = 1.0f;
 }
 
 __global__ void k_copy2d(const float* __restrict__ src, int64_t lds, float* __restrict__ dst, int64_t ldd, int rows,
@@ -289,11 +328,6 @@ __global__ void k_copy2d(const float* __restrict__ src, int64_t lds, float* __re
   const int r = blockIdx.y;
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x)
     if (r < rows) dst[(int64_t)r * ldd + c] = src[(int64_t)r * lds + c];
-}
-
-__global__ void k_copy_diag_inv(const float* __restrict__ Linv, float* __restrict__ X, int64_t d, int64_t k0, int kb) {
-  const int i = blockIdx.x, j = threadIdx.x;
-  if (i < kb && j < kb) X[(k0 + i) * d + k0 + j] = Linv[i * PB + j];
 }
 
 // ---------------------------------------------------------------------------
@@ -382,7 +416,6 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
         const float diff = wi - q;
         loss += __fdiv_rn(diff * diff, d * d);
         const float err = __fdiv_rn(diff, d);
-        a.err[(int64_t)i * a.r + row] = err;
         // shift the sub-block left by one column while applying this column's update
 #pragma unroll
         for (int j = 0; j < SUB - 1; ++j) {
@@ -400,6 +433,10 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
         for (int j = 0; j < SUB - 1; ++j) e[j] = e[j + 1];
         e[SUB - 1] = 0.f;
       }
+      // this sub-block's errors, row-major (rows x 128), as the K-major operand of the trailing update
+      float4* erow = (float4*)(a.err + row * QB + s0);
+#pragma unroll
+      for (int j = 0; j < SUB / 4; ++j) erow[j] = make_float4(e[4 * j], e[4 * j + 1], e[4 * j + 2], e[4 * j + 3]);
       // lazy update of the later columns of this block
       for (int j = s0 + SUB; j < cnt; ++j) {
         float acc = 0.f;
@@ -483,7 +520,8 @@ int llmc_gptq_prepare_hessian(float* H, int64_t d, float percdamp, uint8_t* dead
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
-int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, void* workspace, int* status, void* stream) {
+int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* workspace, int* status,
+                   void* stream) {
   if (!A || !Hinv || !workspace || !status || d <= 0) return LLMC_EINVAL_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t nb = (d + PB - 1) / PB;
@@ -512,21 +550,28 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, void* workspace, int*
       k_copy2d<<<dim3(1, rem), 128, 0, st>>>(T, PB, B + (kb0 + kb) * d + kb0, d, rem, kb); llmc::note_launch();
     }
   }
-  // blocked inverse X = L^-1 (lower); the strictly upper part of X must be zero
-  if (cudaMemsetAsync(X, 0, sizeof(float) * d * d, st) != cudaSuccess) return LLMC_ECUDA;
+  // Xt = L^-T (upper), by right-looking blocked substitution on column blocks of Xt = I:
+  //   Xt[:, i] = Xt[:, i] * Linv_ii^T,   Xt[:, >i] -= Xt[:, i] * L[>i, i]^T
+  // -- every update is an A * B^T product with K = 128 (both operands K-major).
+  float* Xt = X;
+  if (cudaMemsetAsync(Xt, 0, sizeof(float) * d * d, st) != cudaSuccess) return LLMC_ECUDA;
+  k_eye<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(Xt, d); llmc::note_launch();
   for (int64_t i0 = 0; i0 < d; i0 += PB) {
     const int ib = (int)std::min<int64_t>(PB, d - i0);
+    const int nc = (int)(i0 + ib);  // rows of Xt that can be non-zero in these columns
     const float* Ld = LinvD + (i0 / PB) * PB * PB;
-    k_copy_diag_inv<<<ib, PB, 0, st>>>(Ld, X, d, i0, ib); llmc::note_launch();
-    if (i0 == 0) continue;
-    // T2 = L[i0:i0+ib, 0:i0] * X[0:i0, 0:i0]   (X lower triangular)
-    GemmArgs g1 = {ib, (int)i0, (int)i0, B + i0 * d, d, X, d, T, d, 0, 0, 1, nullptr};
-    if (launch_gemm(false, false, g1, st)) return LLMC_ECUDA;
-    // X[i0:i0+ib, 0:i0] = -Linv_ii * T2
-    GemmArgs g2 = {ib, (int)i0, ib, Ld, PB, T, d, X + i0 * d, d, 2, 0, 0, nullptr};
-    if (launch_gemm(false, false, g2, st)) return LLMC_ECUDA;
+    k_copy2d<<<dim3(1, nc), 128, 0, st>>>(Xt + i0, d, T, PB, nc, ib); llmc::note_launch();
+    GemmArgs g1 = {nc, ib, ib, T, PB, Ld, PB, Xt + i0, d, 0, 0, 0, nullptr};
+    if (launch_gemm(false, true, g1, st)) return LLMC_ECUDA;
+    const int rem = (int)(d - i0 - ib);
+    if (rem > 0) {
+      GemmArgs g2 = {nc, rem, ib, Xt + i0, d, B + (i0 + ib) * d + i0, d, Xt + i0 + ib, d, 1, 0, 0, nullptr};
+      if (launch_gemm(false, true, g2, st)) return LLMC_ECUDA;
+    }
   }
-  k_reverse_to_upper<<<rg, 256, 0, st>>>(X, Hinv, d); llmc::note_launch();
+  k_xt_to_u<<<dim3((unsigned)((d + 31) / 32), (unsigned)((d + 31) / 32)), dim3(32, 8), 0, st>>>(Xt, Hinv, d);
+  llmc::note_launch();
+  if (HinvT) { k_xt_to_ut<<<rg, 256, 0, st>>>(Xt, HinvT, d); llmc::note_launch(); }
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
@@ -536,9 +581,10 @@ int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes
   return LLMC_OK;
 }
 
-int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const uint8_t* dead,
-                       const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp, int64_t blocksize,
-                       void* wq_bf16, float* loss_out, void* workspace, const int* status, void* stream) {
+int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
+                       const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp,
+                       int64_t blocksize, void* wq_bf16, float* loss_out, void* workspace, const int* status,
+                       void* stream) {
   if (!args || !Hinv || !loss_out || !workspace || rows < 0 || cols <= 0) return LLMC_EINVAL_ARG;
   if (blocksize != QB) return LLMC_ENOSUPPORT;
   QArgs q = to_qargs(*args);
@@ -571,11 +617,18 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
     k_gptq_block<<<nblk, ROWS, smem, st>>>(ba); llmc::note_launch();
     const int64_t i2 = i1 + cnt;
     if (i2 < cols) {
-      // W[:, i2:] -= Err1 * Hinv[i1:i2, i2:]   (Err1 stored column-major: QB x rows)
-      GemmArgs g = {(int)rows, (int)(cols - i2), cnt, E, rows, Hinv + i1 * cols + i2, cols, W + i2, cols, 1, 0, 0,
-                    status};
-      // the identity fallback has no off-diagonal Hinv: the reference's update is a no-op there
-      if (launch_gemm(true, false, g, st)) return LLMC_ECUDA;
+      // W[:, i2:] -= Err1 * Hinv[i1:i2, i2:]   (Err1 row-major: rows x QB).  With the
+      // transposed factor the product is A * B^T on the tensor cores.  The identity
+      // fallback has no off-diagonal Hinv, so the reference's update is a no-op there.
+      if (HinvT) {
+        GemmArgs g = {(int)rows, (int)(cols - i2), cnt, E, QB, HinvT + i2 * cols + i1, cols, W + i2, cols, 1, 0, 0,
+                      status};
+        if (launch_gemm(false, true, g, st)) return LLMC_ECUDA;
+      } else {
+        GemmArgs g = {(int)rows, (int)(cols - i2), cnt, E, QB, Hinv + i1 * cols + i2, cols, W + i2, cols, 1, 0, 0,
+                      status};
+        if (launch_gemm(false, false, g, st)) return LLMC_ECUDA;
+      }
     }
   }
   k_finish<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows * cols); llmc::note_launch();

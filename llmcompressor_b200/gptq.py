@@ -24,6 +24,7 @@ _lib.extend_signatures(
     {
         "llmc_hessian_accumulate": [_P, _I64, _I64, _I64, _P, _F32, _P, _F32, _P, _P],
         "llmc_hessian_tiles": [_I64],
+        "llmc_gemm_f32_nt": [_I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _I32, _P],
     }
 )
 
@@ -98,10 +99,10 @@ _lib.extend_signatures(
     {
         "llmc_gptq_prepare_hessian": [_P, _I64, _F32, _P, _P],
         "llmc_gptq_hinv_workspace_size": [_I64, _I64P],
-        "llmc_gptq_hinv": [_P, _I64, _P, _P, _P, _P],
+        "llmc_gptq_hinv": [_P, _I64, _P, _P, _P, _P, _P],
         "llmc_gptq_quantize_workspace_size": [_I64, _I64, _I64P],
-        "llmc_gptq_quantize": [_P, _I64, _I64, _P, _P, ctypes.POINTER(_lib.QuantArgs), _P, _P, _I64, _P, _P, _P, _P,
-                               _P],
+        "llmc_gptq_quantize": [_P, _I64, _I64, _P, _P, _P, ctypes.POINTER(_lib.QuantArgs), _P, _P, _I64, _P, _P, _P,
+                               _P, _P],
     }
 )
 
@@ -117,8 +118,9 @@ class InverseHessian:
     consumes the same Hessian (q/k/v, gate/up).  ``status`` stays on the
     device; ``ok()`` reads it (one host sync)."""
 
-    def __init__(self, hinv: torch.Tensor, dead: torch.Tensor, status: torch.Tensor):
-        self.hinv, self.dead, self.status = hinv, dead, status
+    def __init__(self, hinv: torch.Tensor, dead: torch.Tensor, status: torch.Tensor,
+                 hinv_t: torch.Tensor | None = None):
+        self.hinv, self.dead, self.status, self.hinv_t = hinv, dead, status, hinv_t
 
     def ok(self) -> bool:
         return int(self.status.item()) != _lib.ENOT_PD
@@ -139,8 +141,9 @@ def inverse_hessian(H: torch.Tensor, percdamp: float = 0.01) -> InverseHessian:
     check(lib().llmc_gptq_prepare_hessian(ptr(H), d, float(percdamp), ptr(dead), st), "gptq_prepare_hessian")
     ws = torch.empty(_ws_bytes(lib().llmc_gptq_hinv_workspace_size, d), dtype=torch.uint8, device=dev)
     hinv = torch.empty(d, d, dtype=torch.float32, device=dev)
-    check(lib().llmc_gptq_hinv(ptr(H), d, ptr(hinv), ptr(ws), ptr(status), st), "gptq_hinv")
-    return InverseHessian(hinv, dead, status)
+    hinv_t = torch.empty(d, d, dtype=torch.float32, device=dev)
+    check(lib().llmc_gptq_hinv(ptr(H), d, ptr(hinv), ptr(hinv_t), ptr(ws), ptr(status), st), "gptq_hinv")
+    return InverseHessian(hinv, dead, status, hinv_t)
 
 
 def _strategy(args) -> str:
@@ -189,7 +192,8 @@ def quantize_with_inverse(weight: torch.Tensor, quant_args, hinv: InverseHessian
     ws = torch.empty(_ws_bytes(lib().llmc_gptq_quantize_workspace_size, rows, cols), dtype=torch.uint8, device=dev)
     out = torch.empty_like(w)
     loss = torch.empty(1, dtype=torch.float32, device=dev)
-    check(lib().llmc_gptq_quantize(ptr(w), rows, cols, ptr(hinv.hinv), ptr(hinv.dead), ctypes.byref(qa),
+    check(lib().llmc_gptq_quantize(ptr(w), rows, cols, ptr(hinv.hinv), ptr(hinv.hinv_t), ptr(hinv.dead),
+                                   ctypes.byref(qa),
                                    ptr(scale_bf16), ptr(zp), int(blocksize), ptr(out), ptr(loss), ptr(ws),
                                    ptr(hinv.status), stream_ptr(dev)), "gptq_quantize")
     return out, loss

@@ -14,8 +14,8 @@ from ._lib import check, lib, ptr, stream_ptr
 
 _P, _I64 = ctypes.c_void_p, ctypes.c_int64
 _lib.extend_signatures(
-    {"llmc_gptq_quantize_noalloc": [_P, _I64, _I64, _P, _P, ctypes.POINTER(_lib.QuantArgs), _P, _P, _I64, _P, _P, _P,
-                                    _P]}
+    {"llmc_gptq_quantize_noalloc": [_P, _I64, _I64, _P, _P, _P, ctypes.POINTER(_lib.QuantArgs), _P, _P, _I64, _P, _P,
+                                    _P, _P]}
 )
 
 SCRATCH_BYTES = 32 << 20
@@ -29,7 +29,8 @@ def quantize_with_inverse_noalloc(weight: torch.Tensor, quant_args, hinv, scale:
     rows, cols = weight.shape
     qa = _lib.qargs_struct(quant_args)
     zp = None if quant_args.symmetric else zero_point
-    check(lib().llmc_gptq_quantize_noalloc(ptr(weight), rows, cols, ptr(hinv.hinv), ptr(hinv.dead), ctypes.byref(qa),
+    check(lib().llmc_gptq_quantize_noalloc(ptr(weight), rows, cols, ptr(hinv.hinv), ptr(hinv.hinv_t), ptr(hinv.dead),
+                                           ctypes.byref(qa),
                                            ptr(scale), ptr(zp), int(blocksize), ptr(out), ptr(loss),
                                            ptr(hinv.status), stream_ptr(weight.device)),
           "gptq_quantize_noalloc")

@@ -44,7 +44,8 @@ def _call_noalloc(w, inv, scale, out, loss):
     qa = _lib.qargs_struct(ARGS)
     rows, cols = w.shape
     return _lib.lib().llmc_gptq_quantize_noalloc(
-        w.data_ptr(), rows, cols, inv.hinv.data_ptr(), inv.dead.data_ptr(), ctypes.byref(qa), scale.data_ptr(),
+        w.data_ptr(), rows, cols, inv.hinv.data_ptr(), inv.hinv_t.data_ptr(), inv.dead.data_ptr(), ctypes.byref(qa),
+        scale.data_ptr(),
         None, 128, out.data_ptr(), loss.data_ptr(), inv.status.data_ptr(), torch.cuda.current_stream().cuda_stream)
 
 
@@ -69,6 +70,6 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
 
 def test_noalloc_rejects_weights_beyond_the_fixed_scratch():
     qa = _lib.qargs_struct(ARGS)
-    st = _lib.lib().llmc_gptq_quantize_noalloc(None, 4096, 4096, None, None, ctypes.byref(qa), None, None, 128, None,
-                                               None, None, torch.cuda.current_stream().cuda_stream)
+    st = _lib.lib().llmc_gptq_quantize_noalloc(None, 4096, 4096, None, None, None, ctypes.byref(qa), None, None, 128,
+                                               None, None, None, torch.cuda.current_stream().cuda_stream)
     assert st == _lib.EINVAL_SHAPE
