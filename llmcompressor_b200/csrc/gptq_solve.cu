@@ -269,50 +269,108 @@ __global__ void k_xt_to_ut(const float* __restrict__ Xt, float* __restrict__ Ut,
 constexpr int PB = 128;
 constexpr int PLD = PB + 1;  // padded row stride of the shared-memory blocks
 // 16 warps: warp w walks rows (w, w+16, ...), its lanes walk the columns of a row.
-__global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_t k0, int kb, float* Linv,
+__global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_t k0, int n, float* Linv,
                                                     int* status) {
+  // Blocked in 32-column sub-steps: warp 0 factors and inverts each 32x32
+  // diagonal sub-block (warp-synchronous), then all 16 warps apply the panel
+  // solve and the trailing update; the off-diagonal blocks of the inverse
+  // follow block-row by block-row.
   extern __shared__ float sm[];
-  float* S = sm;             // [PB][PLD]  L of this block
-  float* X = sm + PB * PLD;  // [PB][PLD]  its inverse
+  float* S = sm;             // [PB][PLD]  L of this block (lower)
+  float* X = sm + PB * PLD;  // [PB][PLD]  its inverse (lower)
   __shared__ int bad;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  constexpr int NW = 16;
+  constexpr int NW = 16, NT = 512, SB = 32;
   if (t == 0) bad = 0;
-  for (int i = warp; i < kb; i += NW)
-    for (int j = lane; j < kb; j += 32) {
-      S[i * PLD + j] = (j <= i) ? B[(k0 + i) * ld + k0 + j] : 0.f;
-      X[i * PLD + j] = (i == j) ? 1.0f : 0.f;
+  for (int i = warp; i < PB; i += NW)
+    for (int j = lane; j < PB; j += 32) {
+      S[i * PLD + j] = (i < n && j <= i) ? B[(k0 + i) * ld + k0 + j] : 0.f;
+      X[i * PLD + j] = 0.f;
     }
   __syncthreads();
-  // right-looking Cholesky, two barriers per column
-  for (int j = 0; j < kb; ++j) {
-    float p = S[j * PLD + j];
-    if (!(p > 0.0f)) { if (t == 0) bad = 1; p = 1.0f; }
-    const float piv = sqrtf(p);
-    const int i = j + 1 + t;
-    if (i < kb) S[i * PLD + j] = __fdiv_rn(S[i * PLD + j], piv);
-    __syncthreads();
-    if (t == 0) S[j * PLD + j] = piv;
-    for (int r = j + 1 + warp; r < kb; r += NW) {
-      const float srj = S[r * PLD + j];
-      for (int l = j + 1 + lane; l <= r; l += 32) S[r * PLD + l] -= srj * S[l * PLD + j];
+  const int nsub = (n + SB - 1) / SB;
+  for (int kb = 0; kb < nsub; ++kb) {
+    const int o = kb * SB, sz = min(SB, n - o);
+    if (warp == 0) {
+      // (1) unblocked Cholesky of the diagonal sub-block; lane i owns row o+i
+      for (int j = 0; j < sz; ++j) {
+        float p = S[(o + j) * PLD + o + j];
+        if (!(p > 0.0f)) { if (lane == 0) bad = 1; p = 1.0f; }
+        const float piv = sqrtf(p);
+        if (lane > j && lane < sz) S[(o + lane) * PLD + o + j] = __fdiv_rn(S[(o + lane) * PLD + o + j], piv);
+        __syncwarp();
+        if (lane == 0) S[(o + j) * PLD + o + j] = piv;
+        if (lane > j && lane < sz) {
+          const float sij = S[(o + lane) * PLD + o + j];
+          for (int l = j + 1; l <= lane; ++l) S[(o + lane) * PLD + o + l] -= sij * S[(o + l) * PLD + o + j];
+        }
+        __syncwarp();
+      }
+      // (2) its inverse by forward substitution; lane c owns column o+c
+      if (lane < sz) {
+        for (int j = lane; j < sz; ++j) {
+          float s = (j == lane) ? 1.0f : 0.0f;
+          for (int l = lane; l < j; ++l) s -= S[(o + j) * PLD + o + l] * X[(o + l) * PLD + o + lane];
+          X[(o + j) * PLD + o + lane] = __fdiv_rn(s, S[(o + j) * PLD + o + j]);
+        }
+      }
     }
+    __syncthreads();
+    const int r0 = o + sz, rem = n - r0;
+    if (rem <= 0) break;
+    // (3) panel: L21 = A21 * X11^T   (X11 lower: only l <= c)
+    float v[8];
+    int cnt = 0;
+    for (int e = t; e < rem * sz; e += NT, ++cnt) {
+      const int r = r0 + e / sz, c = e % sz;
+      float s = 0.f;
+      for (int l = 0; l <= c; ++l) s = fmaf(S[r * PLD + o + l], X[(o + c) * PLD + o + l], s);
+      v[cnt] = s;
+    }
+    __syncthreads();
+    cnt = 0;
+    for (int e = t; e < rem * sz; e += NT, ++cnt) S[(r0 + e / sz) * PLD + o + e % sz] = v[cnt];
+    __syncthreads();
+    // (4) trailing update of the lower triangle: A22 -= L21 L21^T
+    for (int r = r0 + warp; r < n; r += NW)
+      for (int l = r0 + lane; l <= r; l += 32) {
+        float s = 0.f;
+        for (int c = 0; c < sz; ++c) s = fmaf(S[r * PLD + o + c], S[l * PLD + o + c], s);
+        S[r * PLD + l] -= s;
+      }
     __syncthreads();
   }
   if (t == 0 && bad && status) atomicExch(status, LLMC_ENOT_PD);
-  // inverse by right-looking forward substitution on X = I, two barriers per row
-  for (int l = 0; l < kb; ++l) {
-    if (t <= l) X[l * PLD + t] = __fdiv_rn(X[l * PLD + t], S[l * PLD + l]);
-    __syncthreads();
-    for (int r = l + 1 + warp; r < kb; r += NW) {
-      const float srl = S[r * PLD + l];
-      for (int c = lane; c <= l; c += 32) X[r * PLD + c] -= srl * X[l * PLD + c];
+  // off-diagonal blocks of the inverse: X_ij = -X_ii * sum_{k=j}^{i-1} L_ik X_kj, by block row
+  for (int bi = 1; bi < nsub; ++bi) {
+    const int oi = bi * SB, szi = min(SB, n - oi);
+    float v[8];
+    int cnt = 0;
+    for (int e = t; e < szi * oi; e += NT, ++cnt) {  // T = L[rows of bi, :oi] * X[:oi, :oi]
+      const int r = oi + e / oi, c = e % oi;
+      float s = 0.f;
+      for (int k = c; k < oi; ++k) s = fmaf(S[r * PLD + k], X[k * PLD + c], s);
+      v[cnt] = s;
     }
+    __syncthreads();
+    cnt = 0;
+    for (int e = t; e < szi * oi; e += NT, ++cnt) X[(oi + e / oi) * PLD + e % oi] = v[cnt];
+    __syncthreads();
+    cnt = 0;
+    for (int e = t; e < szi * oi; e += NT, ++cnt) {  // X[rows of bi, :oi] = -X_ii * T
+      const int r = oi + e / oi, c = e % oi;
+      float s = 0.f;
+      for (int m = oi; m <= r; ++m) s = fmaf(X[r * PLD + m], X[m * PLD + c], s);
+      v[cnt] = -s;
+    }
+    __syncthreads();
+    cnt = 0;
+    for (int e = t; e < szi * oi; e += NT, ++cnt) X[(oi + e / oi) * PLD + e % oi] = v[cnt];
     __syncthreads();
   }
   for (int i = warp; i < PB; i += NW)
     for (int j = lane; j < PB; j += 32) {
-      const bool in = i < kb && j < kb && j <= i;
+      const bool in = i < n && j < n && j <= i;
       Linv[i * PB + j] = in ? X[i * PLD + j] : 0.f;
       if (in) B[(k0 + i) * ld + k0 + j] = S[i * PLD + j];
     }

@@ -36,7 +36,10 @@ constexpr int TILE_BYTES = 128 * BK * 4;          // 16 KB per operand tile
 constexpr int BOX_MN_BYTES = 32 * BK * 4;         // 4 KB: one 32-element MN chunk x 32 K rows
 constexpr int STAGE_BYTES = 4 * TILE_BYTES;       // A_hi, B_hi, A_lo, B_lo
 constexpr int SMEM_STAGES = STAGES * STAGE_BYTES;  // 192 KB
-constexpr int SMEM_TOTAL = SMEM_STAGES + 256 + 1024;
+constexpr int EPI_BOX_BYTES = 32 * 32 * 4;           // 4 KB float32 box
+constexpr int EPI_WARP_BYTES = 2 * EPI_BOX_BYTES;     // double-buffered per epilogue warp
+constexpr int SMEM_EPI = 4 * EPI_WARP_BYTES;          // 32 KB
+constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_EPI + 256 + 1024;
 constexpr int THREADS = 320;
 constexpr int XF_WARP0 = 6, NXF = 4;  // split warps 6..9 (epilogue warps are 2..5)
 constexpr uint32_t TMEM_COLS = 256;
@@ -65,12 +68,12 @@ __device__ __forceinline__ void tile_of(const Params& p, int t, int& bm, int& bn
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
-k_gemm_tc32(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, Params p,
-            const int* skip) {
+k_gemm_tc32(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
+            const __grid_constant__ CUtensorMap cmap, Params p, const int* skip) {
   if (skip && *skip) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = (uint64_t*)(smem + SMEM_STAGES);
+  uint64_t* bars = (uint64_t*)(smem + SMEM_STAGES + SMEM_EPI);
   uint64_t* full = bars;                // TMA landed            [STAGES]
   uint64_t* split = bars + STAGES;      // hi/lo written         [STAGES]
   uint64_t* empty = bars + 2 * STAGES;  // MMAs done reading     [STAGES]
@@ -97,6 +100,7 @@ k_gemm_tc32(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
     fence_mbar_init();
     prefetch_tmap(&amap);
     prefetch_tmap(&bmap);
+    prefetch_tmap(&cmap);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
@@ -215,7 +219,7 @@ k_gemm_tc32(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    int acc = 0;
+    int acc = 0, ebuf = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
       int bm, bn;
@@ -223,48 +227,43 @@ k_gemm_tc32(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
       const int m0 = bm * BM, n0 = bn * BN;
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag)) break;
       tc_fence_after();
-      const int gm = m0 + 32 * q + lane;
-      float* crow = p.C + (int64_t)gm * p.ldc;
-      const bool vec = ((p.ldc & 3) == 0) && ((((uintptr_t)p.C) & 15) == 0);
+      // 32x32 boxes of the tile go through swizzled shared memory to a TMA
+      // store (C = +-AB) or a TMA reduce-add of -AB (C -= AB, the read-modify-
+      // write happens in L2).  Out-of-range rows/columns are clipped by TMA.
+      const int gr = m0 + 32 * q;
+      const float sgn = (p.mode == 0) ? 1.0f : -1.0f;
+      uint8_t* wbuf = smem + SMEM_STAGES + (warp - 2) * EPI_WARP_BYTES;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * c), r);
         tmem_ld_wait();
-        const int gn0 = n0 + 32 * c;
-        if (gm >= p.m || gn0 >= p.n) continue;
-        if (vec && gn0 + 32 <= p.n) {
+        const int gc = n0 + 32 * c;
+        if (gr >= p.m || gc >= p.n) continue;
+        uint8_t* box = wbuf + ebuf * EPI_BOX_BYTES;
+        if (lane == 0) bulk_wait_read<1>();  // the copy that last read this buffer is done with it
+        __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4* ptr = (float4*)(crow + gn0 + 4 * j);
-            float4 a = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-            float4 o;
-            if (p.mode == 1) {
-              const float4 cv = *ptr;
-              o = make_float4(cv.x - a.x, cv.y - a.y, cv.z - a.z, cv.w - a.w);
-            } else if (p.mode == 2) {
-              o = make_float4(-a.x, -a.y, -a.z, -a.w);
-            } else {
-              o = a;
-            }
-            *ptr = o;
-          }
-        } else {
-          for (int j = 0; j < 32; ++j) {
-            const int gn = gn0 + j;
-            if (gn >= p.n) break;
-            const float a = __uint_as_float(r[j]);
-            float* ptr = crow + gn;
-            *ptr = (p.mode == 1) ? (*ptr - a) : (p.mode == 2 ? -a : a);
-          }
+        for (int j = 0; j < 8; ++j) {
+          float4 v = make_float4(sgn * __uint_as_float(r[4 * j]), sgn * __uint_as_float(r[4 * j + 1]),
+                                 sgn * __uint_as_float(r[4 * j + 2]), sgn * __uint_as_float(r[4 * j + 3]));
+          *(float4*)(box + lane * 128 + ((j ^ (lane & 7)) << 4)) = v;
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (p.mode == 1) tma_reduce_add_2d(&cmap, smem_u32(box), gc, gr);
+          else tma_store_2d(&cmap, smem_u32(box), gc, gr);
+          bulk_commit();
+        }
+        ebuf ^= 1;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    if (lane == 0) bulk_wait<0>();
   }
 
   tc_fence_before();
@@ -317,7 +316,10 @@ int gemm(const Gemm& g, cudaStream_t st) {
                            : map2d(&am, g.A, (uint64_t)g.k, (uint64_t)g.m, g.lda, 32, 128);
   const bool ok_b = g.b_mn ? map2d(&bm, g.B, (uint64_t)g.n, (uint64_t)g.k, g.ldb, 32, 32)
                            : map2d(&bm, g.B, (uint64_t)g.k, (uint64_t)g.n, g.ldb, 32, 128);
-  if (!ok_a || !ok_b) return LLMC_ENOSUPPORT;
+  CUtensorMap cm;
+  if ((((uintptr_t)g.C) & 15) || (g.ldc & 3)) return LLMC_ENOSUPPORT;
+  const bool ok_c = map2d(&cm, g.C, (uint64_t)g.n, (uint64_t)g.m, g.ldc, 32, 32);
+  if (!ok_a || !ok_b || !ok_c) return LLMC_ENOSUPPORT;
   Params p;
   p.m = g.m; p.n = g.n; p.k = g.k;
   p.tiles_m = (g.m + BM - 1) / BM;
@@ -345,7 +347,7 @@ int gemm(const Gemm& g, cudaStream_t st) {
     if (sms <= 0) sms = 148;
   }
   const int grid = std::min(p.num_tiles, sms);
-  k_gemm_tc32<<<grid, THREADS, SMEM_TOTAL, st>>>(am, bm, p, g.skip); llmc::note_launch();
+  k_gemm_tc32<<<grid, THREADS, SMEM_TOTAL, st>>>(am, bm, cm, p, g.skip); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
