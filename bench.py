@@ -158,7 +158,6 @@ def run_ours(args, rank, world, device):
     pk = peaks()
 
     h_events: list = []
-    pack_events: list = []
 
     def step(layer_idx, record):
         hess.reset()
@@ -172,8 +171,7 @@ def run_ours(args, rank, world, device):
             e1 = torch.cuda.Event(enable_timing=True)
             e1.record()
             h_events.append((e0, e1))
-        return solve_layer(weights[layer_idx % L], specs, hess, qa, gather_to=0,
-                           pack_events=pack_events if record else None)
+        return solve_layer(weights[layer_idx % L], specs, hess, qa, gather_to=0)
 
     def barrier():
         if world > 1:
@@ -209,10 +207,7 @@ def run_ours(args, rank, world, device):
     h_ms = sum(a.elapsed_time(b) for a, b in h_events)
     h_flops = hessian_flops(dims, len(my_chunks) * CHUNK) * args.steps
     h_tflops = h_flops / (h_ms * 1e-3) / 1e12
-    c_ms = sum(a.elapsed_time(b) for a, b, _ in pack_events)
-    c_elems = sum(n for _, _, n in pack_events)
-    c_bytes = c_elems * (2 + 0.5 + 2.0 / 128)
-    c_gbs = c_bytes / (c_ms * 1e-3) / 1e9 if c_ms > 0 else None
+    casts = measure_casts([weights[i] for i in range(min(L, 4))]) if rank == 0 else None
 
     out = {
         "ms": ms,
@@ -222,7 +217,7 @@ def run_ours(args, rank, world, device):
         "hessian_tflops": h_tflops,
         "hessian_ms_per_step": h_ms / args.steps,
         "hessian_flops_per_launch": hessian_flops({"x": CFG["hidden"]}, CHUNK),
-        "cast_gbs": c_gbs,
+        "casts": casts,
         "peaks": pk,
     }
 
@@ -230,6 +225,42 @@ def run_ours(args, rank, world, device):
     if args.e2e:
         out["e2e"] = run_e2e(args, rank, world, device, specs, dims, qa, my_chunks, alpha)
     return out
+
+
+CAST_SCHEMES = ("W4A16", "NVFP4A16", "MXFP4A16", "FP8_BLOCK", "FP8_DYNAMIC")
+
+
+def measure_casts(layers, reps: int = 3) -> dict:
+    """Model-free single-pass casts (observe + qparams + quantize + pack) over
+    the Linear weights of a few layers (436 MB of bf16 per layer, so every
+    launch streams from HBM), one format at a time, timed with CUDA events.
+    Bytes per launch = bf16 weight read + codes and scales written."""
+    from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
+
+    from llmcompressor_b200 import ops
+
+    res = {}
+    for name in CAST_SCHEMES:
+        qa = preset_name_to_scheme(name, ["Linear"]).weights
+        ws = [w for layer in layers for w in layer.values()]
+        gss = [ops.fused_global_scale([w]) if name == "NVFP4A16" else None for w in ws]
+        out_bytes = 0
+        for w, gs in zip(ws, gss):
+            o = ops.modelfree_quantize(w, qa, gs)
+            out_bytes += sum(t.numel() * t.element_size() for k, t in o.items() if t.is_cuda and k != "weight_global_scale")
+        in_bytes = sum(w.numel() * 2 for w in ws)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for w, gs in zip(ws, gss):
+                ops.modelfree_quantize(w, qa, gs)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[name] = {"gbs": (in_bytes + out_bytes) / (ms * 1e-3) / 1e9, "ms": ms, "bytes": in_bytes + out_bytes,
+                     "launches_per_pass": len(ws)}
+    return res
 
 
 def run_e2e(args, rank, world, device, specs, dims, qa, my_chunks, alpha):
@@ -393,7 +424,7 @@ def cpu_sample(steps: int, warmup: int) -> dict:
 def run_micro(args) -> None:
     """One kernel on a small case (profiling captures and per-kernel timing):
     hessian: H += alpha X^T X, X (tokens x d); gptq: factor + block loop of
-    one (rows x d) weight; cast: W4A16 model-free pass over a (rows x d) weight."""
+    one (rows x d) weight; cast: model-free pass of --scheme over a (rows x d) weight."""
     from llmcompressor_b200 import gptq, ops
 
     dev = torch.device("cuda:0")
@@ -422,9 +453,16 @@ def run_micro(args) -> None:
 
         work, unit = None, "ms"
     else:
+        from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
+
+        qa = preset_name_to_scheme(args.scheme, ["Linear"]).weights
         w = (0.02 * torch.randn(rows, d, device=dev, generator=g)).to(torch.bfloat16)
-        fn = lambda: ops.modelfree_quantize(w, qa)  # noqa: E731
-        work, unit = rows * d * (2 + 0.5 + 2 / 128) / 1e9, "GB/s"
+        gs = ops.fused_global_scale([w]) if args.scheme == "NVFP4A16" else None
+        o = ops.modelfree_quantize(w, qa, gs)
+        nbytes = w.numel() * 2 + sum(t.numel() * t.element_size() for k, t in o.items()
+                                     if t.is_cuda and k != "weight_global_scale")
+        fn = lambda: ops.modelfree_quantize(w, qa, gs)  # noqa: E731
+        work, unit = nbytes / 1e9, "GB/s"
     for _ in range(args.warmup):
         fn()
     torch.cuda.synchronize()
@@ -447,6 +485,7 @@ def main():
     ap.add_argument("--d", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--rows", type=int, default=4096)
+    ap.add_argument("--scheme", default="W4A16", choices=list(CAST_SCHEMES), help="format of --micro cast")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=3)
@@ -528,8 +567,8 @@ def main():
             "algorithmic": "N*d*(d+1) flop per launch (lower triangle incl. diagonal), N=16384 tokens",
         },
         "hessian_tflops": res["hessian_tflops"],
-        "cast_gbs": res["cast_gbs"],
-        "cast_frac_hbm": (res["cast_gbs"] / pk["hbm_gbs"]) if res["cast_gbs"] else None,
+        "casts": ({k: {"gbs": v["gbs"], "frac": v["gbs"] / pk["hbm_gbs"]} for k, v in res["casts"].items()}
+                  if res["casts"] else None),
         "gpu_launches": res["launches"],
         "clocks": res["clocks"],
     }

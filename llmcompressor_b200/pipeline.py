@@ -89,6 +89,17 @@ class LayerHessians:
         gptq.hessian_update_(self.H[key], x2d, alpha)
 
 
+_STREAMS: dict[int, list[torch.cuda.Stream]] = {}
+
+
+def _side_streams(dev: torch.device, n: int) -> list[torch.cuda.Stream]:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    pool = _STREAMS.setdefault(idx, [])
+    while len(pool) < n:
+        pool.append(torch.cuda.Stream(device=dev))
+    return pool[:n]
+
+
 def solve_layer(
     weights: dict[str, torch.Tensor],
     specs: list[LinearSpec],
@@ -101,7 +112,12 @@ def solve_layer(
 ) -> dict[str, LayerResult]:
     """GPTQ-quantize and pack every module of one layer from its (averaged)
     Hessians.  On several ranks each rank returns its row slice; with
-    ``gather_to`` set, that rank also receives the full packed tensors."""
+    ``gather_to`` set, that rank also receives the full packed tensors.
+
+    The independent pieces run concurrently on side streams: the
+    factorisations of the distinct Hessians, and each module's block loop as
+    soon as its factor is ready.  The caller's stream waits for all of them
+    before this function returns, so results are ordered on it as usual."""
     rank, ws = world()
     dims = hessians.dims
     rows_of: dict[str, int] = {}
@@ -110,45 +126,85 @@ def solve_layer(
     owners = greedy_owners({k: solve_cost(d, rows_of[k]) for k, d in dims.items()}, ws)
     reduce_to_owners(hessians.H, owners)
     dev = next(iter(hessians.H.values())).device
+    main = torch.cuda.current_stream(dev)
+    streams = _side_streams(dev, max(len(dims), len(specs)))
+
+    # factorisations, largest first, one side stream each
     inv: dict[str, gptq.InverseHessian] = {}
-    for key, d in dims.items():
-        if owners[key] == rank:
-            inv[key] = gptq.inverse_hessian(hessians.H[key], percdamp)
-        else:
-            inv[key] = gptq.InverseHessian(
-                torch.empty(d, d, dtype=torch.float32, device=dev),
-                torch.empty(d, dtype=torch.uint8, device=dev),
-                torch.empty(1, dtype=torch.int32, device=dev),
-            )
-    broadcast_inverse({k: [v.hinv, v.dead, v.status] for k, v in inv.items()}, owners)
+    ready: dict[str, torch.cuda.Event] = {}
+    for i, key in enumerate(sorted(dims, key=lambda k: (-dims[k], k))):
+        d = dims[key]
+        st = streams[i]
+        st.wait_stream(main)
+        with torch.cuda.stream(st):
+            if owners[key] == rank:
+                inv[key] = gptq.inverse_hessian(hessians.H[key], percdamp)
+            else:
+                inv[key] = gptq.InverseHessian(
+                    torch.empty(d, d, dtype=torch.float32, device=dev),
+                    torch.empty(d, dtype=torch.uint8, device=dev),
+                    torch.empty(1, dtype=torch.int32, device=dev),
+                    torch.empty(d, d, dtype=torch.float32, device=dev),
+                )
+            ev = torch.cuda.Event()
+            ev.record(st)
+            ready[key] = ev
+    if ws > 1:
+        for ev in ready.values():
+            main.wait_event(ev)
+        broadcast_inverse({k: [v.hinv, v.dead, v.status, v.hinv_t] for k, v in inv.items()}, owners)
+        bcast = torch.cuda.Event()
+        bcast.record(main)
+        ready = {k: bcast for k in ready}
+
+    # block loops + int4 pack, one side stream per module
+    parts: dict[str, tuple] = {}
+    done = []
+    for j, s in enumerate(specs):
+        st = streams[j % len(streams)]
+        st.wait_event(ready[s.input_key])
+        r0, r1 = row_range(s.out_features, rank, ws)
+        with torch.cuda.stream(st):
+            if r1 > r0:
+                wl = weights[s.name][r0:r1]
+                mn, mx = ops.observe_minmax(wl, quant_args)
+                scale, zp = ops.calculate_qparams(mn, mx, quant_args)
+                wq, loss = gptq.quantize_with_inverse(wl, quant_args, inv[s.input_key], scale, zp, blocksize)
+                if pack_events is not None:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                packed = ops.quantize_pack(wq, quant_args, scale, None if quant_args.symmetric else zp,
+                                           fmt=_lib.FMT_PACK_INT32)
+                if pack_events is not None:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record(st)
+                    pack_events.append((e0, e1, wq.numel()))
+            else:
+                pf = 32 // quant_args.num_bits
+                packed = torch.empty(0, -(-s.in_features // pf), dtype=torch.int32, device=dev)
+                scale = torch.empty(0, ops.stats_shape(1, s.in_features, quant_args)[-1], dtype=torch.bfloat16,
+                                    device=dev)
+                loss = torch.zeros(1, dtype=torch.float32, device=dev)
+            ev = torch.cuda.Event()
+            ev.record(st)
+            done.append(ev)
+        for t in (packed, scale, loss):
+            t.record_stream(main)
+        parts[s.name] = (packed, scale, loss, (r0, r1))
+    for ev in done:
+        main.wait_event(ev)
+    for v in inv.values():
+        for t in (v.hinv, v.dead, v.status, v.hinv_t):
+            if t is not None:
+                t.record_stream(main)
 
     out: dict[str, LayerResult] = {}
     for s in specs:
-        w = weights[s.name]
-        r0, r1 = row_range(s.out_features, rank, ws)
-        wl = w[r0:r1]
-        if r1 > r0:
-            mn, mx = ops.observe_minmax(wl, quant_args)
-            scale, zp = ops.calculate_qparams(mn, mx, quant_args)
-            wq, loss = gptq.quantize_with_inverse(wl, quant_args, inv[s.input_key], scale, zp, blocksize)
-            if pack_events is not None:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e0.record()
-            packed = ops.quantize_pack(wq, quant_args, scale, None if quant_args.symmetric else zp,
-                                       fmt=_lib.FMT_PACK_INT32)
-            if pack_events is not None:
-                e1 = torch.cuda.Event(enable_timing=True)
-                e1.record()
-                pack_events.append((e0, e1, wq.numel()))
-        else:
-            pf = 32 // quant_args.num_bits
-            packed = torch.empty(0, -(-s.in_features // pf), dtype=torch.int32, device=dev)
-            scale = torch.empty(0, ops.stats_shape(1, s.in_features, quant_args)[-1], dtype=torch.bfloat16, device=dev)
-            loss = torch.zeros(1, dtype=torch.float32, device=dev)
+        packed, scale, loss, rr = parts[s.name]
         if ws > 1 and gather_to is not None:
             fp = gather_rows(packed, s.out_features, dst=gather_to)
             fs = gather_rows(scale, s.out_features, dst=gather_to)
             if rank == gather_to:
                 packed, scale = fp, fs
-        out[s.name] = LayerResult(packed, scale, loss, (r0, r1), (s.out_features, s.in_features))
+        out[s.name] = LayerResult(packed, scale, loss, rr, (s.out_features, s.in_features))
     return out
