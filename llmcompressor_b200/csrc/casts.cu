@@ -373,6 +373,486 @@ __global__ void __launch_bounds__(256) k_paramgroup(CastParams p) {
 }
 
 // ------------------------------------------------------------------------
+// Streaming kernels on packed pairs (sm_100a f32x2 / bf16x2 / e4m3x2 /
+// e2m1x2 instructions).  Same results as quant_code, fewer instructions:
+//
+//  * quotient of two bf16 values at once by Markstein's correction:
+//    q0 = x * r (r = RN(1/s)), e = x - q0 * s (exact by fma), q = q0 + e * r
+//    (evaluated on -x so that zeros keep their sign, see quot2).
+//    With r the correctly rounded reciprocal and q0 within an ulp of x / s,
+//    q is the correctly rounded float32 quotient (Markstein 1990; Muller et
+//    al., Handbook of Floating-Point Arithmetic, division with fma) when
+//    nothing overflows or underflows.  For a bf16 x and a scale with at most
+//    8 significant bits, x / s is either exactly a bf16 rounding midpoint or
+//    at least 2^-17 (relative) away from one, so RN_bf16(q) equals torch's
+//    RN_bf16(RN_f32(x / s)) in both cases.  Groups whose reciprocal is not a
+//    normal float divide exactly; with stored (caller-given) scales a pair
+//    whose quotient is not finite is recomputed by exact division.
+//  * int4: RN_bf16(q + 136) of a clamped code c in [-8, 7] is the bf16
+//    number 128 + (c + 8), whose low byte is c + 8: byte permutes pack it.
+//  * E2M1: the hardware RNE conversion of a value in [-6, 6] picks the same
+//    code as compressed-tensors' thresholds (ties 0.25, 1.25, 2.5, 5 go to
+//    the even code below, 0.75, 1.75, 3.5 to the even code above); the
+//    reference's "+ zero_point" turns -0.0 into +0.0 first.
+// ------------------------------------------------------------------------
+__device__ __forceinline__ void pair_f2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_pair(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+// float32 quotients of the two bf16 values of w (low half = first element).
+// Written on nx = -x: q0 = nx * (-r), e = q0 * s + nx (= q0 s - x, exact),
+// q = q0 + e * (-r).  For x = +-0 every step keeps the zero's sign (the
+// form x - q0 s would turn -0 into +0); needs s > 0.
+__device__ __forceinline__ uint64_t quot2(uint32_t w, uint64_t nr2, uint64_t s2) {
+  uint64_t q;
+  asm("{\n\t.reg .b32 lo, hi, t;\n\t.reg .b64 nx, q0, e;\n\t"
+      "xor.b32 t, %1, 0x8000;\n\tshl.b32 lo, t, 16;\n\tlop3.b32 hi, %1, 0xFFFF0000, 0x80000000, 0x6A;\n\t"
+      "mov.b64 nx, {lo, hi};\n\t"
+      "mul.rn.f32x2 q0, nx, %2;\n\tfma.rn.f32x2 e, q0, %3, nx;\n\tfma.rn.f32x2 %0, e, %2, q0;\n\t}"
+      : "=l"(q) : "r"(w), "l"(nr2), "l"(s2));
+  return q;
+}
+__device__ __forceinline__ uint32_t bf2_of(uint64_t q) {
+  uint32_t d;
+  asm("{\n\t.reg .b32 lo, hi;\n\tmov.b64 {lo, hi}, %1;\n\tcvt.rn.bf16x2.f32 %0, hi, lo;\n\t}" : "=r"(d) : "l"(q));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmax2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmin2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t bf2_dup(float v) { uint32_t b = f_to_bf16(v); return b | (b << 16); }
+__device__ __forceinline__ bool finite_bf2(uint32_t q) {
+  return ((q & 0x7F80u) != 0x7F80u) && ((q & 0x7F800000u) != 0x7F800000u);
+}
+// e4m3 bytes of (lo, hi), lo in the low byte; saturating RNE
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t h;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(h) : "f"(hi), "f"(lo));
+  return h;
+}
+// E2M1 codes of v[0..7], element 2k in the low nibble of byte k
+__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
+  uint32_t d;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\tcvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\tcvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(d)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return d;
+}
+__device__ __forceinline__ void ld_v8(const void* p, uint32_t* w) {
+  asm volatile("ld.global.cs.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+               : "l"(p));
+}
+__device__ __forceinline__ void st_v8(void* p, const uint32_t* w) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+__device__ __forceinline__ void st_v4(void* p, const uint32_t* w) {
+  asm volatile("st.global.cs.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+               : "memory");
+}
+
+// Per-group divisor in the forms the pair routines take.
+struct GQ {
+  uint64_t nr2, s2;  // (-r, -r), (s, s)
+  float s, zp;
+  uint32_t zp2;      // zero point as bf16x2
+  bool fast, has_zp, f32q;
+};
+__device__ __forceinline__ GQ to_gq(const ElemQ& e) {
+  GQ g;
+  g.s = e.s; g.zp = e.zp; g.has_zp = e.has_zp; g.f32q = e.f32q;
+  g.fast = e.fast && e.s > 0.0f;  // the pair form keeps zero signs for positive scales only
+  g.nr2 = f2_pair(-e.r, -e.r);
+  g.s2 = f2_pair(e.s, e.s);
+  g.zp2 = e.has_zp ? bf2_dup(e.zp) : 0u;
+  return g;
+}
+
+template <int FMT, int BITS>
+struct OutOf {
+  static constexpr bool OUT4 = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4 || (FMT == LLMC_FMT_PACK_INT32 && BITS == 4));
+  static constexpr int WORDS_PER_8 = OUT4 ? 1 : 2;  // output words per 8 elements
+};
+
+// Codes of the 2*NW bf16 values in w (one parameter group) -> output words o
+// (NW/4 words for 4-bit outputs, NW/2 for 8-bit).  CHECK: scales come from
+// the caller, so a quotient may overflow.
+template <int FMT, int BITS, bool F32Q, bool CHECK, int NW>
+__device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, float qmin, float qmax, uint32_t* o) {
+  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+  if (!F32Q) {
+    uint32_t Q[NW];
+    if (g.fast) {
+#pragma unroll
+      for (int k = 0; k < NW; ++k) Q[k] = bf2_of(quot2(w[k], g.nr2, g.s2));
+      if (CHECK) {
+#pragma unroll
+        for (int k = 0; k < NW; ++k)
+          if (!finite_bf2(Q[k]))
+            Q[k] = (uint32_t)f_to_bf16(__fdiv_rn(bf_lo(w[k]), g.s)) |
+                   ((uint32_t)f_to_bf16(__fdiv_rn(bf_hi(w[k]), g.s)) << 16);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < NW; ++k)
+        Q[k] = (uint32_t)f_to_bf16(__fdiv_rn(bf_lo(w[k]), g.s)) |
+               ((uint32_t)f_to_bf16(__fdiv_rn(bf_hi(w[k]), g.s)) << 16);
+    }
+    const uint32_t QMIN2 = bf2_dup(qmin), QMAX2 = bf2_dup(qmax);
+    if (g.has_zp) {
+#pragma unroll
+      for (int k = 0; k < NW; ++k) Q[k] = hadd2(Q[k], g.zp2);  // rbf(q + zp)
+    }
+    if (FMT == LLMC_FMT_PACK_INT32 || FMT == LLMC_FMT_INT8) {
+#pragma unroll
+      for (int k = 0; k < NW; ++k) Q[k] = hmin2(hmax2(Q[k], QMIN2), QMAX2);
+      if (OUT4) {
+#pragma unroll
+        for (int j = 0; j < NW / 4; ++j) {
+          uint32_t v0 = hadd2(Q[4 * j], 0x43084308u), v1 = hadd2(Q[4 * j + 1], 0x43084308u);
+          uint32_t v2 = hadd2(Q[4 * j + 2], 0x43084308u), v3 = hadd2(Q[4 * j + 3], 0x43084308u);
+          uint32_t p0 = __byte_perm(v0, v1, 0x6420), p1 = __byte_perm(v2, v3, 0x6420);
+          o[j] = __byte_perm(p0 | (p0 >> 4), p1 | (p1 >> 4), 0x6420);
+        }
+      } else {
+        const int bias = (FMT == LLMC_FMT_PACK_INT32) ? 128 : 0;
+#pragma unroll
+        for (int j = 0; j < NW / 2; ++j) {
+          uint32_t b0 = (uint32_t)(__float2int_rn(bf_lo(Q[2 * j])) + bias) & 0xFFu;
+          uint32_t b1 = (uint32_t)(__float2int_rn(bf_hi(Q[2 * j])) + bias) & 0xFFu;
+          uint32_t b2 = (uint32_t)(__float2int_rn(bf_lo(Q[2 * j + 1])) + bias) & 0xFFu;
+          uint32_t b3 = (uint32_t)(__float2int_rn(bf_hi(Q[2 * j + 1])) + bias) & 0xFFu;
+          o[j] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+      }
+    } else if (FMT == LLMC_FMT_FP8) {
+#pragma unroll
+      for (int j = 0; j < NW / 2; ++j) {
+        uint32_t a = hmin2(hmax2(Q[2 * j], QMIN2), QMAX2), b = hmin2(hmax2(Q[2 * j + 1], QMIN2), QMAX2);
+        o[j] = e4m3x2(bf_lo(a), bf_hi(a)) | (e4m3x2(bf_lo(b), bf_hi(b)) << 16);
+      }
+    } else {  // FP4 from a bf16 quotient (MXFP4)
+#pragma unroll
+      for (int j = 0; j < NW / 4; ++j) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint32_t a = hadd2(hmin2(hmax2(Q[4 * j + k], QMIN2), QMAX2), 0u);  // -0 -> +0
+          v[2 * k] = bf_lo(a);
+          v[2 * k + 1] = bf_hi(a);
+        }
+        o[j] = e2m1x8(v);
+      }
+    }
+  } else {
+    float f[2 * NW];
+    if (g.fast) {
+#pragma unroll
+      for (int k = 0; k < NW; ++k) pair_f2(quot2(w[k], g.nr2, g.s2), f[2 * k], f[2 * k + 1]);
+      if (CHECK) {
+#pragma unroll
+        for (int k = 0; k < NW; ++k)
+          if (!(fabsf(f[2 * k]) <= 3.4028234663852886e38f && fabsf(f[2 * k + 1]) <= 3.4028234663852886e38f)) {
+            f[2 * k] = __fdiv_rn(bf_lo(w[k]), g.s);
+            f[2 * k + 1] = __fdiv_rn(bf_hi(w[k]), g.s);
+          }
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < NW; ++k) {
+        f[2 * k] = __fdiv_rn(bf_lo(w[k]), g.s);
+        f[2 * k + 1] = __fdiv_rn(bf_hi(w[k]), g.s);
+      }
+    }
+    if (FMT != LLMC_FMT_NVFP4 && g.has_zp) {
+#pragma unroll
+      for (int k = 0; k < 2 * NW; ++k) f[k] = f[k] + g.zp;
+    }
+    if (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) {
+#pragma unroll
+      for (int j = 0; j < NW / 4; ++j) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = fminf(fmaxf(__fadd_rn(f[8 * j + k], 0.0f), qmin), qmax);
+        o[j] = e2m1x8(v);
+      }
+    } else if (FMT == LLMC_FMT_FP8) {
+#pragma unroll
+      for (int j = 0; j < NW / 2; ++j) {
+        float a0 = fminf(fmaxf(f[4 * j], qmin), qmax), a1 = fminf(fmaxf(f[4 * j + 1], qmin), qmax);
+        float a2 = fminf(fmaxf(f[4 * j + 2], qmin), qmax), a3 = fminf(fmaxf(f[4 * j + 3], qmin), qmax);
+        o[j] = e4m3x2(a0, a1) | (e4m3x2(a2, a3) << 16);
+      }
+    } else {
+      int c[2 * NW];
+#pragma unroll
+      for (int k = 0; k < 2 * NW; ++k) c[k] = __float2int_rn(fminf(fmaxf(f[k], qmin), qmax));
+      if (OUT4) {
+#pragma unroll
+        for (int j = 0; j < NW / 4; ++j) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) word |= ((uint32_t)(c[8 * j + k] + 8) & 0xFu) << (4 * k);
+          o[j] = word;
+        }
+      } else {
+        const int bias = (FMT == LLMC_FMT_PACK_INT32) ? 128 : 0;
+#pragma unroll
+        for (int j = 0; j < NW / 2; ++j) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) word |= ((uint32_t)(c[4 * j + k] + bias) & 0xFFu) << (8 * k);
+          o[j] = word;
+        }
+      }
+    }
+  }
+}
+
+// min / max of the bf16 values in w[0..NW)
+template <int NW>
+__device__ __forceinline__ void minmax_words(const uint32_t* w, float& mn, float& mx) {
+  uint32_t M = w[0], m = w[0];
+#pragma unroll
+  for (int k = 1; k < NW; ++k) { M = hmax2(M, w[k]); m = hmin2(m, w[k]); }
+  mx = fmaxf(bf_lo(M), bf_hi(M));
+  mn = fminf(bf_lo(m), bf_hi(m));
+}
+
+// ------------------------------------------------------------------------
+// k_stream: power-of-two groups of 8..256 columns over the flat tensor.
+// A warp step covers 1024 elements; each lane owns a contiguous span of 32
+// (two 32-byte loads), so a group is LPG = GROUP/32 adjacent lanes (reduced
+// with shuffles) or a lane holds GPL = 32/GROUP whole groups.  Persistent
+// grid; each warp loads its next span before quantizing the current one.
+// Needs numel % 32 == 0 and 32-byte aligned input (16 / 32 for the output).
+// ------------------------------------------------------------------------
+// GROUP == 0: one group for the whole tensor (TENSOR strategy, GIVEN mode).
+template <int FMT, int BITS, int GROUP, int MODE>
+__device__ __forceinline__ void stream_span(const CastParams& p, int64_t e0, bool valid, const uint32_t* w) {
+  constexpr int LPG = GROUP >= 32 ? GROUP / 32 : 1;
+  constexpr int GPL = (GROUP >= 32 || GROUP == 0) ? 1 : 32 / GROUP;
+  constexpr int NW = 16 / GPL;
+  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+  static_assert(GROUP != 0 || MODE == MODE_GIVEN, "whole-tensor spans take stored qparams");
+  const int lane = threadIdx.x & 31;
+  const int64_t g0 = GROUP ? e0 / (GROUP ? GROUP : 1) : 0;
+  float mns[GPL], mxs[GPL];
+  if (MODE != MODE_GIVEN) {
+#pragma unroll
+    for (int j = 0; j < GPL; ++j) {
+      minmax_words<NW>(w + j * NW, mns[j], mxs[j]);
+#pragma unroll
+      for (int o = 1; o < LPG; o <<= 1) {
+        mns[j] = fminf(mns[j], __shfl_xor_sync(0xffffffffu, mns[j], o));
+        mxs[j] = fmaxf(mxs[j], __shfl_xor_sync(0xffffffffu, mxs[j], o));
+      }
+    }
+    if (MODE == MODE_STATS) {
+      if (valid && (lane % LPG) == 0) {
+#pragma unroll
+        for (int j = 0; j < GPL; ++j) { p.min_out[g0 + j] = f_to_bf16(mns[j]); p.max_out[g0 + j] = f_to_bf16(mxs[j]); }
+      }
+      return;
+    }
+  }
+  if (!valid) return;
+  const float qmin = p.a.qmin(), qmax = p.a.qmax();
+  uint32_t o[8];
+#pragma unroll
+  for (int j = 0; j < GPL; ++j) {
+    ElemQ e;
+    float s_store = 0.f, zp_store = 0.f;
+    if (MODE == MODE_FUSED) e = make_elemq_fused<FMT>(p, mns[j], mxs[j], &s_store, &zp_store);
+    else e = make_elemq_given<FMT>(p, g0 + j);
+    GQ g = to_gq(e);
+    uint32_t* oj = o + j * (OUT4 ? NW / 4 : NW / 2);
+    if (FMT == LLMC_FMT_NVFP4) quant_group<FMT, BITS, true, MODE == MODE_GIVEN, NW>(w + j * NW, g, qmin, qmax, oj);
+    else if (MODE == MODE_GIVEN && g.f32q) quant_group<FMT, BITS, true, true, NW>(w + j * NW, g, qmin, qmax, oj);
+    else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, NW>(w + j * NW, g, qmin, qmax, oj);
+    if (MODE == MODE_FUSED && (lane % LPG) == 0) store_scale<FMT>(p, g0 + j, s_store, zp_store);
+  }
+  if (OUT4) st_v4((uint8_t*)p.out + e0 / 2, o);
+  else st_v8((uint8_t*)p.out + e0, o);
+}
+
+template <int FMT, int BITS, int GROUP, int MODE>
+__global__ void __launch_bounds__(256, 3) k_stream(CastParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = p.rows * p.cols;
+  const int64_t steps = (n + 1023) >> 10;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  int64_t it = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  uint32_t a[16], b[16];
+  auto load = [&](int64_t step, uint32_t* buf) {
+    int64_t e0 = (step << 10) + lane * 32;
+    if (e0 < n) {
+      ld_v8(p.w + e0, buf);
+      ld_v8(p.w + e0 + 16, buf + 8);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) buf[k] = 0u;
+    }
+  };
+  if (it < steps) load(it, a);
+  while (it < steps) {
+    int64_t nx = it + nwarps;
+    if (nx < steps) load(nx, b);
+    int64_t e0 = (it << 10) + lane * 32;
+    stream_span<FMT, BITS, GROUP, MODE>(p, e0, e0 < n, a);
+    it = nx;
+    if (it >= steps) break;
+    nx = it + nwarps;
+    if (nx < steps) load(nx, a);
+    e0 = (it << 10) + lane * 32;
+    stream_span<FMT, BITS, GROUP, MODE>(p, e0, e0 < n, b);
+    it = nx;
+  }
+}
+
+// ------------------------------------------------------------------------
+// TENSOR strategy: a grid-wide min/max (16-bit compare-and-swap on an
+// order-preserving encoding of the bf16 bits) into two 16-bit slots, one
+// thread turning them into the qparams, then k_stream<GROUP = 0>.
+// ------------------------------------------------------------------------
+__device__ __forceinline__ uint16_t enc_bf16(uint16_t b) { return (b & 0x8000u) ? (uint16_t)~b : (uint16_t)(b | 0x8000u); }
+__device__ __forceinline__ uint16_t dec_bf16(uint16_t e) { return (e & 0x8000u) ? (uint16_t)(e & 0x7FFFu) : (uint16_t)~e; }
+
+__device__ __forceinline__ void cas_extreme(uint16_t* slot, uint16_t v, bool is_max) {
+  unsigned short* a = (unsigned short*)slot;
+  unsigned short cur = *(volatile unsigned short*)a;
+  for (int t = 0; t < (1 << 16); ++t) {  // lock-free: each failed swap means another thread's succeeded
+    if (is_max ? (v <= cur) : (v >= cur)) return;
+    unsigned short seen = atomicCAS(a, cur, (unsigned short)v);
+    if (seen == cur) return;
+    cur = seen;
+  }
+}
+
+__global__ void __launch_bounds__(256) k_tensor_minmax(const uint16_t* w, int64_t n, uint16_t* slot_min,
+                                                       uint16_t* slot_max) {
+  uint32_t M = 0xFF80FF80u, m = 0x7F807F80u;
+  const int64_t pieces = n / 16;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, st = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = tid; i < pieces; i += st) {
+    uint32_t v[8];
+    ld_v8(w + i * 16, v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { M = hmax2(M, v[k]); m = hmin2(m, v[k]); }
+  }
+  float mx = fmaxf(bf_lo(M), bf_hi(M)), mn = fminf(bf_lo(m), bf_hi(m));
+  for (int64_t i = pieces * 16 + tid; i < n; i += st) {
+    float x = bf16_to_f(w[i]);
+    mn = fminf(mn, x); mx = fmaxf(mx, x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (mn <= INFINITY) cas_extreme(slot_min, enc_bf16(f_to_bf16(mn)), false);  // skips NaN
+    if (mx >= -INFINITY) cas_extreme(slot_max, enc_bf16(f_to_bf16(mx)), true);
+  }
+}
+
+template <int FMT>
+__global__ void k_tensor_finish(CastParams p, uint16_t* slot_min, uint16_t* slot_max) {
+  float mn = bf16_to_f(dec_bf16(*slot_min)), mx = bf16_to_f(dec_bf16(*slot_max));
+  if (p.mode == MODE_STATS) {
+    p.min_out[0] = f_to_bf16(mn);
+    p.max_out[0] = f_to_bf16(mx);
+    return;
+  }
+  float s_store, zp_store;
+  make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
+  store_scale<FMT>(p, 0, s_store, zp_store);
+}
+
+// ------------------------------------------------------------------------
+// k_tile: one CTA per row (CHANNEL) or per block (BLOCK), the whole group
+// held in registers (NP 16-element pieces per thread): one HBM read.
+// Needs cols % 16 == 0, block width % 16 == 0, 32-byte aligned input.
+// ------------------------------------------------------------------------
+template <int FMT, int BITS, int MODE, int NP>
+__global__ void __launch_bounds__(256) k_tile(CastParams p) {
+  __shared__ float sh[32];
+  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+  const int64_t gi = blockIdx.x;
+  const Rect R = group_rect(p, gi);
+  const int64_t ppr = (R.c1 - R.c0) / 16, npc = (R.r1 - R.r0) * ppr;
+  uint32_t w[NP][8];
+  uint32_t M = 0xFF80FF80u, m = 0x7F807F80u;  // (-inf, -inf), (+inf, +inf)
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    int64_t pc = threadIdx.x + 256 * j;
+    if (pc < npc) {
+      int64_t r = R.r0 + pc / ppr, c = R.c0 + (pc % ppr) * 16;
+      ld_v8(p.w + r * p.cols + c, w[j]);
+      if (MODE != MODE_GIVEN) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { M = hmax2(M, w[j][k]); m = hmin2(m, w[j][k]); }
+      }
+    }
+  }
+  ElemQ e;
+  float s_store = 0.f, zp_store = 0.f;
+  if (MODE != MODE_GIVEN) {
+    float mx = fmaxf(bf_lo(M), bf_hi(M)), mn = fminf(bf_lo(m), bf_hi(m));
+    const int64_t h = R.r1 - R.r0, wd = R.c1 - R.c0;
+    if (p.a.strategy == LLMC_STRAT_BLOCK && (h < p.a.bh || wd < p.a.bw)) { mn = fminf(mn, 0.f); mx = fmaxf(mx, 0.f); }
+    mn = block_reduce(mn, false, sh);
+    mx = block_reduce(mx, true, sh);
+    if (MODE == MODE_STATS) {
+      if (threadIdx.x == 0) { p.min_out[gi] = f_to_bf16(mn); p.max_out[gi] = f_to_bf16(mx); }
+      return;
+    }
+    e = make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
+    if (threadIdx.x == 0) store_scale<FMT>(p, gi, s_store, zp_store);
+  } else {
+    e = make_elemq_given<FMT>(p, gi);
+  }
+  const GQ g = to_gq(e);
+  const float qmin = p.a.qmin(), qmax = p.a.qmax();
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    int64_t pc = threadIdx.x + 256 * j;
+    if (pc >= npc) break;
+    int64_t r = R.r0 + pc / ppr, c = R.c0 + (pc % ppr) * 16;
+    uint32_t o[4];
+    if (FMT == LLMC_FMT_NVFP4 || (MODE == MODE_GIVEN && g.f32q))
+      quant_group<FMT, BITS, true, MODE == MODE_GIVEN, 8>(w[j], g, qmin, qmax, o);
+    else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, 8>(w[j], g, qmin, qmax, o);
+    int64_t el = r * p.cols + c;
+    if (OUT4) *(uint2*)((uint8_t*)p.out + el / 2) = make_uint2(o[0], o[1]);
+    else st_v4((uint8_t*)p.out + el, o);
+  }
+}
+
+// ------------------------------------------------------------------------
 // small kernels
 // ------------------------------------------------------------------------
 __global__ void k_absmax(const uint16_t* w, int64_t n, float* out) {
@@ -461,9 +941,110 @@ static int validate(const CastParams& p) {
   return LLMC_OK;
 }
 
+template <int FMT, int BITS, int MODE>
+static bool launch_stream(const CastParams& p, int64_t group, cudaStream_t st) {
+  const int64_t steps = (p.rows * p.cols + 1023) / 1024;
+  dim3 g((unsigned)std::max<int64_t>(1, std::min<int64_t>((steps + 7) / 8, 148 * 3))), b(256);
+  constexpr bool fp4 = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4);
+  if (group == 16) k_stream<FMT, BITS, 16, MODE><<<g, b, 0, st>>>(p);
+  else if (group == 32) k_stream<FMT, BITS, 32, MODE><<<g, b, 0, st>>>(p);
+  else if constexpr (fp4) return false;
+  else if (group == 64) k_stream<FMT, BITS, 64, MODE><<<g, b, 0, st>>>(p);
+  else if (group == 128) k_stream<FMT, BITS, 128, MODE><<<g, b, 0, st>>>(p);
+  else return false;
+  llmc::note_launch();
+  return true;
+}
+
+template <int FMT, int BITS, int MODE>
+static bool launch_tile(const CastParams& p, int64_t pieces, cudaStream_t st) {
+  if constexpr (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) {
+    return false;  // FP4 formats only come with group strategies
+  } else {
+    const int ng = n_groups(p);
+    if (ng <= 0) return true;
+    if (pieces <= 256) k_tile<FMT, BITS, MODE, 1><<<ng, 256, 0, st>>>(p);
+    else if (pieces <= 512) k_tile<FMT, BITS, MODE, 2><<<ng, 256, 0, st>>>(p);
+    else if (pieces <= 1024) k_tile<FMT, BITS, MODE, 4><<<ng, 256, 0, st>>>(p);
+    else if (pieces <= 2048) k_tile<FMT, BITS, MODE, 8><<<ng, 256, 0, st>>>(p);
+    else return false;
+  }
+  llmc::note_launch();
+  return true;
+}
+
+// The register-resident kernels (k_stream, k_tile) when the shape and the
+// pointers allow them; false leaves the launch to the general kernels.
+template <int FMT, int BITS>
+static bool launch_fast(const CastParams& p, cudaStream_t st) {
+  const QArgs& a = p.a;
+  const int64_t n = p.rows * p.cols;
+  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+  if ((uintptr_t)p.w % 32) return false;
+  if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
+    if (n % 32) return false;
+    if (p.mode == MODE_STATS) return launch_stream<LLMC_FMT_INT8, 8, MODE_STATS>(p, a.group, st);
+    if ((uintptr_t)p.out % (OUT4 ? 16 : 32)) return false;
+    if (p.mode == MODE_FUSED) return launch_stream<FMT, BITS, MODE_FUSED>(p, a.group, st);
+    return launch_stream<FMT, BITS, MODE_GIVEN>(p, a.group, st);
+  }
+  if (a.strategy == LLMC_STRAT_TENSOR) {
+    if constexpr (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) {
+      return false;
+    } else {
+      const int64_t steps = (n + 1023) / 1024;
+      dim3 g((unsigned)std::max<int64_t>(1, std::min<int64_t>((steps + 7) / 8, 148 * 3))), b(256);
+      if (p.mode == MODE_GIVEN) {  // stored scale: quantize only
+        if (n % 32 || (uintptr_t)p.out % (OUT4 ? 16 : 32)) return false;
+        k_stream<FMT, BITS, 0, MODE_GIVEN><<<g, b, 0, st>>>(p); llmc::note_launch();
+        return true;
+      }
+      // FUSED / STATS: grid-wide statistics first
+      const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((n / 16 + 255) / 256, 148 * 4));
+      uint16_t *smin, *smax;
+      if (p.mode == MODE_STATS) {
+        smin = p.min_out; smax = p.max_out;
+      } else {
+        // the first 4 bytes of the packed output hold the two slots until
+        // the quantize pass overwrites them
+        if (n % 32 || (uintptr_t)p.out % (OUT4 ? 16 : 32) || n * (OUT4 ? 4 : 8) < 32) return false;
+        smin = (uint16_t*)p.out; smax = smin + 1;
+      }
+      if (cudaMemsetAsync(smin, 0xFF, 2, st) != cudaSuccess || cudaMemsetAsync(smax, 0x00, 2, st) != cudaSuccess)
+        return false;
+      k_tensor_minmax<<<(unsigned)blocks, 256, 0, st>>>(p.w, n, smin, smax); llmc::note_launch();
+      k_tensor_finish<FMT><<<1, 1, 0, st>>>(p, smin, smax); llmc::note_launch();
+      if (p.mode == MODE_STATS) return true;
+      CastParams q = p;  // FUSED: quantize with the qparams just stored
+      q.mode = MODE_GIVEN;
+      q.scale_in = p.scale_out;
+      q.scale_in_f32 = 0;
+      q.zp_in = p.zp_out;
+      k_stream<FMT, BITS, 0, MODE_GIVEN><<<g, b, 0, st>>>(q); llmc::note_launch();
+      return true;
+    }
+  }
+  if (a.strategy == LLMC_STRAT_CHANNEL || a.strategy == LLMC_STRAT_BLOCK) {
+    if (p.cols % 16) return false;
+    int64_t pieces = p.cols / 16;
+    if (a.strategy == LLMC_STRAT_BLOCK) {
+      if (a.bw % 16) return false;
+      pieces = std::min<int64_t>(a.bh, p.rows) * (std::min<int64_t>(a.bw, p.cols) / 16);
+    }
+    if (p.mode == MODE_STATS) return launch_tile<LLMC_FMT_INT8, 8, MODE_STATS>(p, pieces, st);
+    if ((uintptr_t)p.out % 16) return false;
+    if (p.mode == MODE_FUSED) return launch_tile<FMT, BITS, MODE_FUSED>(p, pieces, st);
+    return launch_tile<FMT, BITS, MODE_GIVEN>(p, pieces, st);
+  }
+  return false;
+}
+
 template <int FMT>
 static int launch_fmt(const CastParams& p, cudaStream_t st) {
   const QArgs& a = p.a;
+  if (p.rows * p.cols == 0) return LLMC_OK;
+  bool fast = (FMT == LLMC_FMT_PACK_INT32 && a.bits == 4) ? launch_fast<FMT, 4>(p, st) : launch_fast<FMT, 8>(p, st);
+  if (fast) return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
   bool grp = (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP);
   int64_t tpg = grp ? a.group / 8 : 0;
   bool pow2 = grp && (a.group % 8 == 0) && tpg >= 1 && tpg <= 32 && ((tpg & (tpg - 1)) == 0);

@@ -269,12 +269,43 @@ __global__ void k_xt_to_ut(const float* __restrict__ Xt, float* __restrict__ Ut,
 constexpr int PB = 128;
 constexpr int PLD = PB + 1;  // padded row stride of the shared-memory blocks
 // 16 warps: warp w walks rows (w, w+16, ...), its lanes walk the columns of a row.
+// Cholesky factor and inverse of one 32x32 diagonal sub-block held by one
+// warp in registers: lane i holds row i of the block in a[] on entry and row
+// i of L on exit; x[] returns column i of L^-1.  Rows/columns >= sz are
+// left untouched (zero on entry).
+__device__ __forceinline__ void warp_chol_inv32(float (&a)[32], float (&x)[32], int lane, int sz, bool& bad) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < sz) {
+      float p = __shfl_sync(0xffffffffu, a[j], j);
+      if (!(p > 0.0f)) { bad = true; p = 1.0f; }
+      const float piv = sqrtf(p);
+      if (lane == j) a[j] = piv;
+      else if (lane > j) a[j] = __fdiv_rn(a[j], piv);
+#pragma unroll
+      for (int m = j + 1; m < 32; ++m) {
+        const float lmj = __shfl_sync(0xffffffffu, a[j], m);
+        if (lane >= m) a[m] -= a[j] * lmj;
+      }
+    }
+  }
+  // column `lane` of X = L^-1 by forward substitution over the rows of L
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float sum = (j == lane) ? 1.0f : 0.0f;
+#pragma unroll
+    for (int l = 0; l < j; ++l) sum -= __shfl_sync(0xffffffffu, a[l], j) * x[l];
+    const float ljj = __shfl_sync(0xffffffffu, a[j], j);
+    x[j] = (j >= lane && j < sz) ? __fdiv_rn(sum, ljj) : 0.0f;
+  }
+}
+
 __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_t k0, int n, float* Linv,
                                                     int* status) {
   // Blocked in 32-column sub-steps: warp 0 factors and inverts each 32x32
-  // diagonal sub-block (warp-synchronous), then all 16 warps apply the panel
-  // solve and the trailing update; the off-diagonal blocks of the inverse
-  // follow block-row by block-row.
+  // diagonal sub-block in registers (shuffles), then all 16 warps apply the
+  // panel solve and the trailing update; the off-diagonal blocks of the
+  // inverse follow block-row by block-row.
   extern __shared__ float sm[];
   float* S = sm;             // [PB][PLD]  L of this block (lower)
   float* X = sm + PB * PLD;  // [PB][PLD]  its inverse (lower)
@@ -282,62 +313,91 @@ __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   constexpr int NW = 16, NT = 512, SB = 32;
   if (t == 0) bad = 0;
-  for (int i = warp; i < PB; i += NW)
-    for (int j = lane; j < PB; j += 32) {
-      S[i * PLD + j] = (i < n && j <= i) ? B[(k0 + i) * ld + k0 + j] : 0.f;
-      X[i * PLD + j] = 0.f;
-    }
+  // stage the lower triangle: all of a thread's loads are issued before its stores
+  {
+    float v[PB / NW][PB / 32];
+#pragma unroll
+    for (int a = 0; a < PB / NW; ++a)
+#pragma unroll
+      for (int b = 0; b < PB / 32; ++b) {
+        const int i = warp + a * NW, j = lane + b * 32;
+        v[a][b] = (i < n && j <= i) ? B[(k0 + i) * ld + k0 + j] : 0.f;
+      }
+#pragma unroll
+    for (int a = 0; a < PB / NW; ++a)
+#pragma unroll
+      for (int b = 0; b < PB / 32; ++b) {
+        const int i = warp + a * NW, j = lane + b * 32;
+        S[i * PLD + j] = v[a][b];
+        X[i * PLD + j] = 0.f;
+      }
+  }
   __syncthreads();
   const int nsub = (n + SB - 1) / SB;
   for (int kb = 0; kb < nsub; ++kb) {
     const int o = kb * SB, sz = min(SB, n - o);
     if (warp == 0) {
-      // (1) unblocked Cholesky of the diagonal sub-block; lane i owns row o+i
-      for (int j = 0; j < sz; ++j) {
-        float p = S[(o + j) * PLD + o + j];
-        if (!(p > 0.0f)) { if (lane == 0) bad = 1; p = 1.0f; }
-        const float piv = sqrtf(p);
-        if (lane > j && lane < sz) S[(o + lane) * PLD + o + j] = __fdiv_rn(S[(o + lane) * PLD + o + j], piv);
-        __syncwarp();
-        if (lane == 0) S[(o + j) * PLD + o + j] = piv;
-        if (lane > j && lane < sz) {
-          const float sij = S[(o + lane) * PLD + o + j];
-          for (int l = j + 1; l <= lane; ++l) S[(o + lane) * PLD + o + l] -= sij * S[(o + l) * PLD + o + j];
-        }
-        __syncwarp();
-      }
-      // (2) its inverse by forward substitution; lane c owns column o+c
+      float a[32], x[32];
+#pragma unroll
+      for (int l = 0; l < 32; ++l) a[l] = (lane < sz && l <= lane) ? S[(o + lane) * PLD + o + l] : 0.f;
+      bool b = false;
+      warp_chol_inv32(a, x, lane, sz, b);
+      if (b) bad = 1;
       if (lane < sz) {
-        for (int j = lane; j < sz; ++j) {
-          float s = (j == lane) ? 1.0f : 0.0f;
-          for (int l = lane; l < j; ++l) s -= S[(o + j) * PLD + o + l] * X[(o + l) * PLD + o + lane];
-          X[(o + j) * PLD + o + lane] = __fdiv_rn(s, S[(o + j) * PLD + o + j]);
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+          if (l <= lane) S[(o + lane) * PLD + o + l] = a[l];
+          if (l >= lane && l < sz) X[(o + l) * PLD + o + lane] = x[l];
         }
       }
     }
     __syncthreads();
     const int r0 = o + sz, rem = n - r0;
     if (rem <= 0) break;
-    // (3) panel: L21 = A21 * X11^T   (X11 lower: only l <= c)
-    float v[8];
-    int cnt = 0;
-    for (int e = t; e < rem * sz; e += NT, ++cnt) {
-      const int r = r0 + e / sz, c = e % sz;
-      float s = 0.f;
-      for (int l = 0; l <= c; ++l) s = fmaf(S[r * PLD + o + l], X[(o + c) * PLD + o + l], s);
-      v[cnt] = s;
-    }
-    __syncthreads();
-    cnt = 0;
-    for (int e = t; e < rem * sz; e += NT, ++cnt) S[(r0 + e / sz) * PLD + o + e % sz] = v[cnt];
-    __syncthreads();
-    // (4) trailing update of the lower triangle: A22 -= L21 L21^T
-    for (int r = r0 + warp; r < n; r += NW)
-      for (int l = r0 + lane; l <= r; l += 32) {
-        float s = 0.f;
-        for (int c = 0; c < sz; ++c) s = fmaf(S[r * PLD + o + c], S[l * PLD + o + c], s);
-        S[r * PLD + l] -= s;
+    // (3) panel: L21 = A21 * X11^T.  Lane c keeps row c of X11 in registers;
+    // warps take the rows (at most 96 = 16 warps x 6).
+    {
+      float xr[32];
+#pragma unroll
+      for (int l = 0; l < 32; ++l) xr[l] = (l <= lane && lane < sz) ? X[(o + lane) * PLD + o + l] : 0.f;
+      float v[6];
+#pragma unroll
+      for (int k = 0; k < 6; ++k) {
+        const int r = r0 + warp + NW * k;
+        float acc = 0.f;
+        if (r < n) {
+#pragma unroll
+          for (int l = 0; l < 32; ++l) acc = fmaf(S[r * PLD + o + l], xr[l], acc);
+        }
+        v[k] = acc;
       }
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < 6; ++k) {
+        const int r = r0 + warp + NW * k;
+        if (r < n && lane < sz) S[r * PLD + o + lane] = v[k];
+      }
+      __syncthreads();
+    }
+    // (4) trailing update of the lower triangle: A22 -= L21 L21^T.  Lane
+    // keeps row l of L21 in registers; warps take the rows r >= l.
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+      const int l = r0 + lane + 32 * m;
+      float lr[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) lr[c] = (l < n && c < sz) ? S[l * PLD + o + c] : 0.f;
+#pragma unroll
+      for (int k = 0; k < 6; ++k) {
+        const int r = r0 + warp + NW * k;
+        if (r < n && l <= r) {
+          float acc = 0.f;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) acc = fmaf(S[r * PLD + o + c], lr[c], acc);
+          S[r * PLD + l] -= acc;
+        }
+      }
+    }
     __syncthreads();
   }
   if (t == 0 && bad && status) atomicExch(status, LLMC_ENOT_PD);
@@ -406,7 +466,7 @@ struct BlockArgs {
   int strategy;
   int64_t gs;
   float qmin, qmax;
-  float* err;          // QB x r (column-major errors of this block)
+  float* err;          // rows x QB row-major errors of this block
   float* loss;         // r per-row losses
   const int* status;   // ENOT_PD -> identity
 };
@@ -420,87 +480,162 @@ __device__ __forceinline__ void scale_of(const BlockArgs& a, int64_t row, int co
   z = a.zp ? (float)a.zp[idx] : 0.0f;
 }
 
+// Correctly rounded x / y from r = RN(1/y) (Markstein's correction: with r
+// the correctly rounded reciprocal and x*r within an ulp of x/y, one fma
+// residual and one fma step give RN(x/y) when nothing overflows or
+// underflows).  Callers use it only where 1/y is a normal float.
+__device__ __forceinline__ float div_mk(float x, float y, float r) {
+  // on -x, so that x = +-0 keeps its sign through the correction (y > 0)
+  const float q0 = __fmul_rn(-x, -r);
+  const float e = __fmaf_rn(q0, y, -x);
+  return __fmaf_rn(e, -r, q0);
+}
+__device__ __forceinline__ bool recip_ok(float r) { return r > 1.0e-30f && r < 1.0e30f; }
+
 // fake_quantize of one float32 value with a bf16 scale (CT forward_helpers.py:175-210):
 // float32 quotient, + zp, clamp, round half-even, -> bf16, - zp, * scale rounded to bf16.
-__device__ __forceinline__ float fake_quant(float w, float s, float z, float qmin, float qmax) {
-  float q = __fdiv_rn(w, s) + z;
+__device__ __forceinline__ float fake_quant(float w, float s, float rs, bool fast, float z, float qmin, float qmax) {
+  float q = (fast ? div_mk(w, s, rs) : __fdiv_rn(w, s)) + z;
   q = rintf(fminf(fmaxf(q, qmin), qmax));
   float deq = rbf(q - z);
   return rbf(deq * s);
 }
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// One 128-column GPTQ block for ROWS rows per CTA, one row per thread.  The
+// block's factor rows (64 KB) are staged with asynchronous 16-byte copies and
+// the rows of W with batched vector loads, so staging costs a few memory
+// round trips; the 32 columns of a sub-block live in registers with every
+// index known at compile time; divisions use per-column reciprocals.
 __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
   extern __shared__ float sm[];
-  float* U1 = sm;                // [QB][QB]
-  float* QS = sm + QB * QB;      // [ROWS][QS_LD]
+  float* U1 = sm;                  // [QB][QB]
+  float* QS = U1 + QB * QB;        // [ROWS][QS_LD]
+  float* RD = QS + ROWS * QS_LD;   // [QB]  RN(1/d)
+  float* D2 = RD + QB;             // [QB]  RN(d*d)
+  float* RD2 = D2 + QB;            // [QB]  RN(1/(d*d))
   const int t = threadIdx.x;
   const int64_t row0 = (int64_t)blockIdx.x * ROWS;
   const int64_t row = row0 + t;
   const bool identity = a.status && *a.status == LLMC_ENOT_PD;
   const int cnt = a.count;
+  // rows of U and W start on 16-byte boundaries
+  const bool vec = (a.c % 4) == 0 && ((uintptr_t)a.U % 16) == 0 && ((uintptr_t)a.W % 16) == 0;
 
-  for (int e = t; e < QB * QB; e += ROWS) {
-    const int i = e / QB, j = e % QB;
-    float v = 0.f;
-    if (i < cnt && j < cnt) v = identity ? (i == j ? 1.f : 0.f) : a.U[(int64_t)(a.i1 + i) * a.c + a.i1 + j];
-    U1[e] = v;
+  if (identity || !vec || cnt < QB) {
+    for (int e = t; e < QB * QB; e += ROWS) {
+      const int i = e / QB, j = e % QB;
+      float v = 0.f;
+      if (i < cnt && j < cnt) v = identity ? (i == j ? 1.f : 0.f) : a.U[(int64_t)(a.i1 + i) * a.c + a.i1 + j];
+      U1[e] = v;
+    }
+  } else {
+    for (int e = t; e < QB * QB / 4; e += ROWS) {
+      const int i = e >> 5, j4 = (e & 31) * 4;
+      cp_async16(U1 + i * QB + j4, a.U + (int64_t)(a.i1 + i) * a.c + a.i1 + j4);
+    }
   }
-  // stage this CTA's rows of the block (coalesced along columns)
-  for (int e = t; e < ROWS * QB; e += ROWS) {
-    const int rr = e / QB, j = e % QB;
-    const int64_t gr = row0 + rr;
-    QS[rr * QS_LD + j] = (gr < a.r && j < cnt) ? a.W[gr * a.c + a.i1 + j] : 0.f;
+  // rows of W: 8 independent 16-byte loads in flight per thread
+  constexpr int PER = ROWS * QB / 4 / ROWS;  // float4 per thread (32)
+#pragma unroll
+  for (int b0 = 0; b0 < PER; b0 += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = (b0 + u) * ROWS + t;
+      const int rr = e >> 5, j4 = (e & 31) * 4;
+      const int64_t gr = row0 + rr;
+      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gr < a.r) {
+        const float* src = a.W + gr * a.c + a.i1 + j4;
+        if (vec && j4 + 4 <= cnt) v[u] = *(const float4*)src;
+        else {
+          if (j4 + 0 < cnt) v[u].x = src[0];
+          if (j4 + 1 < cnt) v[u].y = src[1];
+          if (j4 + 2 < cnt) v[u].z = src[2];
+          if (j4 + 3 < cnt) v[u].w = src[3];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = (b0 + u) * ROWS + t;
+      float* d = QS + (e >> 5) * QS_LD + (e & 31) * 4;
+      d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w;
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  for (int i = t; i < QB; i += ROWS) {
+    const float d = U1[i * QB + i];
+    const float d2 = __fmul_rn(d, d);
+    RD[i] = __frcp_rn(d);
+    D2[i] = d2;
+    RD2[i] = __frcp_rn(d2);
   }
   __syncthreads();
 
   float loss = 0.f;
   if (row < a.r) {
+    float s = 0.f, z = 0.f, rs = 0.f;
+    bool sfast = false;
+    int64_t next_g = -1;  // first column of the next scale group
     for (int s0 = 0; s0 < cnt; s0 += SUB) {
       float w[SUB], e[SUB];
 #pragma unroll
-      for (int j = 0; j < SUB; ++j) { w[j] = QS[t * QS_LD + s0 + j]; e[j] = 0.f; }
+      for (int j = 0; j < SUB; ++j) w[j] = QS[t * QS_LD + s0 + j];
       const int n = min(SUB, cnt - s0);
-      float s = 0.f, z = 0.f;
-      int cur_g = -1;
-      for (int ii = 0; ii < n; ++ii) {
-        const int i = s0 + ii;
-        const int col = a.i1 + i;
-        const int g = (a.strategy == LLMC_STRAT_GROUP) ? (int)(col / a.gs) : 0;
-        if (g != cur_g) { scale_of(a, row, col, s, z); cur_g = g; }
-        const float wi = w[0];
-        const float d = U1[i * QB + i];
-        const float q = fake_quant(wi, s, z, a.qmin, a.qmax);
-        QS[t * QS_LD + i] = q;
-        const float diff = wi - q;
-        loss += __fdiv_rn(diff * diff, d * d);
-        const float err = __fdiv_rn(diff, d);
-        // shift the sub-block left by one column while applying this column's update
 #pragma unroll
-        for (int j = 0; j < SUB - 1; ++j) {
-          const int cj = min(i + 1 + j, QB - 1);
-          w[j] = w[j + 1] - err * U1[i * QB + cj];
+      for (int ii = 0; ii < SUB; ++ii) {
+        e[ii] = 0.f;
+        if (ii < n) {
+          const int i = s0 + ii;
+          const int col = a.i1 + i;
+          if (col >= next_g) {
+            scale_of(a, row, col, s, z);
+            rs = __frcp_rn(s);
+            sfast = recip_ok(rs);
+            next_g = (a.strategy == LLMC_STRAT_GROUP) ? (col / a.gs + 1) * a.gs : (int64_t)1 << 62;
+          }
+          const float d = U1[i * QB + i];
+          const float wi = w[ii];
+          const float q = fake_quant(wi, s, rs, sfast, z, a.qmin, a.qmax);
+          QS[t * QS_LD + i] = q;
+          const float diff = wi - q;
+          const bool dfast = recip_ok(RD[i]) && recip_ok(RD2[i]);
+          const float dd = __fmul_rn(diff, diff);
+          loss += dfast ? div_mk(dd, D2[i], RD2[i]) : __fdiv_rn(dd, D2[i]);
+          const float err = dfast ? div_mk(diff, d, RD[i]) : __fdiv_rn(diff, d);
+          e[ii] = err;
+#pragma unroll
+          for (int j = ii + 1; j < SUB; ++j) w[j] -= err * U1[i * QB + s0 + j];
         }
-        w[SUB - 1] = 0.f;
-#pragma unroll
-        for (int j = 0; j < SUB - 1; ++j) e[j] = e[j + 1];
-        e[SUB - 1] = err;
-      }
-      // align errors when the sub-block was partial
-      for (int k = n; k < SUB; ++k) {
-#pragma unroll
-        for (int j = 0; j < SUB - 1; ++j) e[j] = e[j + 1];
-        e[SUB - 1] = 0.f;
       }
       // this sub-block's errors, row-major (rows x 128), as the K-major operand of the trailing update
       float4* erow = (float4*)(a.err + row * QB + s0);
 #pragma unroll
       for (int j = 0; j < SUB / 4; ++j) erow[j] = make_float4(e[4 * j], e[4 * j + 1], e[4 * j + 2], e[4 * j + 3]);
-      // lazy update of the later columns of this block
-      for (int j = s0 + SUB; j < cnt; ++j) {
-        float acc = 0.f;
+      // lazy update of the later columns of this block, four columns at a time
+      for (int j = s0 + SUB; j < cnt; j += 4) {
+        float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
 #pragma unroll
-        for (int ii = 0; ii < SUB; ++ii) acc = fmaf(e[ii], U1[(s0 + ii) * QB + j], acc);
-        QS[t * QS_LD + j] -= acc;
+        for (int ii = 0; ii < SUB; ++ii) {
+          const float* u = U1 + (s0 + ii) * QB + j;
+          acc0 = fmaf(e[ii], u[0], acc0);
+          acc1 = fmaf(e[ii], u[1], acc1);
+          acc2 = fmaf(e[ii], u[2], acc2);
+          acc3 = fmaf(e[ii], u[3], acc3);
+        }
+        QS[t * QS_LD + j] -= acc0;
+        QS[t * QS_LD + j + 1] -= acc1;
+        QS[t * QS_LD + j + 2] -= acc2;
+        QS[t * QS_LD + j + 3] -= acc3;
       }
     }
     a.loss[row] += loss / 2.0f;
@@ -654,13 +789,14 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
   if (rows == 0) {
     return cudaMemsetAsync(loss_out, 0, sizeof(float), st) == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
   }
+  if ((uintptr_t)workspace % 16) return LLMC_EINVAL_ARG;
   float* W = (float*)workspace;
-  float* E = W + rows * cols;
+  float* E = W + ((rows * cols + 3) & ~(int64_t)3);  // 16-byte aligned rows for the vector stores
   float* L = E + (int64_t)QB * rows;
   k_init_w<<<grid_for(rows * cols), 256, 0, st>>>((const uint16_t*)w_bf16, W, rows, cols, dead); llmc::note_launch();
   if (cudaMemsetAsync(L, 0, sizeof(float) * rows, st) != cudaSuccess) return LLMC_ECUDA;
   static uint64_t attr_mask = 0;
-  const int smem = (QB * QB + ROWS * QS_LD) * (int)sizeof(float);
+  const int smem = (QB * QB + ROWS * QS_LD + 3 * QB) * (int)sizeof(float);
   if (!set_smem_attr(k_gptq_block, smem, &attr_mask)) return LLMC_ECUDA;
   BlockArgs ba;
   ba.W = W; ba.r = rows; ba.c = cols; ba.U = Hinv;

@@ -89,6 +89,16 @@ LARGE = [
     ("MXFP4A16", 1024, 2048, "student_t"),
     ("NVFP4A16", 1024, 4096, "normal"),
     ("FP8", 128, 4096, "normal"),
+    # shapes that select each kernel: channel rows held in 1/2/4/8 registers
+    # pieces or too long for them, per-tensor with a ragged tail, group-16
+    # spans with numel % 32 != 0
+    ("FP8_DYNAMIC", 64, 28672, "student_t"),
+    ("FP8_DYNAMIC", 16, 40000, "normal"),
+    ("W8A16", 96, 14336, "normal"),
+    ("FP8", 33, 1000, "student_t"),
+    ("FP8", 256, 4100, "normal"),
+    ("NVFP4A16", 33, 1040, "normal"),
+    ("MXFP4A16", 7, 4096, "student_t"),
 ]
 
 
@@ -187,3 +197,55 @@ def test_edge_cases_and_errors():
     z = ops.modelfree_quantize(torch.zeros(8, 256, dtype=torch.bfloat16, device="cuda"), args)
     assert torch.all(z["weight_scale"].float() == 2.0**-7)
     assert torch.all(z["weight_packed"] == 0x88888888 - 2**32)
+
+
+@pytest.mark.parametrize("scheme", ["W4A16", "W4A16_ASYM", "W8A16", "FP8_DYNAMIC", "FP8", "FP8_BLOCK", "MXFP4A16",
+                                    "NVFP4A16"])
+def test_unaligned_views_match_aligned(scheme):
+    """A weight view 16 bytes past an aligned address (not 32-byte aligned) takes
+    the general kernels; its results equal the aligned copy's bit for bit."""
+    rows, cols = 256, 2048
+    args = _weights_args(scheme)
+    base = rand_bf16(rows * cols + 8, 1, seed=11).reshape(-1).cuda()
+    view = base[8:].view(rows, cols)
+    assert view.data_ptr() % 32 == 16
+    dense = view.clone()
+    gs = ops.fused_global_scale([dense]) if scheme == "NVFP4A16" else None
+    a = ops.modelfree_quantize(view, args, gs)
+    b = ops.modelfree_quantize(dense, args, gs)
+    for k in b:
+        np.testing.assert_array_equal(bits(a[k]), bits(b[k]), err_msg=f"{scheme}:{k}")
+
+
+def test_float32_scales_quotient_matches_torch():
+    """Stored float32 scales: float32 quotient, round half-even, clamp, as torch
+    evaluates x.float() / s -- many random scales through the paired fast path."""
+    rows, cols, gsz = 512, 4096, 128
+    g = torch.Generator().manual_seed(9)
+    wt = (torch.randn(rows, cols, generator=g) * 2).to(torch.bfloat16)
+    st = torch.rand(rows, cols // gsz, generator=g) * 0.03 + 1e-4
+    args = QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="group", group_size=gsz)
+    out = ops.quantize_pack(wt.cuda(), args, st.cuda(), fmt=_lib.FMT_INT8)
+    q = wt.float() / st.repeat_interleave(gsz, dim=1)
+    ref = torch.clamp(torch.round(q), -128, 127).to(torch.int8)
+    np.testing.assert_array_equal(bits(out), bits(ref))
+
+
+def test_overflowing_and_tiny_scales_match_torch():
+    """Quotients that overflow float32 (huge weights, tiny stored scales) and
+    scales whose reciprocal is not a normal float take the exact division."""
+    rows, cols, gsz = 64, 256, 32
+    g = torch.Generator().manual_seed(4)
+    wt = torch.randn(rows, cols, generator=g)
+    wt[:, :64] *= 1e30
+    wt = wt.to(torch.bfloat16)
+    st = torch.full((rows, cols // gsz), 0.5)
+    st[:, 0] = 1e-12      # x / s overflows for the 1e30 columns
+    st[:, 1] = 1e-38      # reciprocal above the normal range
+    st[:, 2] = 3e38       # reciprocal below it
+    st = st.to(torch.bfloat16)
+    args = QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="group", group_size=gsz)
+    out = ops.quantize_pack(wt.cuda(), args, st.cuda(), fmt=_lib.FMT_INT8)
+    q = (wt.float() / st.float().repeat_interleave(gsz, dim=1)).to(torch.bfloat16).float()
+    ref = torch.clamp(torch.round(q), -128, 127).to(torch.int8)
+    np.testing.assert_array_equal(bits(out), bits(ref))
