@@ -214,3 +214,77 @@ def fused_absmax(stats: list[tuple[np.ndarray, np.ndarray]]) -> np.float32:
         a = max(a, F32(-mn.min()))
         a = max(a, F32(mx.max()))
     return F32(a)
+
+
+# ---------------------------------------------------------------- MSE grid search
+def fake_quant_groups(x: np.ndarray, scale: np.ndarray, zp, args: QArgs, dtype: str = "bf16") -> np.ndarray:
+    """``fake_quantize`` of grouped values ``x`` (..., n) with per-group scale
+    / zero point (...,) as ``_quantize_dequantize`` evaluates it
+    (CT/quantization/lifecycle/forward_helpers.py ``_quantize_dequantize``):
+    quotient and every later op rounded to the tensor's dtype."""
+    from .numerics import cast_to_fp4
+
+    R = rb if dtype == "bf16" else (lambda v: np.asarray(v, dtype=F32))
+    s = np.asarray(scale, F32)[..., None]
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        q = R(x / s)
+        if zp is not None:
+            z = np.asarray(zp, F32)[..., None]
+            q = R(q + z)
+        qmin, qmax = calculate_range(args)
+        q = np.clip(q, qmin, qmax)
+        if args.type == "int":
+            q = np.rint(q)
+        elif args.num_bits == 8:
+            q = round_fp8_e4m3(q)
+        else:
+            q = cast_to_fp4(q)
+        if zp is not None:
+            q = R(q - z)
+        return R(q * s)
+
+
+def mse_minmax(w: np.ndarray, args: QArgs, maxshrink: float = 0.2, patience: int = 5, grid: float = 100.0,
+               norm: float = 2.4, dtype: str = "bf16"):
+    """``memoryless_mse`` observer statistics: the eager grid search of
+    ``_grid_search_eager`` (S/observers/mse_quant.py:90-141) with
+    ``_calculate_error`` (:235-273).
+
+    Per group: candidates (min, max) * p, p = 1 - i/grid for i < int(maxshrink *
+    grid); error = sum(|fake_quant(x) - x| ** norm) in the tensor's dtype
+    (the exponent itself rounded to that dtype, as torch's ``pow`` with a
+    Python scalar does; each power rounded to the dtype, summed in float64
+    here, then rounded);
+    a candidate replaces the best when its error is strictly lower; the search
+    stops for the whole tensor after ``patience`` consecutive steps in which no
+    group improved.  Returns (min_vals, max_vals) like ``minmax``.
+    """
+    R = rb if dtype == "bf16" else (lambda v: np.asarray(v, dtype=F32))
+    f = flatten_weight(np.asarray(w, dtype=F32), args)
+    mn0, mx0 = f.min(axis=-1), f.max(axis=-1)
+    best = np.full(mn0.shape, F32(3.3895313892515355e38 if dtype == "bf16" else np.finfo(F32).max), F32)
+    bmn, bmx = mn0.copy(), mx0.copy()
+    steps = int(maxshrink * grid)
+    no_improve = 0
+    for i in range(steps):
+        p = F32(1 - i / grid)
+        smn, smx = R(mn0 * p), R(mx0 * p)
+        scale, zp = calculate_qparams(smn, smx, args, dtype=dtype)
+        zpv = None if zp is None else np.asarray(zp, F32)
+        q = fake_quant_groups(f, scale, zpv, args, dtype)
+        with np.errstate(over="ignore", invalid="ignore"):
+            d = np.abs(R(q - f)).astype(F32)
+            # torch casts the exponent to the tensor's dtype: bf16(2.4) = 2.40625
+            e = R(np.power(d, R(F32(norm))).astype(F32))
+            err = R(e.astype(np.float64).sum(axis=-1).astype(F32))
+        improved = err < best
+        if improved.any():
+            best = np.where(improved, err, best)
+            bmn = np.where(improved, smn, bmn)
+            bmx = np.where(improved, smx, bmx)
+            no_improve = 0
+        else:
+            no_improve += 1
+            if no_improve >= patience:
+                break
+    return bmn.astype(F32), bmx.astype(F32)

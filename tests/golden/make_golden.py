@@ -10,6 +10,8 @@ seeded synthetic inputs and stores inputs and outputs as ``.npz`` files:
 * ``observer_<case>.npz`` -- memoryless min-max statistics and
   ``calculate_qparams`` output (``S/observers/min_max.py:106-110``,
   ``S/observers/base.py:99-123``).
+* ``mse_<case>.npz`` -- the ``memoryless_mse`` grid-search observer
+  (``S/observers/mse.py``, ``S/observers/mse_quant.py``) and its qparams.
 * ``hessian.npz`` -- ``accumulate_hessian`` over several calls
   (``S/modifiers/gptq/gptq_quantize.py:63-97``).
 * ``gptq_<case>.npz`` -- ``quantize_weight``
@@ -221,6 +223,42 @@ def gen_observers():
         print("observer", name, tuple(mn.shape), qp["scale"].dtype, qp["zero_point"].dtype)
 
 
+MSE_CASES = {
+    "int4_sym_group128": (QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=128),
+                          (96, 512)),
+    "int4_asym_group128": (QuantizationArgs(num_bits=4, type="int", symmetric=False, strategy="group",
+                                            group_size=128), (96, 512)),
+    "int8_sym_channel": (QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="channel"), (96, 512)),
+    "int8_asym_channel": (QuantizationArgs(num_bits=8, type="int", symmetric=False, strategy="channel"), (96, 512)),
+    "int4_sym_tensor": (QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="tensor"), (64, 256)),
+    "fp8_block_128": (QuantizationArgs(num_bits=8, type="float", symmetric=True, strategy="block",
+                                       block_structure=[128, 128]), (200, 300)),
+    "int4_sym_group32": (QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=32),
+                         (64, 512)),
+}
+
+
+def gen_mse_observers():
+    """``memoryless_mse`` (S/observers/mse.py:12-45 -> mse_quant.py:19-141, the
+    eager grid search with the default maxshrink 0.2, grid 100, patience 5,
+    norm 2.4) on bf16 weights, then ``get_qparams``."""
+    for i, (name, (args, (r, c))) in enumerate(MSE_CASES.items()):
+        w = make_weight(r, c, seed=500 + i, kind="student_t" if i % 2 else "normal")
+        obs = Observer.load_from_registry("memoryless_mse", base_name="weight", args=args)
+        obs(w)
+        mn, mx = obs.min_vals.clone(), obs.max_vals.clone()
+        qp = obs.get_qparams()
+        np.savez_compressed(
+            os.path.join(HERE, f"mse_{name}.npz"),
+            weight=to_np(w),
+            min_vals=to_np(mn),
+            max_vals=to_np(mx),
+            scale=to_np(qp["scale"]),
+            zero_point=to_np(qp["zero_point"]),
+        )
+        print("mse", name, tuple(mn.shape), qp["scale"].dtype)
+
+
 # --------------------------------------------------------------------------
 # Hessian + GPTQ
 # --------------------------------------------------------------------------
@@ -304,7 +342,11 @@ def gen_gptq():
 
 if __name__ == "__main__":
     torch.manual_seed(0)
+    if sys.argv[1:] == ["mse"]:
+        gen_mse_observers()
+        sys.exit(0)
     gen_observers()
+    gen_mse_observers()
     gen_modelfree()
     gen_nvfp4_fused()
     gen_hessian()

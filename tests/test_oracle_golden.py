@@ -175,3 +175,49 @@ def test_bf16_rounding_against_torch():
     x = (rng.standard_normal(200000) * np.exp(rng.uniform(-30, 30, 200000))).astype(np.float32)
     ref = torch.from_numpy(x).to(torch.bfloat16).view(torch.uint16).numpy()
     np.testing.assert_array_equal(numerics.f32_to_bf16_bits(x), ref)
+
+
+MSE_CASES = {
+    "int4_sym_group128": QArgs(4, "int", True, "group", 128),
+    "int4_asym_group128": QArgs(4, "int", False, "group", 128),
+    "int8_sym_channel": QArgs(8, "int", True, "channel", None),
+    "int8_asym_channel": QArgs(8, "int", False, "channel", None),
+    "int4_sym_tensor": QArgs(4, "int", True, "tensor", None),
+    "fp8_block_128": QArgs(8, "float", True, "block", None, (128, 128), zp_dtype="fp8"),
+    "int4_sym_group32": QArgs(4, "int", True, "group", 32),
+}
+
+
+@pytest.mark.parametrize("case", sorted(MSE_CASES))
+def test_mse_observer_bit_exact(case):
+    """``memoryless_mse`` grid search (S/observers/mse_quant.py) on bf16 weights."""
+    g = load(f"mse_{case}")
+    args = MSE_CASES[case]
+    mn, mx = observers.mse_minmax(bf16(g["weight"]), args)
+    np.testing.assert_array_equal(numerics.f32_to_bf16_bits(mn), g["min_vals"].reshape(mn.shape))
+    np.testing.assert_array_equal(numerics.f32_to_bf16_bits(mx), g["max_vals"].reshape(mx.shape))
+    scale, zp = observers.calculate_qparams(mn, mx, args)
+    np.testing.assert_array_equal(numerics.f32_to_bf16_bits(scale), g["scale"].reshape(scale.shape))
+
+
+# T/llmcompressor/observers/test_mse.py:9-44: float32 arange(24)/24 as 6x4, 8 bits
+MSE_KNOWN = [
+    ("tensor", True, 4.8103e-06), ("tensor", False, 1.1258e-06),
+    ("channel", True, 2.5675e-06), ("channel", False, 2.3696e-07),
+    ("group", True, 3.1282e-06), ("group", False, 1.3794e-07),
+    ("block", True, 2.8968e-06), ("block", False, 5.6068e-07),
+]
+
+
+@pytest.mark.parametrize("strategy,symmetric,exp_loss", MSE_KNOWN)
+def test_reference_mse_known_answers(strategy, symmetric, exp_loss):
+    t = (np.arange(24, dtype=np.float32) / np.float32(24)).reshape(6, 4)
+    args = QArgs(8, "int", symmetric, strategy, 2 if strategy == "group" else None,
+                 (3, 2) if strategy == "block" else None)
+    mn, mx = observers.mse_minmax(t, args, dtype="f32")
+    scale, zp = observers.calculate_qparams(mn, mx, args, dtype="f32")
+    f = observers.flatten_weight(t, args)
+    q = observers.fake_quant_groups(f, scale.reshape(f.shape[:-1]), np.asarray(zp, np.float32).reshape(f.shape[:-1]),
+                                    args, dtype="f32")
+    loss = float(np.sum(np.abs(f - q) ** 2) / t.size)
+    assert loss == pytest.approx(exp_loss, abs=1e-10)
