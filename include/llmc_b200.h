@@ -83,6 +83,22 @@ const char* llmc_status_string(int status);
 int llmc_observe_minmax(const void* w_bf16, int64_t rows, int64_t cols, const LlmcQuantArgs* args,
                         void* min_bf16, void* max_bf16, void* stream);
 
+/* MSE grid-search statistics of a bf16 weight (the `memoryless_mse` weight
+ * observer): S/observers/mse.py:12-45 -> S/observers/mse_quant.py:19-141
+ * (`_grid_search_mse`, eager search) and :235-273 (`_calculate_error`),
+ * observer_kwargs maxshrink / patience / grid / norm (reference defaults 0.2,
+ * 5, 100, 2.4).  Outputs as llmc_observe_minmax (the chosen shrunk range);
+ * feed them to llmc_calculate_qparams as `get_qparams` does.  GROUP and
+ * TENSOR_GROUP need a group of 32 * {1,2,4,8,16,32} or a power of two below
+ * 32; CHANNEL, BLOCK and TENSOR groups up to 32768 values; at most 64 grid
+ * steps.  `workspace`: llmc_observe_mse_workspace_size bytes of device
+ * memory (8 bytes per group + 8).  The first call on a device, and a call
+ * with a new `norm`, synchronises `stream` to upload the power table. */
+int llmc_observe_mse_workspace_size(int64_t rows, int64_t cols, const LlmcQuantArgs* args, int64_t* bytes);
+int llmc_observe_mse(const void* w_bf16, int64_t rows, int64_t cols, const LlmcQuantArgs* args, float maxshrink,
+                     int patience, float grid, float norm, void* min_bf16, void* max_bf16, void* workspace,
+                     void* stream);
+
 /* Absolute maximum of `n` bf16 values, max-accumulated into *absmax_f32
  * (initialise it to 0).  Used for fused-set NVFP4 global scales:
  * `Observer.get_global_scale`, S/observers/base.py:78-96. */

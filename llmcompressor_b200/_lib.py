@@ -64,6 +64,8 @@ _SIGS = {
     "llmc_kernel_launches": [],
     "llmc_status_string": [_I32],
     "llmc_observe_minmax": [_P, _I64, _I64, _QA, _P, _P, _P],
+    "llmc_observe_mse_workspace_size": [_I64, _I64, _QA, _P],
+    "llmc_observe_mse": [_P, _I64, _I64, _QA, ctypes.c_float, _I32, ctypes.c_float, ctypes.c_float, _P, _P, _P, _P],
     "llmc_absmax_accumulate": [_P, _I64, _P, _P],
     "llmc_global_scale": [_P, _P, _P],
     "llmc_calculate_qparams": [_P, _P, _I64, _QA, _P, _P, _P, _P],

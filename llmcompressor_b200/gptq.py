@@ -154,15 +154,20 @@ def weight_qparams(module: torch.nn.Module, quant_args) -> tuple[torch.Tensor, t
     """The weight observer's qparams (S/modifiers/gptq/gptq_quantize.py:168-173).
 
     Weights are always observed memorylessly (S/modifiers/quantization/calibration.py:64-78);
-    the min-max statistics of the unmodified weight are recomputed on the GPU.
+    the statistics of the unmodified weight are recomputed on the GPU: min-max, or
+    the MSE grid search when the attached observer is an MSE observer.
     An attached observer's statistics are released as ``get_qparams`` does.
     """
     from . import ops
 
     obs = getattr(module, "weight_observer", None)
     if obs is not None and "mse" in type(obs).__name__.lower():
-        raise NotImplementedError("MSE weight observers are not implemented on this path")
-    mn, mx = ops.observe_minmax(module.weight, quant_args)
+        # S/observers/mse.py: the grid search on the GPU with the observer's knobs
+        mn, mx = ops.observe_mse(module.weight, quant_args, getattr(obs, "maxshrink", None),
+                                 getattr(obs, "patience", None), getattr(obs, "grid", None),
+                                 getattr(obs, "norm", None))
+    else:
+        mn, mx = ops.observe_minmax(module.weight, quant_args)
     scale, zp = ops.calculate_qparams(mn, mx, quant_args)
     if obs is not None and hasattr(obs, "delete_statistics"):
         try:

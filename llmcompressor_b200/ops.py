@@ -63,6 +63,69 @@ def observe_minmax(w: torch.Tensor, args) -> tuple[torch.Tensor, torch.Tensor]:
     return mn, mx
 
 
+MSE_DEFAULTS = {"maxshrink": 0.20, "patience": 5, "grid": 100.0, "norm": 2.4}
+
+
+def observe_mse(w: torch.Tensor, args, maxshrink: float | None = None, patience: int | None = None,
+                grid: float | None = None, norm: float | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """MSE grid-search statistics (``memoryless_mse``: S/observers/mse.py:12-45,
+    S/observers/mse_quant.py:19-141).  Unset knobs come from
+    ``args.observer_kwargs`` and then the reference's defaults."""
+    w = _check_weight(w)
+    kw = dict(MSE_DEFAULTS)
+    kw.update(getattr(args, "observer_kwargs", None) or {})
+    maxshrink = float(kw["maxshrink"] if maxshrink is None else maxshrink)
+    patience = int(kw["patience"] if patience is None else patience)
+    grid = float(kw["grid"] if grid is None else grid)
+    norm = float(kw["norm"] if norm is None else norm)
+    rows, cols = w.shape
+    shape = stats_shape(rows, cols, args)
+    mn = torch.empty(shape, dtype=torch.bfloat16, device=w.device)
+    mx = torch.empty(shape, dtype=torch.bfloat16, device=w.device)
+    qa = qargs_struct(args)
+    nbytes = ctypes.c_int64(0)
+    check(lib().llmc_observe_mse_workspace_size(rows, cols, ctypes.byref(qa), ctypes.byref(nbytes)), "observe_mse")
+    ws = torch.empty(max(int(nbytes.value), 8), dtype=torch.uint8, device=w.device)
+    check(lib().llmc_observe_mse(ptr(w), rows, cols, ctypes.byref(qa), maxshrink, patience, grid, norm, ptr(mn),
+                                 ptr(mx), ptr(ws), stream_ptr(w.device)), "observe_mse")
+    return mn, mx
+
+
+class MemorylessMSEObserver:
+    """GPU mirror of the reference's ``memoryless_mse`` weight observer
+    (S/observers/mse.py:12-45): ``forward(weight)`` sets ``min_vals`` /
+    ``max_vals``; ``get_qparams()`` returns scale / zero_point (and
+    ``global_scale`` for TENSOR_GROUP) and drops the statistics, as
+    ``Observer.get_qparams`` (S/observers/base.py:99-123) does."""
+
+    def __init__(self, args, base_name: str = "weight", **_):
+        self.args = args
+        self.base_name = base_name
+        kw = dict(MSE_DEFAULTS)
+        kw.update(getattr(args, "observer_kwargs", None) or {})
+        self.maxshrink, self.patience = float(kw["maxshrink"]), int(kw["patience"])
+        self.grid, self.norm = float(kw["grid"]), float(kw["norm"])
+        self.min_vals = self.max_vals = None
+        self._global_scale = None
+
+    def __call__(self, observed: torch.Tensor):
+        return self.forward(observed)
+
+    def forward(self, observed: torch.Tensor):
+        self.min_vals, self.max_vals = observe_mse(observed, self.args, self.maxshrink, self.patience, self.grid,
+                                                   self.norm)
+        if _strategy(self.args) == "tensor_group":
+            self._global_scale = fused_global_scale([observed])
+        return self
+
+    def get_qparams(self) -> dict:
+        assert self.min_vals is not None, "No statistics available"
+        scale, zp = calculate_qparams(self.min_vals, self.max_vals, self.args, global_scale=self._global_scale)
+        out = {"scale": scale, "zero_point": zp, "global_scale": self._global_scale}
+        self.min_vals = self.max_vals = None
+        return out
+
+
 def absmax_(w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """Max-accumulate |w| into the float32 scalar ``out`` (initialise to 0)."""
     require_cuda(w, out)
