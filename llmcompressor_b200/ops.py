@@ -91,6 +91,33 @@ def observe_mse(w: torch.Tensor, args, maxshrink: float | None = None, patience:
     return mn, mx
 
 
+def grid_search_mse(observed: torch.Tensor, args, token_args=None, maxshrink: float = 0.20, patience: int = 5,
+                    grid: float = 100.0, norm: float = 2.4, chunk_size: int = 5):
+    """Drop-in for the reference's ``_grid_search_mse`` (S/observers/mse_quant.py:19-87)
+    on a bf16 *weight* view from ``flatten_for_calibration``: (1, r, G, gs) for
+    group strategies, (1, r, 1, c) channel, (1, 1, n) tensor, (1, R, C, bh*bw)
+    block (zero-padded).  Returns (min_vals, max_vals) shaped like the
+    reference's.  ``token_args`` / ``chunk_size`` only steer the reference's
+    evaluation order and are not needed here."""
+    s = _strategy(args)
+    if observed.dim() == 4 and observed.shape[0] == 1 and s in ("group", "tensor_group"):
+        _, r, g, gs = observed.shape
+        w2 = observed.reshape(r, g * gs)
+    elif observed.dim() == 4 and observed.shape[0] == 1 and s == "channel":
+        w2 = observed.reshape(observed.shape[1], observed.shape[3])
+    elif observed.dim() == 3 and observed.shape[0] == 1 and s == "tensor":
+        w2 = observed.reshape(1, observed.shape[2])
+    elif observed.dim() == 4 and observed.shape[0] == 1 and s == "block":
+        bh, bw = args.block_structure
+        _, R, C, _ = observed.shape
+        w2 = observed.reshape(R, C, bh, bw).transpose(1, 2).reshape(R * bh, C * bw)
+    else:
+        raise NotImplementedError(f"MSE search over an observed view of shape {tuple(observed.shape)} ({s})")
+    mn, mx = observe_mse(w2.contiguous(), args, maxshrink, patience, grid, norm)
+    lead = observed.shape[1:-1]
+    return mn.reshape(lead), mx.reshape(lead)
+
+
 class MemorylessMSEObserver:
     """GPU mirror of the reference's ``memoryless_mse`` weight observer
     (S/observers/mse.py:12-45): ``forward(weight)`` sets ``min_vals`` /

@@ -75,3 +75,28 @@ def test_mse_observer_object_and_knobs():
     np.testing.assert_array_equal(bits(qp["scale"]).reshape(osc.shape), onum.f32_to_bf16_bits(osc))
     with pytest.raises(AssertionError):
         obs.get_qparams()
+
+
+@pytest.mark.parametrize("case", ["int4_sym_group128", "int8_sym_channel", "int4_sym_tensor", "fp8_block_128"])
+def test_grid_search_view_dropin(case):
+    """The drop-in for _grid_search_mse takes the reference's flattened weight views."""
+    g = load(f"mse_{case}")
+    args, qa = CASES[case]
+    w = to_dev_bf16(g["weight"])
+    r, c = w.shape
+    s = getattr(args.strategy, "value", args.strategy)
+    if s == "group":
+        view = w.reshape(1, r, c // args.group_size, args.group_size)
+    elif s == "channel":
+        view = w.reshape(1, r, 1, c)
+    elif s == "tensor":
+        view = w.reshape(1, 1, r * c)
+    else:
+        bh, bw = args.block_structure
+        pr, pc = -(-r // bh) * bh, -(-c // bw) * bw
+        p = torch.zeros(pr, pc, dtype=w.dtype, device=w.device)
+        p[:r, :c] = w
+        view = p.reshape(pr // bh, bh, pc // bw, bw).transpose(1, 2).reshape(1, pr // bh, pc // bw, bh * bw)
+    mn, mx = ops.grid_search_mse(view, args)
+    np.testing.assert_array_equal(bits(mn).reshape(g["min_vals"].shape), g["min_vals"])
+    np.testing.assert_array_equal(bits(mx).reshape(g["max_vals"].shape), g["max_vals"])
