@@ -793,34 +793,38 @@ __global__ void k_tensor_finish(CastParams p, uint16_t* slot_min, uint16_t* slot
 }
 
 // ------------------------------------------------------------------------
-// k_tile: one CTA per row (CHANNEL) or per block (BLOCK), the whole group
-// held in registers (NP 16-element pieces per thread): one HBM read.
-// Needs cols % 16 == 0, block width % 16 == 0, 32-byte aligned input.
+// k_tile: CHANNEL rows and BLOCK tiles, one CTA per group at a time, the
+// whole group held in registers (NP 16-value pieces per thread): one HBM
+// read.  Persistent over groups; with PF the CTA loads its next group while
+// it quantizes the current one.  Needs cols % 16 == 0, block width % 16 == 0,
+// 32-byte aligned input.
 // ------------------------------------------------------------------------
-template <int FMT, int BITS, int MODE, int NP>
-__global__ void __launch_bounds__(256) k_tile(CastParams p) {
-  __shared__ float sh[32];
-  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
-  const int64_t gi = blockIdx.x;
+template <int NP>
+__device__ __forceinline__ void tile_load(const CastParams& p, int64_t gi, uint32_t (&w)[NP][8]) {
   const Rect R = group_rect(p, gi);
   const int64_t ppr = (R.c1 - R.c0) / 16, npc = (R.r1 - R.r0) * ppr;
-  uint32_t w[NP][8];
-  uint32_t M = 0xFF80FF80u, m = 0x7F807F80u;  // (-inf, -inf), (+inf, +inf)
 #pragma unroll
   for (int j = 0; j < NP; ++j) {
-    int64_t pc = threadIdx.x + 256 * j;
-    if (pc < npc) {
-      int64_t r = R.r0 + pc / ppr, c = R.c0 + (pc % ppr) * 16;
-      ld_v8(p.w + r * p.cols + c, w[j]);
-      if (MODE != MODE_GIVEN) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { M = hmax2(M, w[j][k]); m = hmin2(m, w[j][k]); }
-      }
-    }
+    const int64_t pc = threadIdx.x + 256 * j;
+    if (pc < npc) ld_v8(p.w + (R.r0 + pc / ppr) * p.cols + R.c0 + (pc % ppr) * 16, w[j]);
   }
+}
+
+template <int FMT, int BITS, int MODE, int NP>
+__device__ __forceinline__ void tile_process(const CastParams& p, int64_t gi, const uint32_t (&w)[NP][8], float* sh) {
+  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+  const Rect R = group_rect(p, gi);
+  const int64_t ppr = (R.c1 - R.c0) / 16, npc = (R.r1 - R.r0) * ppr;
   ElemQ e;
   float s_store = 0.f, zp_store = 0.f;
   if (MODE != MODE_GIVEN) {
+    uint32_t M = 0xFF80FF80u, m = 0x7F807F80u;  // (-inf, -inf), (+inf, +inf)
+#pragma unroll
+    for (int j = 0; j < NP; ++j)
+      if (threadIdx.x + 256 * j < npc) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { M = hmax2(M, w[j][k]); m = hmin2(m, w[j][k]); }
+      }
     float mx = fmaxf(bf_lo(M), bf_hi(M)), mn = fminf(bf_lo(m), bf_hi(m));
     const int64_t h = R.r1 - R.r0, wd = R.c1 - R.c0;
     if (p.a.strategy == LLMC_STRAT_BLOCK && (h < p.a.bh || wd < p.a.bw)) { mn = fminf(mn, 0.f); mx = fmaxf(mx, 0.f); }
@@ -839,14 +843,100 @@ __global__ void __launch_bounds__(256) k_tile(CastParams p) {
   const float qmin = p.a.qmin(), qmax = p.a.qmax();
 #pragma unroll
   for (int j = 0; j < NP; ++j) {
-    int64_t pc = threadIdx.x + 256 * j;
+    const int64_t pc = threadIdx.x + 256 * j;
     if (pc >= npc) break;
-    int64_t r = R.r0 + pc / ppr, c = R.c0 + (pc % ppr) * 16;
+    const int64_t el = (R.r0 + pc / ppr) * p.cols + R.c0 + (pc % ppr) * 16;
     uint32_t o[4];
     if (FMT == LLMC_FMT_NVFP4 || (MODE == MODE_GIVEN && g.f32q))
       quant_group<FMT, BITS, true, MODE == MODE_GIVEN, 8>(w[j], g, qmin, qmax, o);
     else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, 8>(w[j], g, qmin, qmax, o);
-    int64_t el = r * p.cols + c;
+    if (OUT4) *(uint2*)((uint8_t*)p.out + el / 2) = make_uint2(o[0], o[1]);
+    else st_v4((uint8_t*)p.out + el, o);
+  }
+}
+
+template <int FMT, int BITS, int MODE, int NP, bool PF>
+__global__ void __launch_bounds__(256, PF ? 2 : 1) k_tile(CastParams p, int64_t ng) {
+  __shared__ float sh[32];
+  int64_t gi = blockIdx.x;
+  if (!PF) {
+    for (; gi < ng; gi += gridDim.x) {
+      uint32_t w[NP][8];
+      tile_load<NP>(p, gi, w);
+      tile_process<FMT, BITS, MODE, NP>(p, gi, w, sh);
+    }
+    return;
+  }
+  uint32_t a[NP][8], b[NP][8];
+  if (gi < ng) tile_load<NP>(p, gi, a);
+  while (gi < ng) {
+    int64_t nx = gi + gridDim.x;
+    if (nx < ng) tile_load<NP>(p, nx, b);
+    tile_process<FMT, BITS, MODE, NP>(p, gi, a, sh);
+    gi = nx;
+    if (gi >= ng) break;
+    nx = gi + gridDim.x;
+    if (nx < ng) tile_load<NP>(p, nx, a);
+    tile_process<FMT, BITS, MODE, NP>(p, gi, b, sh);
+    gi = nx;
+  }
+}
+
+// ------------------------------------------------------------------------
+// k_rowwarp: CHANNEL rows of up to 4096 columns, one warp per row, NPL
+// 16-value pieces per lane (32-byte loads, consecutive across the warp);
+// shuffles only, no CTA barrier, so many rows are in flight per SM.
+// ------------------------------------------------------------------------
+template <int FMT, int BITS, int MODE, int NPL>
+__global__ void __launch_bounds__(256) k_rowwarp(CastParams p) {
+  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= p.rows) return;  // whole warp
+  const int64_t pieces = p.cols / 16;
+  const uint16_t* src = p.w + row * p.cols;
+  uint32_t w[NPL][8];
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    const int64_t pc = lane + 32 * j;
+    if (pc < pieces) ld_v8(src + pc * 16, w[j]);
+  }
+  ElemQ e;
+  float s_store = 0.f, zp_store = 0.f;
+  if (MODE != MODE_GIVEN) {
+    uint32_t M = 0xFF80FF80u, m = 0x7F807F80u;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j)
+      if (lane + 32 * j < pieces) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { M = hmax2(M, w[j][k]); m = hmin2(m, w[j][k]); }
+      }
+    float mx = fmaxf(bf_lo(M), bf_hi(M)), mn = fminf(bf_lo(m), bf_hi(m));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if (MODE == MODE_STATS) {
+      if (lane == 0) { p.min_out[row] = f_to_bf16(mn); p.max_out[row] = f_to_bf16(mx); }
+      return;
+    }
+    e = make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
+    if (lane == 0) store_scale<FMT>(p, row, s_store, zp_store);
+  } else {
+    e = make_elemq_given<FMT>(p, row);
+  }
+  const GQ g = to_gq(e);
+  const float qmin = p.a.qmin(), qmax = p.a.qmax();
+#pragma unroll
+  for (int j = 0; j < NPL; ++j) {
+    const int64_t pc = lane + 32 * j;
+    if (pc >= pieces) break;
+    const int64_t el = row * p.cols + pc * 16;
+    uint32_t o[4];
+    if (FMT == LLMC_FMT_NVFP4 || (MODE == MODE_GIVEN && g.f32q))
+      quant_group<FMT, BITS, true, MODE == MODE_GIVEN, 8>(w[j], g, qmin, qmax, o);
+    else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, 8>(w[j], g, qmin, qmax, o);
     if (OUT4) *(uint2*)((uint8_t*)p.out + el / 2) = make_uint2(o[0], o[1]);
     else st_v4((uint8_t*)p.out + el, o);
   }
@@ -961,12 +1051,22 @@ static bool launch_tile(const CastParams& p, int64_t pieces, cudaStream_t st) {
   if constexpr (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) {
     return false;  // FP4 formats only come with group strategies
   } else {
-    const int ng = n_groups(p);
+    const int64_t ng = n_groups(p);
     if (ng <= 0) return true;
-    if (pieces <= 256) k_tile<FMT, BITS, MODE, 1><<<ng, 256, 0, st>>>(p);
-    else if (pieces <= 512) k_tile<FMT, BITS, MODE, 2><<<ng, 256, 0, st>>>(p);
-    else if (pieces <= 1024) k_tile<FMT, BITS, MODE, 4><<<ng, 256, 0, st>>>(p);
-    else if (pieces <= 2048) k_tile<FMT, BITS, MODE, 8><<<ng, 256, 0, st>>>(p);
+    if (p.a.strategy == LLMC_STRAT_CHANNEL && pieces <= 256) {
+      const unsigned blocks = (unsigned)((p.rows * 32 + 255) / 256);
+      if (pieces <= 32) k_rowwarp<FMT, BITS, MODE, 1><<<blocks, 256, 0, st>>>(p);
+      else if (pieces <= 64) k_rowwarp<FMT, BITS, MODE, 2><<<blocks, 256, 0, st>>>(p);
+      else if (pieces <= 128) k_rowwarp<FMT, BITS, MODE, 4><<<blocks, 256, 0, st>>>(p);
+      else k_rowwarp<FMT, BITS, MODE, 8><<<blocks, 256, 0, st>>>(p);
+      llmc::note_launch();
+      return true;
+    }
+    const unsigned pg = (unsigned)std::min<int64_t>(ng, 148 * 2);
+    if (pieces <= 256) k_tile<FMT, BITS, MODE, 1, true><<<pg, 256, 0, st>>>(p, ng);
+    else if (pieces <= 512) k_tile<FMT, BITS, MODE, 2, true><<<pg, 256, 0, st>>>(p, ng);
+    else if (pieces <= 1024) k_tile<FMT, BITS, MODE, 4, true><<<pg, 256, 0, st>>>(p, ng);
+    else if (pieces <= 2048) k_tile<FMT, BITS, MODE, 8, false><<<(unsigned)std::min<int64_t>(ng, 148 * 8), 256, 0, st>>>(p, ng);
     else return false;
   }
   llmc::note_launch();

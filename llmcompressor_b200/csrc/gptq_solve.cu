@@ -269,34 +269,48 @@ __global__ void k_xt_to_ut(const float* __restrict__ Xt, float* __restrict__ Ut,
 constexpr int PB = 128;
 constexpr int PLD = PB + 1;  // padded row stride of the shared-memory blocks
 // 16 warps: warp w walks rows (w, w+16, ...), its lanes walk the columns of a row.
-// Cholesky factor and inverse of one 32x32 diagonal sub-block held by one
-// warp in registers: lane i holds row i of the block in a[] on entry and row
-// i of L on exit; x[] returns column i of L^-1.  Rows/columns >= sz are
-// left untouched (zero on entry).
-__device__ __forceinline__ void warp_chol_inv32(float (&a)[32], float (&x)[32], int lane, int sz, bool& bad) {
+// Cholesky factor and inverse of the 32x32 diagonal sub-block at (o, o) of S
+// (row stride PLD) by one warp, written back as L into S and as L^-1 into X.
+// Lane i keeps a window of its row, a[m] = S[o+i][o+j+m], that shifts left as
+// the column j advances, so the loop body is the same for every j and the
+// code stays small (a fully unrolled 32x32 factorisation does not fit the
+// instruction cache).  The inverse is the same kind of loop: lane c carries
+// the right-hand side of column c of L^-1 in a shifting window t[].
+__device__ __forceinline__ void warp_chol_inv32(float* S, float* X, int o, int lane, int sz, bool& bad) {
+  float a[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (j < sz) {
-      float p = __shfl_sync(0xffffffffu, a[j], j);
-      if (!(p > 0.0f)) { bad = true; p = 1.0f; }
-      const float piv = sqrtf(p);
-      if (lane == j) a[j] = piv;
-      else if (lane > j) a[j] = __fdiv_rn(a[j], piv);
+  for (int l = 0; l < 32; ++l) a[l] = (lane < sz && l <= lane) ? S[(o + lane) * PLD + o + l] : 0.f;
+  for (int j = 0; j < sz; ++j) {
+    float p = __shfl_sync(0xffffffffu, a[0], j);
+    if (!(p > 0.0f)) { bad = true; p = 1.0f; }
+    const float piv = sqrtf(p);
+    float a0 = a[0];
+    if (lane == j) a0 = piv;
+    else if (lane > j) a0 = __fdiv_rn(a0, piv);
+    if (lane >= j && lane < sz) S[(o + lane) * PLD + o + j] = a0;  // column j of L
 #pragma unroll
-      for (int m = j + 1; m < 32; ++m) {
-        const float lmj = __shfl_sync(0xffffffffu, a[j], m);
-        if (lane >= m) a[m] -= a[j] * lmj;
-      }
+    for (int m = 1; m < 32; ++m) {
+      const float lmj = __shfl_sync(0xffffffffu, a0, min(j + m, 31));
+      if (lane >= j + m) a[m] -= a0 * lmj;
     }
+#pragma unroll
+    for (int m = 0; m < 31; ++m) a[m] = a[m + 1];
+    a[31] = 0.f;
   }
-  // column `lane` of X = L^-1 by forward substitution over the rows of L
+  __syncwarp();
+  // column `lane` of X = L^-1 by forward substitution: t[m] = rhs of row j + m
+  float t[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float sum = (j == lane) ? 1.0f : 0.0f;
+  for (int m = 0; m < 32; ++m) t[m] = (m == lane) ? 1.0f : 0.0f;
+  for (int j = 0; j < sz; ++j) {
+    const float xj = __fdiv_rn(t[0], S[(o + j) * PLD + o + j]);
+    if (lane < sz) X[(o + j) * PLD + o + lane] = (j >= lane) ? xj : 0.0f;
 #pragma unroll
-    for (int l = 0; l < j; ++l) sum -= __shfl_sync(0xffffffffu, a[l], j) * x[l];
-    const float ljj = __shfl_sync(0xffffffffu, a[j], j);
-    x[j] = (j >= lane && j < sz) ? __fdiv_rn(sum, ljj) : 0.0f;
+    for (int m = 1; m < 32; ++m)
+      if (j + m < sz) t[m] -= S[(o + j + m) * PLD + o + j] * xj;
+#pragma unroll
+    for (int m = 0; m < 31; ++m) t[m] = t[m + 1];
+    t[31] = 0.f;
   }
 }
 
@@ -337,19 +351,9 @@ __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_
   for (int kb = 0; kb < nsub; ++kb) {
     const int o = kb * SB, sz = min(SB, n - o);
     if (warp == 0) {
-      float a[32], x[32];
-#pragma unroll
-      for (int l = 0; l < 32; ++l) a[l] = (lane < sz && l <= lane) ? S[(o + lane) * PLD + o + l] : 0.f;
       bool b = false;
-      warp_chol_inv32(a, x, lane, sz, b);
+      warp_chol_inv32(S, X, o, lane, sz, b);
       if (b) bad = 1;
-      if (lane < sz) {
-#pragma unroll
-        for (int l = 0; l < 32; ++l) {
-          if (l <= lane) S[(o + lane) * PLD + o + l] = a[l];
-          if (l >= lane && l < sz) X[(o + l) * PLD + o + lane] = x[l];
-        }
-      }
     }
     __syncthreads();
     const int r0 = o + sz, rem = n - r0;
@@ -401,31 +405,61 @@ __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_
     __syncthreads();
   }
   if (t == 0 && bad && status) atomicExch(status, LLMC_ENOT_PD);
-  // off-diagonal blocks of the inverse: X_ij = -X_ii * sum_{k=j}^{i-1} L_ik X_kj, by block row
+  // off-diagonal blocks of the inverse, by block row bi:
+  //   T = L[rows of bi, :oi] * X[:oi, :oi],  X[rows of bi, :oi] = -X_ii * T.
+  // A thread holds 2 rows x 3 columns of the block row (16 warps x 32 lanes);
+  // X is zero above its diagonal, so every sum runs over the full range.
   for (int bi = 1; bi < nsub; ++bi) {
     const int oi = bi * SB, szi = min(SB, n - oi);
-    float v[8];
-    int cnt = 0;
-    for (int e = t; e < szi * oi; e += NT, ++cnt) {  // T = L[rows of bi, :oi] * X[:oi, :oi]
-      const int r = oi + e / oi, c = e % oi;
-      float s = 0.f;
-      for (int k = c; k < oi; ++k) s = fmaf(S[r * PLD + k], X[k * PLD + c], s);
-      v[cnt] = s;
+    const int r0 = warp, r1 = warp + NW;
+    float acc[2][3];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int v = 0; v < 3; ++v) acc[u][v] = 0.f;
+    for (int k = 0; k < oi; ++k) {
+      const float l0 = S[(oi + r0) * PLD + k], l1 = S[(oi + r1) * PLD + k];
+#pragma unroll
+      for (int v = 0; v < 3; ++v) {
+        const int c = lane + 32 * v;
+        const float xk = (c < oi) ? X[k * PLD + c] : 0.f;
+        acc[0][v] = fmaf(l0, xk, acc[0][v]);
+        acc[1][v] = fmaf(l1, xk, acc[1][v]);
+      }
     }
     __syncthreads();
-    cnt = 0;
-    for (int e = t; e < szi * oi; e += NT, ++cnt) X[(oi + e / oi) * PLD + e % oi] = v[cnt];
-    __syncthreads();
-    cnt = 0;
-    for (int e = t; e < szi * oi; e += NT, ++cnt) {  // X[rows of bi, :oi] = -X_ii * T
-      const int r = oi + e / oi, c = e % oi;
-      float s = 0.f;
-      for (int m = oi; m <= r; ++m) s = fmaf(X[r * PLD + m], X[m * PLD + c], s);
-      v[cnt] = -s;
+#pragma unroll
+    for (int v = 0; v < 3; ++v) {
+      const int c = lane + 32 * v;
+      if (c < oi) {
+        if (r0 < szi) X[(oi + r0) * PLD + c] = acc[0][v];
+        if (r1 < szi) X[(oi + r1) * PLD + c] = acc[1][v];
+      }
     }
     __syncthreads();
-    cnt = 0;
-    for (int e = t; e < szi * oi; e += NT, ++cnt) X[(oi + e / oi) * PLD + e % oi] = v[cnt];
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int v = 0; v < 3; ++v) acc[u][v] = 0.f;
+    for (int m = 0; m < szi; ++m) {
+      const float x0 = X[(oi + r0) * PLD + oi + m], x1 = X[(oi + r1) * PLD + oi + m];
+#pragma unroll
+      for (int v = 0; v < 3; ++v) {
+        const int c = lane + 32 * v;
+        const float tm = (c < oi) ? X[(oi + m) * PLD + c] : 0.f;
+        acc[0][v] = fmaf(x0, tm, acc[0][v]);
+        acc[1][v] = fmaf(x1, tm, acc[1][v]);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int v = 0; v < 3; ++v) {
+      const int c = lane + 32 * v;
+      if (c < oi) {
+        if (r0 < szi) X[(oi + r0) * PLD + c] = -acc[0][v];
+        if (r1 < szi) X[(oi + r1) * PLD + c] = -acc[1][v];
+      }
+    }
     __syncthreads();
   }
   for (int i = warp; i < PB; i += NW)
@@ -626,11 +660,11 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
         float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
 #pragma unroll
         for (int ii = 0; ii < SUB; ++ii) {
-          const float* u = U1 + (s0 + ii) * QB + j;
-          acc0 = fmaf(e[ii], u[0], acc0);
-          acc1 = fmaf(e[ii], u[1], acc1);
-          acc2 = fmaf(e[ii], u[2], acc2);
-          acc3 = fmaf(e[ii], u[3], acc3);
+          const float4 u = *(const float4*)(U1 + (s0 + ii) * QB + j);  // one broadcast 16-byte read
+          acc0 = fmaf(e[ii], u.x, acc0);
+          acc1 = fmaf(e[ii], u.y, acc1);
+          acc2 = fmaf(e[ii], u.z, acc2);
+          acc3 = fmaf(e[ii], u.w, acc3);
         }
         QS[t * QS_LD + j] -= acc0;
         QS[t * QS_LD + j + 1] -= acc1;
