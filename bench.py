@@ -208,6 +208,8 @@ def run_ours(args, rank, world, device):
     h_flops = hessian_flops(dims, len(my_chunks) * CHUNK) * args.steps
     h_tflops = h_flops / (h_ms * 1e-3) / 1e12
     casts = measure_casts([weights[i] for i in range(min(L, 4))]) if rank == 0 else None
+    del weights, pool
+    mfree = modelfree_layers(device) if rank == 0 else None
 
     out = {
         "ms": ms,
@@ -218,6 +220,7 @@ def run_ours(args, rank, world, device):
         "hessian_ms_per_step": h_ms / args.steps,
         "hessian_flops_per_launch": hessian_flops({"x": CFG["hidden"]}, CHUNK),
         "casts": casts,
+        "modelfree": mfree,
         "peaks": pk,
     }
 
@@ -261,6 +264,80 @@ def measure_casts(layers, reps: int = 3) -> dict:
         res[name] = {"gbs": (in_bytes + out_bytes) / (ms * 1e-3) / 1e9, "ms": ms, "bytes": in_bytes + out_bytes,
                      "launches_per_pass": len(ws)}
     return res
+
+
+def modelfree_layers(device, reps: int = 3) -> dict:
+    """Device-resident model-free passes at BASELINE configs[3] / configs[4]
+    shapes, one layer (or expert sample) each, timed with CUDA events:
+
+    * C4: one Llama-3-70B-shaped layer (q/k/v/o 8192-wide, gate/up/down 28672),
+      ~N(0, 0.02) with 0.1% of values x50, NVFP4A16 with fused q/k/v and
+      gate/up global scales: absmax pass + quantize/pack pass, 4.5625 B per
+      weight (2 B absmax read + 2.5625 B quantize pass).
+    * C5: DeepSeek-V3-shaped MoE expert matrices (32 experts x gate/up/down,
+      7168 x 2048), rows 0.02 * Student-t(4), FP8_BLOCK (3.0001 B/weight) and
+      MXFP4A16 (2.53125 B/weight), single pass."""
+    from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
+
+    from llmcompressor_b200 import ops
+
+    g = torch.Generator(device=device).manual_seed(3)
+
+    def normal_outliers(r, c):
+        w = 0.02 * torch.randn(r, c, device=device, generator=g)
+        m = torch.rand(r, c, device=device, generator=g) < 0.001
+        return torch.where(m, w * 50, w).to(torch.bfloat16)
+
+    def student_t(r, c):
+        z = torch.randn(r, c, device=device, generator=g)
+        chi = torch.distributions.Chi2(torch.tensor(4.0, device=device)).sample((r, 1))
+        return (0.02 * z / torch.sqrt(chi / 4.0)).to(torch.bfloat16)
+
+    out = {}
+    h, inter = 8192, 28672
+    c4 = {"q": normal_outliers(h, h), "k": normal_outliers(1024, h), "v": normal_outliers(1024, h),
+          "o": normal_outliers(h, h), "gate": normal_outliers(inter, h), "up": normal_outliers(inter, h),
+          "down": normal_outliers(h, inter)}
+    nv = preset_name_to_scheme("NVFP4A16", ["Linear"]).weights
+    sets = [["q", "k", "v"], ["o"], ["gate", "up"], ["down"]]
+
+    def c4_pass():
+        for st in sets:
+            gs = ops.fused_global_scale([c4[n] for n in st])
+            for n in st:
+                ops.modelfree_quantize(c4[n], nv, gs)
+
+    nweights = sum(w.numel() for w in c4.values())
+    c4_pass()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        c4_pass()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    out["C4_llama70b_layer_NVFP4A16"] = {"weights": nweights, "ms": ms,
+                                         "gbs": nweights * 4.5625 / (ms * 1e-3) / 1e9,
+                                         "bytes_per_weight": 4.5625}
+    del c4
+    experts = [student_t(2048, 7168) for _ in range(64)] + [student_t(7168, 2048) for _ in range(32)]
+    for name, bpw in (("FP8_BLOCK", 3.0001), ("MXFP4A16", 2.53125)):
+        a = preset_name_to_scheme(name, ["Linear"]).weights
+        for w in experts[:2]:
+            ops.modelfree_quantize(w, a)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            for w in experts:
+                ops.modelfree_quantize(w, a)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        n = sum(w.numel() for w in experts)
+        out[f"C5_dsv3_32experts_{name}"] = {"weights": n, "ms": ms, "gbs": n * bpw / (ms * 1e-3) / 1e9,
+                                            "bytes_per_weight": bpw}
+    return out
 
 
 def run_e2e(args, rank, world, device, specs, dims, qa, my_chunks, alpha):
@@ -569,6 +646,8 @@ def main():
         "hessian_tflops": res["hessian_tflops"],
         "casts": ({k: {"gbs": v["gbs"], "frac": v["gbs"] / pk["hbm_gbs"]} for k, v in res["casts"].items()}
                   if res["casts"] else None),
+        "modelfree": ({k: {"gbs": v["gbs"], "frac": v["gbs"] / pk["hbm_gbs"], "ms": v["ms"], "weights": v["weights"]}
+                       for k, v in res["modelfree"].items()} if res["modelfree"] else None),
         "gpu_launches": res["launches"],
         "clocks": res["clocks"],
     }

@@ -9,12 +9,14 @@
 //
 // Design (one persistent CTA per SM, 192 threads, warp-specialised):
 //   warp 0      TMA producer: X tiles (64 tokens x 64 features, 128B swizzle)
-//               into a 3-stage ring; both operands are MN-major views of X.
+//               into a 4-stage ring (192 KB: four stages keep the tensor
+//               cores fed, three measurably starve them); both operands are
+//               MN-major views of X.
 //   warp 1      allocates 512 TMEM columns and issues tcgen05.mma
 //               (M=128, N=256, K=16, bf16 -> f32) for output tile 128x256,
 //               double-buffered accumulators (2 x 256 columns).
 //   warps 2..5  epilogue: tcgen05.ld 32x32 boxes, x alpha, stage in swizzled
-//               smem, TMA reduce-add into H -- the box itself and, for boxes
+//               smem (one buffer per warp), TMA reduce-add into H -- the box itself and, for boxes
 //               strictly below the diagonal, its transpose (the mirror).
 // Only tiles that touch the lower triangle are computed; boxes entirely
 // above the diagonal inside those tiles are skipped (their values arrive as
@@ -32,16 +34,16 @@ namespace hess {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;   // 16 KB: two 64-feature chunks
 constexpr int B_BYTES = BN * BK * 2;   // 32 KB: four 64-feature chunks
 constexpr int CHUNK_BYTES = 64 * BK * 2;  // 8 KB: one TMA box (64 features x 64 tokens)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_WARPS = 4;
 constexpr int EPI_BOX_BYTES = 32 * 32 * 4;                 // 4 KB fp32 32x32 box
-constexpr int EPI_WARP_BYTES = 2 * 2 * EPI_BOX_BYTES;      // 2 buffers x (direct + mirror)
-constexpr int SMEM_STAGES = STAGES * STAGE_BYTES;          // 144 KB
-constexpr int SMEM_EPI = EPI_WARPS * EPI_WARP_BYTES;       // 64 KB
+constexpr int EPI_WARP_BYTES = 2 * EPI_BOX_BYTES;          // one buffer: direct + mirror box
+constexpr int SMEM_STAGES = STAGES * STAGE_BYTES;          // 192 KB
+constexpr int SMEM_EPI = EPI_WARPS * EPI_WARP_BYTES;       // 32 KB
 constexpr int SMEM_BAR = 256;
 constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_EPI + SMEM_BAR + 1024;  // + alignment slack
 constexpr int THREADS = 192;
@@ -187,7 +189,6 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
     uint8_t* wbuf = epi + (warp - 2) * EPI_WARP_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
-    int buf = 0;
     for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
       int bi, bj;
       tile_coords(t, p.mb, bi, bj);
@@ -201,9 +202,9 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * c), r);
         tmem_ld_wait();
-        uint8_t* dbox = wbuf + buf * (2 * EPI_BOX_BYTES);
+        uint8_t* dbox = wbuf;
         uint8_t* mbox = dbox + EPI_BOX_BYTES;
-        if (lane == 0) bulk_wait_read<1>();  // the group that last used this buffer has been read
+        if (lane == 0) bulk_wait_read<0>();  // the previous box's reduce has read the buffer
         __syncwarp();
         // direct box: row `lane`, 32 columns, 128B-swizzled rows
 #pragma unroll
@@ -230,7 +231,6 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
           if (mirror) tma_reduce_add_2d(&hmap, smem_u32(mbox), gr, gc);
           bulk_commit();
         }
-        buf ^= 1;
       }
       tc_fence_before();
       __syncwarp();
