@@ -276,7 +276,8 @@ def modelfree_layers(device, reps: int = 3) -> dict:
       weight (2 B absmax read + 2.5625 B quantize pass).
     * C5: DeepSeek-V3-shaped MoE expert matrices (32 experts x gate/up/down,
       7168 x 2048), rows 0.02 * Student-t(4), FP8_BLOCK (3.0001 B/weight) and
-      MXFP4A16 (2.53125 B/weight), single pass."""
+      MXFP4A16 (2.53125 B/weight), single pass, the expert set through the
+      batched launch (48 tensors per launch)."""
     from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
 
     from llmcompressor_b200 import ops
@@ -324,13 +325,11 @@ def modelfree_layers(device, reps: int = 3) -> dict:
     experts = [student_t(2048, 7168) for _ in range(64)] + [student_t(7168, 2048) for _ in range(32)]
     for name, bpw in (("FP8_BLOCK", 3.0001), ("MXFP4A16", 2.53125)):
         a = preset_name_to_scheme(name, ["Linear"]).weights
-        for w in experts[:2]:
-            ops.modelfree_quantize(w, a)
+        ops.modelfree_quantize_batch(experts[:2], a)
         torch.cuda.synchronize()
         e0.record()
         for _ in range(reps):
-            for w in experts:
-                ops.modelfree_quantize(w, a)
+            ops.modelfree_quantize_batch(experts, a)  # the expert set in batched launches
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / reps
@@ -501,7 +500,8 @@ def cpu_sample(steps: int, warmup: int) -> dict:
 def run_micro(args) -> None:
     """One kernel on a small case (profiling captures and per-kernel timing):
     hessian: H += alpha X^T X, X (tokens x d); gptq: factor + block loop of
-    one (rows x d) weight; cast: model-free pass of --scheme over a (rows x d) weight."""
+    one (rows x d) weight; cast: model-free pass of --scheme over a (rows x d) weight;
+    castbatch: --tensors such weights through the batched launch."""
     from llmcompressor_b200 import gptq, ops
 
     dev = torch.device("cuda:0")
@@ -529,6 +529,17 @@ def run_micro(args) -> None:
             return gptq.quantize_with_inverse(w, qa, inv, scale, zp)
 
         work, unit = None, "ms"
+    elif args.micro == "castbatch":
+        from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
+
+        qa = preset_name_to_scheme(args.scheme, ["Linear"]).weights
+        ws = [(0.02 * torch.randn(rows, d, device=dev, generator=g)).to(torch.bfloat16) for _ in range(args.tensors)]
+        gss = [ops.fused_global_scale([w]) for w in ws] if args.scheme == "NVFP4A16" else None
+        outs = ops.modelfree_quantize_batch(ws, qa, gss)
+        nbytes = sum(w.numel() * 2 for w in ws) + sum(t.numel() * t.element_size() for o in outs
+                                                      for k, t in o.items() if t.is_cuda and k != "weight_global_scale")
+        fn = lambda: ops.modelfree_quantize_batch(ws, qa, gss)  # noqa: E731
+        work, unit = nbytes / 1e9, "GB/s"
     else:
         from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
 
@@ -557,12 +568,13 @@ def run_micro(args) -> None:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--micro", choices=["hessian", "gptq", "hinv", "cast"], default=None,
+    ap.add_argument("--micro", choices=["hessian", "gptq", "hinv", "cast", "castbatch"], default=None,
                     help="time one kernel on a small case instead of the model benchmark")
     ap.add_argument("--d", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--scheme", default="W4A16", choices=list(CAST_SCHEMES), help="format of --micro cast")
+    ap.add_argument("--tensors", type=int, default=32, help="tensors of --micro castbatch")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=3)

@@ -143,6 +143,23 @@ int llmc_modelfree_quantize(const void* w_bf16, int64_t rows, int64_t cols, cons
                             const float* global_scale, int out_format, void* packed_out, void* scale_out,
                             void* zp_out, void* stream);
 
+/* Several tensors through llmc_modelfree_quantize in as few launches as
+ * possible (all with the same args and format): a batched launch for up to 48
+ * tensors at a time, each with its own pointers; tensors whose shape or
+ * alignment the batched kernels do not take get their own launch.  Used for
+ * MoE expert sets and whole shards (S/entrypoints/model_free/process.py:104-121
+ * per tensor). */
+typedef struct {
+  const void* w;              /* bf16 (rows x cols) */
+  int64_t rows, cols;
+  const float* global_scale;  /* NVFP4: float32 scalar; else NULL */
+  void* out;                  /* as llmc_modelfree_quantize */
+  void* scale_out;
+  void* zp_out;               /* asymmetric only */
+} LlmcCastJob;
+int llmc_modelfree_quantize_batch(const LlmcCastJob* jobs, int njobs, const LlmcQuantArgs* args, int out_format,
+                                  void* stream);
+
 /* pack_to_int32(zero_point, num_bits, packed_dim=0)
  * (CT/compressors/pack_quantized/helpers.py:20-89): int8 (rows, groups) ->
  * int32 (ceil(rows*bits/32), groups). */

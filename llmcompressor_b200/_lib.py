@@ -53,6 +53,20 @@ class QuantArgs(ctypes.Structure):
 _lib = None
 _lock = threading.Lock()
 
+class CastJob(ctypes.Structure):
+    """``LlmcCastJob`` (include/llmc_b200.h)."""
+
+    _fields_ = [
+        ("w", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("global_scale", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("scale_out", ctypes.c_void_p),
+        ("zp_out", ctypes.c_void_p),
+    ]
+
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int
@@ -65,6 +79,7 @@ _SIGS = {
     "llmc_status_string": [_I32],
     "llmc_observe_minmax": [_P, _I64, _I64, _QA, _P, _P, _P],
     "llmc_observe_mse_workspace_size": [_I64, _I64, _QA, _P],
+    "llmc_modelfree_quantize_batch": [ctypes.POINTER(CastJob), _I32, _QA, _I32, _P],
     "llmc_observe_mse": [_P, _I64, _I64, _QA, ctypes.c_float, _I32, ctypes.c_float, ctypes.c_float, _P, _P, _P, _P],
     "llmc_absmax_accumulate": [_P, _I64, _P, _P],
     "llmc_global_scale": [_P, _P, _P],

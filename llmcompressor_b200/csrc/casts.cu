@@ -14,6 +14,8 @@
 // STATS (min/max only) and GIVEN (quantize + pack with stored qparams).
 #include "llmc_common.cuh"
 
+#include <string.h>
+
 #include <algorithm>
 #include <atomic>
 
@@ -943,6 +945,102 @@ __global__ void __launch_bounds__(256) k_rowwarp(CastParams p) {
 }
 
 // ------------------------------------------------------------------------
+// Batched launches: many tensors (model-free shards, MoE experts) in one
+// persistent launch.  The job table travels in the kernel parameters; a work
+// unit is a 1024-value span (group strategies) or a parameter group (CHANNEL
+// rows, BLOCK tiles), numbered across the jobs.
+// ------------------------------------------------------------------------
+constexpr int kBatchMax = 48;
+struct CastJob {
+  const uint16_t* w;
+  int64_t rows, cols;
+  int64_t first;  // first work unit of this job
+  const float* gs;
+  void* out;
+  void* scale_out;
+  int8_t* zp_out;
+};
+struct CastBatch {
+  CastParams base;  // arguments, format and mode shared by the jobs
+  int njobs;
+  int64_t units;
+  CastJob job[kBatchMax];
+};
+
+__device__ __forceinline__ int find_job(const CastBatch& b, int64_t u) {
+  int lo = 0, hi = b.njobs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (b.job[mid].first <= u) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+__device__ __forceinline__ CastParams job_params(const CastBatch& b, int j) {
+  CastParams p = b.base;
+  const CastJob& jb = b.job[j];
+  p.w = jb.w; p.rows = jb.rows; p.cols = jb.cols; p.gs = jb.gs;
+  p.out = jb.out; p.scale_out = jb.scale_out; p.zp_out = jb.zp_out;
+  return p;
+}
+
+template <int FMT, int BITS, int GROUP>
+__global__ void __launch_bounds__(256, 3) k_stream_batch(const __grid_constant__ CastBatch b) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  int64_t it = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  uint32_t a[16], c[16];
+  int ja = 0, jc = 0;
+  int64_t ea = 0, ec = 0;
+  auto load = [&](int64_t u, uint32_t* buf, int& j, int64_t& e0) {
+    j = find_job(b, u);
+    const CastJob& jb = b.job[j];
+    e0 = ((u - jb.first) << 10) + lane * 32;
+    if (e0 < jb.rows * jb.cols) {
+      ld_v8(jb.w + e0, buf);
+      ld_v8(jb.w + e0 + 16, buf + 8);
+    }
+  };
+  if (it < b.units) load(it, a, ja, ea);
+  while (it < b.units) {
+    int64_t nx = it + nwarps;
+    if (nx < b.units) load(nx, c, jc, ec);
+    {
+      const CastParams p = job_params(b, ja);
+      stream_span<FMT, BITS, GROUP, MODE_FUSED>(p, ea, ea < p.rows * p.cols, a);
+    }
+    it = nx;
+    if (it >= b.units) break;
+    nx = it + nwarps;
+    if (nx < b.units) load(nx, a, ja, ea);
+    {
+      const CastParams p = job_params(b, jc);
+      stream_span<FMT, BITS, GROUP, MODE_FUSED>(p, ec, ec < p.rows * p.cols, c);
+    }
+    it = nx;
+  }
+}
+
+template <int FMT, int BITS, int NP>
+__global__ void __launch_bounds__(256, 2) k_tile_batch(const __grid_constant__ CastBatch b) {
+  __shared__ float sh[32];
+  int64_t gi = blockIdx.x;
+  uint32_t a[NP][8], c[NP][8];
+  int ja = 0, jc = 0;
+  if (gi < b.units) { ja = find_job(b, gi); const CastParams p = job_params(b, ja); tile_load<NP>(p, gi - b.job[ja].first, a); }
+  while (gi < b.units) {
+    int64_t nx = gi + gridDim.x;
+    if (nx < b.units) { jc = find_job(b, nx); const CastParams p = job_params(b, jc); tile_load<NP>(p, nx - b.job[jc].first, c); }
+    { const CastParams p = job_params(b, ja); tile_process<FMT, BITS, MODE_FUSED, NP>(p, gi - b.job[ja].first, a, sh); }
+    gi = nx;
+    if (gi >= b.units) break;
+    nx = gi + gridDim.x;
+    if (nx < b.units) { ja = find_job(b, nx); const CastParams p = job_params(b, ja); tile_load<NP>(p, nx - b.job[ja].first, a); }
+    { const CastParams p = job_params(b, jc); tile_process<FMT, BITS, MODE_FUSED, NP>(p, gi - b.job[jc].first, c, sh); }
+    gi = nx;
+  }
+}
+
+// ------------------------------------------------------------------------
 // small kernels
 // ------------------------------------------------------------------------
 __global__ void k_absmax(const uint16_t* w, int64_t n, float* out) {
@@ -1180,6 +1278,89 @@ static int launch(const CastParams& p, cudaStream_t st) {
   }
 }
 
+// One batched launch for jobs[0..n) that all meet the fast kernels' shape
+// and alignment rules (the caller checked); false if the strategy has no
+// batched kernel.
+template <int FMT, int BITS>
+static bool launch_batch_fmt(CastBatch& b, cudaStream_t st) {
+  const QArgs& a = b.base.a;
+  int64_t units = 0;
+  int64_t pieces = 0;
+  for (int i = 0; i < b.njobs; ++i) {
+    CastJob& j = b.job[i];
+    j.first = units;
+    if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
+      units += (j.rows * j.cols + 1023) / 1024;
+    } else {
+      CastParams p = b.base;
+      p.rows = j.rows; p.cols = j.cols;
+      units += n_groups(p);
+      const int64_t pc = a.strategy == LLMC_STRAT_CHANNEL ? j.cols / 16
+                                                           : std::min<int64_t>(a.bh, j.rows) * (std::min<int64_t>(a.bw, j.cols) / 16);
+      pieces = std::max(pieces, pc);
+    }
+  }
+  b.units = units;
+  if (units == 0) return true;
+  if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
+    dim3 g((unsigned)std::max<int64_t>(1, std::min<int64_t>((units + 7) / 8, 148 * 3))), bl(256);
+    constexpr bool fp4 = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4);
+    const int64_t group = a.group;
+    if (group == 16) k_stream_batch<FMT, BITS, 16><<<g, bl, 0, st>>>(b);
+    else if (group == 32) k_stream_batch<FMT, BITS, 32><<<g, bl, 0, st>>>(b);
+    else if constexpr (fp4) return false;
+    else if (group == 64) k_stream_batch<FMT, BITS, 64><<<g, bl, 0, st>>>(b);
+    else if (group == 128) k_stream_batch<FMT, BITS, 128><<<g, bl, 0, st>>>(b);
+    else return false;
+    llmc::note_launch();
+    return true;
+  }
+  if constexpr (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) {
+    return false;
+  } else {
+    if (a.strategy != LLMC_STRAT_CHANNEL && a.strategy != LLMC_STRAT_BLOCK) return false;
+    const unsigned g = (unsigned)std::min<int64_t>(units, 148 * 2);
+    if (pieces <= 256) k_tile_batch<FMT, BITS, 1><<<g, 256, 0, st>>>(b);
+    else if (pieces <= 512) k_tile_batch<FMT, BITS, 2><<<g, 256, 0, st>>>(b);
+    else if (pieces <= 1024) k_tile_batch<FMT, BITS, 4><<<g, 256, 0, st>>>(b);
+    else return false;
+    llmc::note_launch();
+    return true;
+  }
+}
+
+static bool launch_batch(CastBatch& b, cudaStream_t st) {
+  const bool b4 = b.base.a.bits == 4;
+  switch (b.base.fmt) {
+    case LLMC_FMT_PACK_INT32: return b4 ? launch_batch_fmt<LLMC_FMT_PACK_INT32, 4>(b, st) : launch_batch_fmt<LLMC_FMT_PACK_INT32, 8>(b, st);
+    case LLMC_FMT_FP8: return launch_batch_fmt<LLMC_FMT_FP8, 8>(b, st);
+    case LLMC_FMT_NVFP4: return launch_batch_fmt<LLMC_FMT_NVFP4, 8>(b, st);
+    case LLMC_FMT_MXFP4: return launch_batch_fmt<LLMC_FMT_MXFP4, 8>(b, st);
+    case LLMC_FMT_INT8: return launch_batch_fmt<LLMC_FMT_INT8, 8>(b, st);
+    default: return false;
+  }
+}
+
+// Whether one model-free job can ride in a batched launch.
+static bool batchable(const CastParams& p) {
+  const QArgs& a = p.a;
+  const bool out4 = (p.fmt == LLMC_FMT_NVFP4 || p.fmt == LLMC_FMT_MXFP4 || (p.fmt == LLMC_FMT_PACK_INT32 && a.bits == 4));
+  if ((uintptr_t)p.w % 32 || p.rows * p.cols == 0) return false;
+  if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
+    if ((p.rows * p.cols) % 32) return false;
+    if (a.group != 16 && a.group != 32 && a.group != 64 && a.group != 128) return false;
+    return (uintptr_t)p.out % (out4 ? 16 : 32) == 0;
+  }
+  if (a.strategy == LLMC_STRAT_CHANNEL || a.strategy == LLMC_STRAT_BLOCK) {
+    if (p.cols % 16 || (uintptr_t)p.out % 16) return false;
+    if (a.strategy == LLMC_STRAT_BLOCK && a.bw % 16) return false;
+    const int64_t pc = a.strategy == LLMC_STRAT_CHANNEL ? p.cols / 16
+                                                         : std::min<int64_t>(a.bh, p.rows) * (std::min<int64_t>(a.bw, p.cols) / 16);
+    return pc <= 1024;
+  }
+  return false;
+}
+
 static int check_fmt(const QArgs& a, int fmt) {
   switch (fmt) {
     case LLMC_FMT_PACK_INT32:
@@ -1281,6 +1462,42 @@ int llmc_modelfree_quantize(const void* w, int64_t rows, int64_t cols, const Llm
   if (!p.a.symmetric && !zp_out && rows * cols > 0) return LLMC_EINVAL_ARG;
   if ((fmt == LLMC_FMT_NVFP4 || fmt == LLMC_FMT_MXFP4) && (cols & 1)) return LLMC_EINVAL_SHAPE;
   return launch(p, (cudaStream_t)stream);
+}
+
+int llmc_modelfree_quantize_batch(const LlmcCastJob* jobs, int njobs, const LlmcQuantArgs* args, int fmt,
+                                  void* stream) {
+  if (!args || njobs < 0 || (njobs > 0 && !jobs)) return LLMC_EINVAL_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  CastBatch b;
+  memset(&b, 0, sizeof(b));
+  b.base.a = to_qargs(*args);
+  b.base.mode = MODE_FUSED;
+  b.base.fmt = fmt;
+  if (int v = check_fmt(b.base.a, fmt)) return v;
+  for (int i = 0; i < njobs; ++i) {
+    const LlmcCastJob& j = jobs[i];
+    CastParams p = b.base;
+    p.w = (const uint16_t*)j.w; p.rows = j.rows; p.cols = j.cols; p.gs = j.global_scale;
+    p.out = j.out; p.scale_out = j.scale_out; p.zp_out = p.a.symmetric ? nullptr : (int8_t*)j.zp_out;
+    if (int v = validate(p)) return v;
+    if ((!p.out || !p.scale_out) && p.rows * p.cols > 0) return LLMC_EINVAL_ARG;
+    if (fmt == LLMC_FMT_NVFP4 && !p.gs) return LLMC_EINVAL_ARG;
+    if (!p.a.symmetric && !j.zp_out && p.rows * p.cols > 0) return LLMC_EINVAL_ARG;
+    if ((fmt == LLMC_FMT_NVFP4 || fmt == LLMC_FMT_MXFP4) && (p.cols & 1)) return LLMC_EINVAL_SHAPE;
+    if (!batchable(p)) {  // odd shape or alignment: its own launch
+      if (int v = launch(p, st)) return v;
+      continue;
+    }
+    CastJob& q = b.job[b.njobs++];
+    q.w = p.w; q.rows = p.rows; q.cols = p.cols; q.gs = p.gs;
+    q.out = p.out; q.scale_out = p.scale_out; q.zp_out = p.zp_out;
+    if (b.njobs == kBatchMax) {
+      if (!launch_batch(b, st)) return LLMC_ENOSUPPORT;
+      b.njobs = 0;
+    }
+  }
+  if (b.njobs > 0 && !launch_batch(b, st)) return LLMC_ENOSUPPORT;
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
 int llmc_pack_zero_point(const int8_t* zp, int64_t rows, int64_t groups, int bits, int32_t* out, void* stream) {

@@ -264,16 +264,7 @@ def pack_zero_point(zp: torch.Tensor, num_bits: int) -> torch.Tensor:
     return out
 
 
-def modelfree_quantize(w: torch.Tensor, args, global_scale: torch.Tensor | None = None) -> dict:
-    """One weight through observe -> qparams -> quantize -> pack in a single
-    pass; returns the compressed-tensors state dict entries for it.
-
-    Keys and dtypes follow the compressors: ``weight_packed`` (int32 or uint8)
-    or ``weight`` (fp8), ``weight_scale`` (bf16 / fp8 / uint8 E8M0),
-    ``weight_global_scale`` (NVFP4), ``weight_shape`` (pack_quantized),
-    ``weight_zero_point`` (asymmetric pack_quantized, packed along rows).
-    """
-    w = _check_weight(w)
+def _modelfree_buffers(w: torch.Tensor, args, global_scale: torch.Tensor | None):
     rows, cols = w.shape
     fmt = format_of(args)
     sshape = stats_shape(rows, cols, args)
@@ -289,14 +280,67 @@ def modelfree_quantize(w: torch.Tensor, args, global_scale: torch.Tensor | None 
     else:
         scale = torch.empty(sshape, dtype=torch.bfloat16, device=w.device)
     zp = None if args.symmetric else torch.empty(sshape, dtype=torch.int8, device=w.device)
-    qa = qargs_struct(args)
-    check(lib().llmc_modelfree_quantize(ptr(w), rows, cols, ctypes.byref(qa), ptr(global_scale), fmt, ptr(out),
-                                        ptr(scale), ptr(zp), stream_ptr(w.device)), "modelfree_quantize")
+    return fmt, out, scale, zp, global_scale
+
+
+def _modelfree_state(fmt, args, rows, cols, out, scale, zp, global_scale) -> dict:
     res: dict[str, torch.Tensor] = {}
     if fmt == _lib.FMT_FP8:
         res["weight"] = out
         res["weight_scale"] = scale
         return res
+    res["weight_packed"] = out
+    res["weight_scale"] = scale
+    if fmt == _lib.FMT_NVFP4:
+        res["weight_global_scale"] = global_scale
+    if fmt == _lib.FMT_PACK_INT32:
+        res["weight_shape"] = torch.tensor([rows, cols], dtype=torch.int64)
+        if zp is not None:
+            res["weight_zero_point"] = pack_zero_point(zp, args.num_bits)
+    return res
+
+
+def modelfree_quantize(w: torch.Tensor, args, global_scale: torch.Tensor | None = None) -> dict:
+    """One weight through observe -> qparams -> quantize -> pack in a single
+    pass; returns the compressed-tensors state dict entries for it.
+
+    Keys and dtypes follow the compressors: ``weight_packed`` (int32 or uint8)
+    or ``weight`` (fp8), ``weight_scale`` (bf16 / fp8 / uint8 E8M0),
+    ``weight_global_scale`` (NVFP4), ``weight_shape`` (pack_quantized),
+    ``weight_zero_point`` (asymmetric pack_quantized, packed along rows).
+    """
+    w = _check_weight(w)
+    rows, cols = w.shape
+    fmt, out, scale, zp, global_scale = _modelfree_buffers(w, args, global_scale)
+    qa = qargs_struct(args)
+    check(lib().llmc_modelfree_quantize(ptr(w), rows, cols, ctypes.byref(qa), ptr(global_scale), fmt, ptr(out),
+                                        ptr(scale), ptr(zp), stream_ptr(w.device)), "modelfree_quantize")
+    return _modelfree_state(fmt, args, rows, cols, out, scale, zp, global_scale)
+
+
+def modelfree_quantize_batch(ws: list[torch.Tensor], args,
+                             global_scales: list[torch.Tensor | None] | None = None) -> list[dict]:
+    """``modelfree_quantize`` for many weights with the same args (MoE expert
+    sets, the tensors of a shard) in as few launches as possible."""
+    if not ws:
+        return []
+    gss = list(global_scales) if global_scales is not None else [None] * len(ws)
+    ws = [_check_weight(w) for w in ws]
+    dev = ws[0].device
+    jobs = (_lib.CastJob * len(ws))()
+    bufs = []
+    for i, (w, gs) in enumerate(zip(ws, gss)):
+        if w.device != dev:
+            raise ValueError("all weights of a batch must be on one device")
+        fmt, out, scale, zp, gs = _modelfree_buffers(w, args, gs)
+        bufs.append((fmt, out, scale, zp, gs))
+        jobs[i].w, jobs[i].rows, jobs[i].cols = ptr(w), w.shape[0], w.shape[1]
+        jobs[i].global_scale, jobs[i].out, jobs[i].scale_out, jobs[i].zp_out = ptr(gs), ptr(out), ptr(scale), ptr(zp)
+    qa = qargs_struct(args)
+    check(lib().llmc_modelfree_quantize_batch(jobs, len(ws), ctypes.byref(qa), bufs[0][0], stream_ptr(dev)),
+          "modelfree_quantize_batch")
+    return [_modelfree_state(fmt, args, w.shape[0], w.shape[1], out, scale, zp, gs)
+            for w, (fmt, out, scale, zp, gs) in zip(ws, bufs)]
     res["weight_packed"] = out
     res["weight_scale"] = scale
     if fmt == _lib.FMT_NVFP4:

@@ -249,3 +249,25 @@ def test_overflowing_and_tiny_scales_match_torch():
     q = (wt.float() / st.float().repeat_interleave(gsz, dim=1)).to(torch.bfloat16).float()
     ref = torch.clamp(torch.round(q), -128, 127).to(torch.int8)
     np.testing.assert_array_equal(bits(out), bits(ref))
+
+
+@pytest.mark.parametrize("scheme", ["W4A16", "W4A16_ASYM", "W8A16", "FP8_DYNAMIC", "FP8_BLOCK", "MXFP4A16",
+                                    "NVFP4A16", "FP8"])
+def test_modelfree_batch_matches_single(scheme):
+    """The batched launch equals one launch per tensor, bit for bit, across
+    shapes the batched kernels take and shapes they hand back (unaligned view,
+    ragged columns), and across more tensors than one batch holds."""
+    args = _weights_args(scheme)
+    shapes = [(64, 1024), (128, 2048), (32, 4096), (256, 512)] * 13  # 52 tensors: two batches
+    ws = [rand_bf16(r, c, seed=i, kind="student_t" if i % 3 == 0 else "normal").cuda() for i, (r, c) in enumerate(shapes)]
+    base = rand_bf16(64 * 1024 + 8, 1, seed=99).reshape(-1).cuda()
+    ws.append(base[8:].view(64, 1024))  # 16 bytes past alignment
+    if scheme in ("FP8_DYNAMIC", "W8A16"):
+        ws.append(rand_bf16(48, 1000, seed=77).cuda())  # cols % 16 != 0
+    gss = [ops.fused_global_scale([w]) for w in ws] if scheme == "NVFP4A16" else None
+    got = ops.modelfree_quantize_batch(ws, args, gss)
+    for i, w in enumerate(ws):
+        ref = ops.modelfree_quantize(w, args, gss[i] if gss else None)
+        assert set(got[i]) == set(ref)
+        for k in ref:
+            np.testing.assert_array_equal(bits(got[i][k]), bits(ref[k]), err_msg=f"{scheme}[{i}]:{k}")
