@@ -236,8 +236,10 @@ CAST_SCHEMES = ("W4A16", "NVFP4A16", "MXFP4A16", "FP8_BLOCK", "FP8_DYNAMIC")
 def measure_casts(layers, reps: int = 3) -> dict:
     """Model-free single-pass casts (observe + qparams + quantize + pack) over
     the Linear weights of a few layers (436 MB of bf16 per layer, so every
-    launch streams from HBM), one format at a time, timed with CUDA events.
-    Bytes per launch = bf16 weight read + codes and scales written."""
+    launch streams from HBM), one format at a time, timed with CUDA events:
+    one launch per tensor (``gbs``) and the batched launch over the same
+    tensors (``batched_gbs``, as a shard is processed).  Bytes = bf16 weight
+    read + codes and scales written."""
     from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
 
     from llmcompressor_b200 import ops
@@ -261,8 +263,16 @@ def measure_casts(layers, reps: int = 3) -> dict:
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / reps
+        batch = ops.ModelfreeBatch(ws, qa, gss)
+        batch.run()
+        e0.record()
+        for _ in range(reps):
+            batch.run()
+        e1.record()
+        torch.cuda.synchronize()
+        ms_b = e0.elapsed_time(e1) / reps
         res[name] = {"gbs": (in_bytes + out_bytes) / (ms * 1e-3) / 1e9, "ms": ms, "bytes": in_bytes + out_bytes,
-                     "launches_per_pass": len(ws)}
+                     "launches_per_pass": len(ws), "batched_gbs": (in_bytes + out_bytes) / (ms_b * 1e-3) / 1e9}
     return res
 
 
@@ -325,11 +335,12 @@ def modelfree_layers(device, reps: int = 3) -> dict:
     experts = [student_t(2048, 7168) for _ in range(64)] + [student_t(7168, 2048) for _ in range(32)]
     for name, bpw in (("FP8_BLOCK", 3.0001), ("MXFP4A16", 2.53125)):
         a = preset_name_to_scheme(name, ["Linear"]).weights
-        ops.modelfree_quantize_batch(experts[:2], a)
+        batch = ops.ModelfreeBatch(experts, a)
+        batch.run()
         torch.cuda.synchronize()
         e0.record()
         for _ in range(reps):
-            ops.modelfree_quantize_batch(experts, a)  # the expert set in batched launches
+            batch.run()  # the expert set in batched launches
         e1.record()
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / reps
@@ -535,10 +546,11 @@ def run_micro(args) -> None:
         qa = preset_name_to_scheme(args.scheme, ["Linear"]).weights
         ws = [(0.02 * torch.randn(rows, d, device=dev, generator=g)).to(torch.bfloat16) for _ in range(args.tensors)]
         gss = [ops.fused_global_scale([w]) for w in ws] if args.scheme == "NVFP4A16" else None
-        outs = ops.modelfree_quantize_batch(ws, qa, gss)
+        batch = ops.ModelfreeBatch(ws, qa, gss)
+        outs = batch.run().results
         nbytes = sum(w.numel() * 2 for w in ws) + sum(t.numel() * t.element_size() for o in outs
                                                       for k, t in o.items() if t.is_cuda and k != "weight_global_scale")
-        fn = lambda: ops.modelfree_quantize_batch(ws, qa, gss)  # noqa: E731
+        fn = batch.run
         work, unit = nbytes / 1e9, "GB/s"
     else:
         from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
@@ -656,7 +668,8 @@ def main():
             "algorithmic": "N*d*(d+1) flop per launch (lower triangle incl. diagonal), N=16384 tokens",
         },
         "hessian_tflops": res["hessian_tflops"],
-        "casts": ({k: {"gbs": v["gbs"], "frac": v["gbs"] / pk["hbm_gbs"]} for k, v in res["casts"].items()}
+        "casts": ({k: {"gbs": v["gbs"], "frac": v["gbs"] / pk["hbm_gbs"], "batched_gbs": v["batched_gbs"],
+                       "batched_frac": v["batched_gbs"] / pk["hbm_gbs"]} for k, v in res["casts"].items()}
                   if res["casts"] else None),
         "modelfree": ({k: {"gbs": v["gbs"], "frac": v["gbs"] / pk["hbm_gbs"], "ms": v["ms"], "weights": v["weights"]}
                        for k, v in res["modelfree"].items()} if res["modelfree"] else None),

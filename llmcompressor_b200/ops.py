@@ -318,29 +318,51 @@ def modelfree_quantize(w: torch.Tensor, args, global_scale: torch.Tensor | None 
     return _modelfree_state(fmt, args, rows, cols, out, scale, zp, global_scale)
 
 
+class ModelfreeBatch:
+    """A prepared batched model-free pass over fixed weights: outputs and the
+    job table are allocated once, ``run()`` only launches (a few microseconds
+    of host work), ``results`` holds the compressed-tensors entries per weight.
+    Use it when the same set of tensors is quantized repeatedly or when host
+    overhead matters (many small expert tensors)."""
+
+    def __init__(self, ws: list[torch.Tensor], args, global_scales: list[torch.Tensor | None] | None = None):
+        gss = list(global_scales) if global_scales is not None else [None] * len(ws)
+        self.ws = [_check_weight(w) for w in ws]
+        self.dev = self.ws[0].device if self.ws else None
+        self.jobs = (_lib.CastJob * max(1, len(self.ws)))()
+        self.qa = qargs_struct(args)
+        self.fmt = format_of(args)
+        bufs = []
+        for i, (w, gs) in enumerate(zip(self.ws, gss)):
+            if w.device != self.dev:
+                raise ValueError("all weights of a batch must be on one device")
+            fmt, out, scale, zp, gs = _modelfree_buffers(w, args, gs)
+            bufs.append((out, scale, zp, gs))
+            j = self.jobs[i]
+            j.w, j.rows, j.cols = ptr(w), w.shape[0], w.shape[1]
+            j.global_scale, j.out, j.scale_out, j.zp_out = ptr(gs), ptr(out), ptr(scale), ptr(zp)
+        self._bufs = bufs
+        self._args = args
+
+    def run(self) -> "ModelfreeBatch":
+        if self.ws:
+            check(lib().llmc_modelfree_quantize_batch(self.jobs, len(self.ws), ctypes.byref(self.qa), self.fmt,
+                                                      stream_ptr(self.dev)), "modelfree_quantize_batch")
+        return self
+
+    @property
+    def results(self) -> list[dict]:
+        return [_modelfree_state(self.fmt, self._args, w.shape[0], w.shape[1], out, scale, zp, gs)
+                for w, (out, scale, zp, gs) in zip(self.ws, self._bufs)]
+
+
 def modelfree_quantize_batch(ws: list[torch.Tensor], args,
                              global_scales: list[torch.Tensor | None] | None = None) -> list[dict]:
     """``modelfree_quantize`` for many weights with the same args (MoE expert
     sets, the tensors of a shard) in as few launches as possible."""
     if not ws:
         return []
-    gss = list(global_scales) if global_scales is not None else [None] * len(ws)
-    ws = [_check_weight(w) for w in ws]
-    dev = ws[0].device
-    jobs = (_lib.CastJob * len(ws))()
-    bufs = []
-    for i, (w, gs) in enumerate(zip(ws, gss)):
-        if w.device != dev:
-            raise ValueError("all weights of a batch must be on one device")
-        fmt, out, scale, zp, gs = _modelfree_buffers(w, args, gs)
-        bufs.append((fmt, out, scale, zp, gs))
-        jobs[i].w, jobs[i].rows, jobs[i].cols = ptr(w), w.shape[0], w.shape[1]
-        jobs[i].global_scale, jobs[i].out, jobs[i].scale_out, jobs[i].zp_out = ptr(gs), ptr(out), ptr(scale), ptr(zp)
-    qa = qargs_struct(args)
-    check(lib().llmc_modelfree_quantize_batch(jobs, len(ws), ctypes.byref(qa), bufs[0][0], stream_ptr(dev)),
-          "modelfree_quantize_batch")
-    return [_modelfree_state(fmt, args, w.shape[0], w.shape[1], out, scale, zp, gs)
-            for w, (fmt, out, scale, zp, gs) in zip(ws, bufs)]
+    return ModelfreeBatch(ws, args, global_scales).run().results
     res["weight_packed"] = out
     res["weight_scale"] = scale
     if fmt == _lib.FMT_NVFP4:
