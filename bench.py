@@ -133,6 +133,17 @@ def make_pool(dims, device, seed=1, pin_host=False):
     return pool
 
 
+# DRAM bytes per k_hessian_tc launch measured by ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum) at the bench's chunk size, and the algorithmic bytes
+# (X once + the lower triangle of H read and written):
+# profiles/k_hessian_tc__d4096_n16384.md, profiles/k_hessian_tc__d14336_n16384_traffic.md
+HESSIAN_TRAFFIC = {4096: 300.8e6 + 39.1e6, 14336: 4602.2e6 + 804.9e6}
+
+
+def hessian_algorithmic_bytes(d: int, tokens: int = CHUNK) -> float:
+    return tokens * d * 2 + 2 * (d * (d + 1) // 2) * 4
+
+
 def hessian_flops(dims, tokens):
     return sum(tokens * d * (d + 1) for d in dims.values())
 
@@ -578,6 +589,20 @@ def run_micro(args) -> None:
           flush=True)
 
 
+def _layer_hessian_dims():
+    return [CFG["hidden"]] * 3 + [CFG["intermediate"]]
+
+
+def traffic_per_launch() -> float:
+    ds = _layer_hessian_dims()
+    return sum(HESSIAN_TRAFFIC[d] for d in ds) / len(ds)
+
+
+def algorithmic_per_launch() -> float:
+    ds = _layer_hessian_dims()
+    return sum(hessian_algorithmic_bytes(d) for d in ds) / len(ds)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--micro", choices=["hessian", "gptq", "hinv", "cast", "castbatch"], default=None,
@@ -664,7 +689,10 @@ def main():
             "unit": "TFLOP/s",
             "frac": res["hessian_tflops"] / h_peak,
             "peak_source": f"{pk['source']} bf16_tflops_sustained",
-            "traffic": None,
+            "traffic": traffic_per_launch(),
+            "traffic_algorithmic": algorithmic_per_launch(),
+            "traffic_note": "ncu DRAM bytes per launch, mean over the step's launches (3 at d=4096, 1 at d=14336); "
+                            "profiles/k_hessian_tc__*",
             "algorithmic": "N*d*(d+1) flop per launch (lower triangle incl. diagonal), N=16384 tokens",
         },
         "hessian_tflops": res["hessian_tflops"],

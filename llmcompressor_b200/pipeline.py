@@ -93,8 +93,13 @@ _STREAMS: dict[int, list[torch.cuda.Stream]] = {}
 
 
 def _side_streams(dev: torch.device, n: int) -> list[torch.cuda.Stream]:
+    """n side streams of this device; the first has the highest priority the
+    device offers (the layer's critical path runs there)."""
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     pool = _STREAMS.setdefault(idx, [])
+    if not pool:
+        lo, hi = torch.cuda.Stream.priority_range() if hasattr(torch.cuda.Stream, "priority_range") else (0, -1)
+        pool.append(torch.cuda.Stream(device=dev, priority=min(lo, hi)))
     while len(pool) < n:
         pool.append(torch.cuda.Stream(device=dev))
     return pool[:n]
@@ -130,9 +135,10 @@ def solve_layer(
     streams = _side_streams(dev, max(len(dims), len(specs)))
 
     # factorisations, largest first, one side stream each
+    order = sorted(dims, key=lambda k: (-dims[k], k))
     inv: dict[str, gptq.InverseHessian] = {}
     ready: dict[str, torch.cuda.Event] = {}
-    for i, key in enumerate(sorted(dims, key=lambda k: (-dims[k], k))):
+    for i, key in enumerate(order):
         d = dims[key]
         st = streams[i]
         st.wait_stream(main)
@@ -157,11 +163,15 @@ def solve_layer(
         bcast.record(main)
         ready = {k: bcast for k in ready}
 
-    # block loops + int4 pack, one side stream per module
+    # block loops + int4 pack, one side stream per module; the modules that
+    # read the largest Hessian follow its factorisation on the high-priority
+    # stream (the layer's critical path), the others spread over the rest
+    crit = order[0]
+    others = streams[1:] or streams
     parts: dict[str, tuple] = {}
     done = []
     for j, s in enumerate(specs):
-        st = streams[j % len(streams)]
+        st = streams[0] if s.input_key == crit else others[j % len(others)]
         st.wait_event(ready[s.input_key])
         r0, r1 = row_range(s.out_features, rank, ws)
         with torch.cuda.stream(st):
