@@ -807,7 +807,7 @@ __device__ __forceinline__ void tile_load(const CastParams& p, int64_t gi, uint3
   const int64_t ppr = (R.c1 - R.c0) / 16, npc = (R.r1 - R.r0) * ppr;
 #pragma unroll
   for (int j = 0; j < NP; ++j) {
-    const int64_t pc = threadIdx.x + 256 * j;
+    const int64_t pc = threadIdx.x + (int64_t)blockDim.x * j;
     if (pc < npc) ld_v8(p.w + (R.r0 + pc / ppr) * p.cols + R.c0 + (pc % ppr) * 16, w[j]);
   }
 }
@@ -823,7 +823,7 @@ __device__ __forceinline__ void tile_process(const CastParams& p, int64_t gi, co
     uint32_t M = 0xFF80FF80u, m = 0x7F807F80u;  // (-inf, -inf), (+inf, +inf)
 #pragma unroll
     for (int j = 0; j < NP; ++j)
-      if (threadIdx.x + 256 * j < npc) {
+      if (threadIdx.x + (int64_t)blockDim.x * j < npc) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) { M = hmax2(M, w[j][k]); m = hmin2(m, w[j][k]); }
       }
@@ -845,7 +845,7 @@ __device__ __forceinline__ void tile_process(const CastParams& p, int64_t gi, co
   const float qmin = p.a.qmin(), qmax = p.a.qmax();
 #pragma unroll
   for (int j = 0; j < NP; ++j) {
-    const int64_t pc = threadIdx.x + 256 * j;
+    const int64_t pc = threadIdx.x + (int64_t)blockDim.x * j;
     if (pc >= npc) break;
     const int64_t el = (R.r0 + pc / ppr) * p.cols + R.c0 + (pc % ppr) * 16;
     uint32_t o[4];
@@ -857,8 +857,10 @@ __device__ __forceinline__ void tile_process(const CastParams& p, int64_t gi, co
   }
 }
 
-template <int FMT, int BITS, int MODE, int NP, bool PF>
-__global__ void __launch_bounds__(256, PF ? 2 : 1) k_tile(CastParams p, int64_t ng) {
+// THR threads per CTA; 128-thread CTAs holding a whole 128x128 block (NP = 8)
+// put four blocks in flight per SM without prefetch registers.
+template <int FMT, int BITS, int MODE, int NP, bool PF, int THR = 256>
+__global__ void __launch_bounds__(THR, PF ? 2 : (THR == 128 ? 4 : 1)) k_tile(CastParams p, int64_t ng) {
   __shared__ float sh[32];
   int64_t gi = blockIdx.x;
   if (!PF) {
@@ -1161,7 +1163,9 @@ static bool launch_tile(const CastParams& p, int64_t pieces, cudaStream_t st) {
       return true;
     }
     const unsigned pg = (unsigned)std::min<int64_t>(ng, 148 * 2);
-    if (pieces <= 256) k_tile<FMT, BITS, MODE, 1, true><<<pg, 256, 0, st>>>(p, ng);
+    if (p.a.strategy == LLMC_STRAT_BLOCK && pieces > 512 && pieces <= 1024)
+      k_tile<FMT, BITS, MODE, 8, false, 128><<<(unsigned)std::min<int64_t>(ng, 148 * 16), 128, 0, st>>>(p, ng);
+    else if (pieces <= 256) k_tile<FMT, BITS, MODE, 1, true><<<pg, 256, 0, st>>>(p, ng);
     else if (pieces <= 512) k_tile<FMT, BITS, MODE, 2, true><<<pg, 256, 0, st>>>(p, ng);
     else if (pieces <= 1024) k_tile<FMT, BITS, MODE, 4, true><<<pg, 256, 0, st>>>(p, ng);
     else if (pieces <= 2048) k_tile<FMT, BITS, MODE, 8, false><<<(unsigned)std::min<int64_t>(ng, 148 * 8), 256, 0, st>>>(p, ng);
@@ -1354,6 +1358,7 @@ static bool batchable(const CastParams& p) {
   if (a.strategy == LLMC_STRAT_CHANNEL || a.strategy == LLMC_STRAT_BLOCK) {
     if (p.cols % 16 || (uintptr_t)p.out % 16) return false;
     if (a.strategy == LLMC_STRAT_BLOCK && a.bw % 16) return false;
+    if (a.strategy == LLMC_STRAT_CHANNEL && p.cols <= 4096) return false;  // the warp-per-row kernel is faster
     const int64_t pc = a.strategy == LLMC_STRAT_CHANNEL ? p.cols / 16
                                                          : std::min<int64_t>(a.bh, p.rows) * (std::min<int64_t>(a.bw, p.cols) / 16);
     return pc <= 1024;
