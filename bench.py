@@ -137,7 +137,7 @@ def make_pool(dims, device, seed=1, pin_host=False):
 # dram__bytes_write.sum) at the bench's chunk size, and the algorithmic bytes
 # (X once + the lower triangle of H read and written):
 # profiles/k_hessian_tc__d4096_n16384.md, profiles/k_hessian_tc__d14336_n16384_traffic.md
-HESSIAN_TRAFFIC = {4096: 300.8e6 + 39.1e6, 14336: 4602.2e6 + 804.9e6}
+HESSIAN_TRAFFIC = {4096: 201.4e6 + 7.4e6, 14336: 3512.9e6 + 772.9e6}
 
 
 def hessian_algorithmic_bytes(d: int, tokens: int = CHUNK) -> float:

@@ -143,6 +143,12 @@ int llmc_modelfree_quantize(const void* w_bf16, int64_t rows, int64_t cols, cons
                             const float* global_scale, int out_format, void* packed_out, void* scale_out,
                             void* zp_out, void* stream);
 
+/* int8 tensors holding int4 values (-8..7) -> two per byte, the even column
+ * in the low nibble: `_pack_int4_to_int8` of the reference's checkpoint
+ * repacker (S/utils/pack_int4_to_int8.py:13-28).  in: int8 (rows x cols),
+ * cols even; out: int8 (rows x cols/2). */
+int llmc_pack_int4_to_int8(const int8_t* in, int64_t rows, int64_t cols, int8_t* out, void* stream);
+
 /* Several tensors through llmc_modelfree_quantize in as few launches as
  * possible (all with the same args and format): a batched launch for up to 48
  * tensors at a time, each with its own pointers; tensors whose shape or

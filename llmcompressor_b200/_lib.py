@@ -80,6 +80,7 @@ _SIGS = {
     "llmc_observe_minmax": [_P, _I64, _I64, _QA, _P, _P, _P],
     "llmc_observe_mse_workspace_size": [_I64, _I64, _QA, _P],
     "llmc_modelfree_quantize_batch": [ctypes.POINTER(CastJob), _I32, _QA, _I32, _P],
+    "llmc_pack_int4_to_int8": [_P, _I64, _I64, _P, _P],
     "llmc_observe_mse": [_P, _I64, _I64, _QA, ctypes.c_float, _I32, ctypes.c_float, ctypes.c_float, _P, _P, _P, _P],
     "llmc_absmax_accumulate": [_P, _I64, _P, _P],
     "llmc_global_scale": [_P, _P, _P],

@@ -1022,6 +1022,20 @@ __global__ void __launch_bounds__(256, 3) k_stream_batch(const __grid_constant__
   }
 }
 
+// 128-thread CTAs, one group at a time without prefetch: several CTAs per SM
+// keep their loads in flight (the batched form of k_tile<..., THR = 128>).
+template <int FMT, int BITS, int NP>
+__global__ void __launch_bounds__(128, 4) k_tile_batch128(const __grid_constant__ CastBatch b) {
+  __shared__ float sh[32];
+  for (int64_t gi = blockIdx.x; gi < b.units; gi += gridDim.x) {
+    const int j = find_job(b, gi);
+    const CastParams p = job_params(b, j);
+    uint32_t w[NP][8];
+    tile_load<NP>(p, gi - b.job[j].first, w);
+    tile_process<FMT, BITS, MODE_FUSED, NP>(p, gi - b.job[j].first, w, sh);
+  }
+}
+
 template <int FMT, int BITS, int NP>
 __global__ void __launch_bounds__(256, 2) k_tile_batch(const __grid_constant__ CastBatch b) {
   __shared__ float sh[32];
@@ -1078,6 +1092,39 @@ __global__ void k_qparams(const uint16_t* mn, const uint16_t* mx, int64_t n, QAr
     if (a.zp_dtype == LLMC_ZP_INT8) ((int8_t*)zp_out)[i] = (int8_t)(int32_t)zp;
     else if (a.zp_dtype == LLMC_ZP_UINT8) ((uint8_t*)zp_out)[i] = (uint8_t)(int32_t)zp;
     else ((float*)zp_out)[i] = 0.0f;
+  }
+}
+
+// int8 tensors holding int4 codes -> two codes per byte, even column in the
+// low nibble (S/utils/pack_int4_to_int8.py:13-28 `_pack_int4_to_int8`).  A
+// thread packs 32 values (two 16-byte loads, one 16-byte store) when the
+// row length and pointers allow, else one output byte.
+__global__ void k_pack_int4_int8(const int8_t* __restrict__ in, int64_t rows, int64_t cols, int8_t* __restrict__ out,
+                                 int vec) {
+  const int64_t half = cols / 2, n = rows * half;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, st = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {  // cols % 32 == 0, 16-byte aligned: 16 output bytes per step
+    const int64_t n16 = n / 16;
+    for (int64_t i = tid; i < n16; i += st) {
+      const uint4 a = __ldcs((const uint4*)in + 2 * i), b = __ldcs((const uint4*)in + 2 * i + 1);
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t lo = w[2 * k] & 0x0F0F0F0Fu, hi = w[2 * k + 1] & 0x0F0F0F0Fu;
+        // bytes b0..b3 of lo (cols 0..3 of 8) and hi (cols 4..7): pair (0,1) (2,3) of each
+        const uint32_t plo = (lo & 0x000F000Fu) | ((lo >> 4) & 0x00F000F0u);  // [c0|c1<<4, -, c2|c3<<4, -]
+        const uint32_t phi = (hi & 0x000F000Fu) | ((hi >> 4) & 0x00F000F0u);
+        o[k] = __byte_perm(plo, phi, 0x6420);
+      }
+      __stcs((uint4*)out + i, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+    return;
+  }
+  for (int64_t i = tid; i < n; i += st) {
+    const int64_t r = i / half, c = i % half;
+    const uint8_t lo = (uint8_t)in[r * cols + 2 * c] & 0x0F, hi = (uint8_t)in[r * cols + 2 * c + 1] & 0x0F;
+    out[i] = (int8_t)(uint8_t)((hi << 4) | lo);
   }
 }
 
@@ -1324,9 +1371,10 @@ static bool launch_batch_fmt(CastBatch& b, cudaStream_t st) {
   } else {
     if (a.strategy != LLMC_STRAT_CHANNEL && a.strategy != LLMC_STRAT_BLOCK) return false;
     const unsigned g = (unsigned)std::min<int64_t>(units, 148 * 2);
+    const unsigned g128 = (unsigned)std::min<int64_t>(units, 148 * 16);
     if (pieces <= 256) k_tile_batch<FMT, BITS, 1><<<g, 256, 0, st>>>(b);
-    else if (pieces <= 512) k_tile_batch<FMT, BITS, 2><<<g, 256, 0, st>>>(b);
-    else if (pieces <= 1024) k_tile_batch<FMT, BITS, 4><<<g, 256, 0, st>>>(b);
+    else if (pieces <= 512) k_tile_batch128<FMT, BITS, 4><<<g128, 128, 0, st>>>(b);
+    else if (pieces <= 1024) k_tile_batch128<FMT, BITS, 8><<<g128, 128, 0, st>>>(b);
     else return false;
     llmc::note_launch();
     return true;
@@ -1502,6 +1550,17 @@ int llmc_modelfree_quantize_batch(const LlmcCastJob* jobs, int njobs, const Llmc
     }
   }
   if (b.njobs > 0 && !launch_batch(b, st)) return LLMC_ENOSUPPORT;
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_pack_int4_to_int8(const int8_t* in, int64_t rows, int64_t cols, int8_t* out, void* stream) {
+  if (rows < 0 || cols < 0 || ((!in || !out) && rows * cols > 0)) return LLMC_EINVAL_ARG;
+  if (cols % 2) return LLMC_EINVAL_SHAPE;
+  if (rows * cols == 0) return LLMC_OK;
+  const int vec = (cols % 32 == 0) && ((uintptr_t)in % 16 == 0) && ((uintptr_t)out % 16 == 0);
+  const int64_t work = vec ? rows * cols / 32 : rows * cols / 2;
+  const unsigned blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 8));
+  k_pack_int4_int8<<<blocks, 256, 0, (cudaStream_t)stream>>>(in, rows, cols, out, vec); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 

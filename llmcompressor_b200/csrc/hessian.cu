@@ -7,17 +7,22 @@
 // float32, so scaling the float32 sum by 2 is the same arithmetic up to
 // summation order).
 //
-// Design (one persistent CTA per SM, 192 threads, warp-specialised):
+// Design (one persistent CTA per SM, 192 threads, warp-specialised), output
+// tiles of 256 x 256:
 //   warp 0      TMA producer: X tiles (64 tokens x 64 features, 128B swizzle)
-//               into a 4-stage ring (192 KB: four stages keep the tensor
-//               cores fed, three measurably starve them); both operands are
-//               MN-major views of X.
-//   warp 1      allocates 512 TMEM columns and issues tcgen05.mma
-//               (M=128, N=256, K=16, bf16 -> f32) for output tile 128x256,
-//               double-buffered accumulators (2 x 256 columns).
+//               into a 3-stage ring of 64 KB (A: 256 features, B: 256
+//               features); both operands are MN-major views of X.
+//   warp 1      allocates all 512 TMEM columns and issues tcgen05.mma
+//               (M=128, N=256, K=16, bf16 -> f32): two MMAs per K step, the
+//               two 128-row halves of A against the same B, into two 256-column
+//               accumulators.  A 256 x 256 tile per SM reads a third fewer
+//               operand bytes per flop than 128 x 256 tiles, which outweighs
+//               the accumulators no longer being double-buffered (the MMAs of
+//               the next tile wait for this tile's epilogue).
 //   warps 2..5  epilogue: tcgen05.ld 32x32 boxes, x alpha, stage in swizzled
-//               smem (one buffer per warp), TMA reduce-add into H -- the box itself and, for boxes
-//               strictly below the diagonal, its transpose (the mirror).
+//               smem (one buffer per warp), TMA reduce-add into H -- the box
+//               itself and, for boxes strictly below the diagonal, its
+//               transpose (the mirror).
 // Only tiles that touch the lower triangle are computed; boxes entirely
 // above the diagonal inside those tiles are skipped (their values arrive as
 // mirrors), so every element of H receives exactly one reduce-add per call.
@@ -34,21 +39,21 @@ namespace hess {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;   // 16 KB: two 64-feature chunks
+constexpr int BM = 256, BN = 256, BK = 64, STAGES = 3;
+constexpr int A_BYTES = BM * BK * 2;   // 32 KB: four 64-feature chunks
 constexpr int B_BYTES = BN * BK * 2;   // 32 KB: four 64-feature chunks
 constexpr int CHUNK_BYTES = 64 * BK * 2;  // 8 KB: one TMA box (64 features x 64 tokens)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_WARPS = 4;
 constexpr int EPI_BOX_BYTES = 32 * 32 * 4;                 // 4 KB fp32 32x32 box
 constexpr int EPI_WARP_BYTES = 2 * EPI_BOX_BYTES;          // one buffer: direct + mirror box
-constexpr int SMEM_STAGES = STAGES * STAGE_BYTES;          // 192 KB
+constexpr int SMEM_STAGES = STAGES * STAGE_BYTES;          // 192 KB (3 x 64 KB)
 constexpr int SMEM_EPI = EPI_WARPS * EPI_WARP_BYTES;       // 32 KB
 constexpr int SMEM_BAR = 256;
 constexpr int SMEM_TOTAL = SMEM_STAGES + SMEM_EPI + SMEM_BAR + 1024;  // + alignment slack
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t IDESC = instr_desc(1, true, true, BM, BN);
+constexpr uint32_t IDESC = instr_desc(1, true, true, 128, BN);  // two M=128 MMAs per K step
 
 struct Params {
   int64_t d, n_tokens;
@@ -60,23 +65,20 @@ struct Params {
   float num_add;
 };
 
-// Tiles touching the lower triangle: row tile bi (128 rows) pairs with column
-// tiles bj = 0 .. floor(bi/2) (256 columns).  tiles_before(bi) = sum_{r<bi} (r/2 + 1).
-__device__ __forceinline__ int tiles_before(int bi) {
-  int m = bi >> 1;
-  return (bi & 1) ? (m + 1) * (m + 1) : m * (m + 1);
-}
+// Tiles touching the lower triangle: row tile bi (256 rows) pairs with column
+// tiles bj = 0 .. bi.  tiles_before(bi) = sum_{r<bi} (r + 1).
+__device__ __forceinline__ int tiles_before(int bi) { return bi * (bi + 1) / 2; }
 // Tile order.  The persistent CTAs walk the tile list in waves of one tile
 // per CTA and move through the token dimension in step, so each wave reads
 // every X column its tiles touch once from DRAM and serves the rest from L2.
 // Enumerating the lower triangle row by row makes every wave touch nearly all
-// column panels (d = 14336: X read ~15 times per launch); here row tiles are
-// grouped in bands of RB and, inside a band, column tiles in chunks of CB, so
-// consecutive tiles form compact RB x CB blocks (~8 X reads at d = 14336).
-constexpr int RB = 24, CB = 6;
+// column panels; here row tiles are grouped in bands of RB and, inside a
+// band, column tiles in chunks of CB, so consecutive tiles form compact
+// RB x CB blocks (d = 14336: X read ~6 times per launch instead of ~11).
+constexpr int RB = 16, CB = 8;
 __device__ __forceinline__ int chunk_tiles(int r0, int r1, int c) {
   int n = 0;
-  for (int bi = r0; bi < r1; ++bi) n += max(0, min(CB, (bi >> 1) + 1 - c * CB));
+  for (int bi = r0; bi < r1; ++bi) n += max(0, min(CB, bi + 1 - c * CB));
   return n;
 }
 __device__ __forceinline__ void tile_coords(int t, int mb, int& bi, int& bj) {
@@ -88,10 +90,10 @@ __device__ __forceinline__ void tile_coords(int t, int mb, int& bi, int& bj) {
   const int r0 = lo * RB, r1 = min(mb, r0 + RB);
   int u = t - tiles_before(r0);
   int c = 0;
-  const int cmax = ((mb >> 1) + CB) / CB;  // chunks of the widest row: the walk ends by then
+  const int cmax = (mb + CB) / CB;  // chunks of the widest row: the walk ends by then
   for (int cnt = chunk_tiles(r0, r1, c); u >= cnt && c < cmax; cnt = chunk_tiles(r0, r1, ++c)) u -= cnt;
   for (bi = r0; bi < r1; ++bi) {
-    const int k = max(0, min(CB, (bi >> 1) + 1 - c * CB));
+    const int k = max(0, min(CB, bi + 1 - c * CB));
     if (u < k) { bj = c * CB + u; return; }
     u -= k;
   }
@@ -108,8 +110,8 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
   uint64_t* bars = (uint64_t*)(smem + SMEM_STAGES + SMEM_EPI);
   uint64_t* full = bars;                 // [STAGES]
   uint64_t* empty = bars + STAGES;       // [STAGES]
-  uint64_t* tfull = bars + 2 * STAGES;   // [2]
-  uint64_t* tempty = bars + 2 * STAGES + 2;  // [2]
+  uint64_t* tfull = bars + 2 * STAGES;   // [1] (slot 2 unused)
+  uint64_t* tempty = bars + 2 * STAGES + 2;  // [1] (slot 2 unused)
   uint64_t* drain = bars + 2 * STAGES + 4;  // MMA completion before TMEM is freed
   uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 5);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
@@ -119,7 +121,8 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(smem_u32(&full[s]), 1); mbar_init(smem_u32(&empty[s]), 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(smem_u32(&tfull[b]), 1); mbar_init(smem_u32(&tempty[b]), EPI_WARPS); }
+    mbar_init(smem_u32(&tfull[0]), 1);           // the tile's MMAs are done
+    mbar_init(smem_u32(&tempty[0]), EPI_WARPS);  // the epilogue has read the accumulators
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -175,12 +178,11 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
       uint32_t acc_phase = 0;
       for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
-        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, abort_flag)) break;
+        if (!mbar_wait(smem_u32(&tempty[0]), acc_phase ^ 1, abort_flag)) break;
         tc_fence_after();
-        const uint32_t dt = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t dt = tmem_base;
         bool ok = true;
         for (int ks = 0; ks < nk; ++ks) {
           if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag)) { ok = false; break; }
@@ -189,16 +191,19 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
           const uint32_t sb = sa + A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = smem_desc(sa + kk * 2048, CHUNK_BYTES, 1024, SWZ_128B);
             const uint64_t bd = smem_desc(sb + kk * 2048, CHUNK_BYTES, 1024, SWZ_128B);
-            mma_f16_ss(dt, ad, bd, IDESC, (ks | kk) != 0);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint64_t ad = smem_desc(sa + h * 2 * CHUNK_BYTES + kk * 2048, CHUNK_BYTES, 1024, SWZ_128B);
+              mma_f16_ss(dt + (uint32_t)(h * BN), ad, bd, IDESC, (ks | kk) != 0);
+            }
           }
           mma_commit(smem_u32(&empty[stage]));
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        mma_commit(smem_u32(&tfull[acc]));
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        mma_commit(smem_u32(&tfull[0]));
+        acc_phase ^= 1;
       }
       // every MMA this thread issued has finished before TMEM can be freed
       mma_commit(smem_u32(drain));
@@ -209,20 +214,20 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     uint8_t* wbuf = epi + (warp - 2) * EPI_WARP_BYTES;
-    int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
       int bi, bj;
       tile_coords(t, p.mb, bi, bj);
       const int row0 = bi * BM, col0 = bj * BN;
-      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag)) break;
+      if (!mbar_wait(smem_u32(&tfull[0]), acc_phase, abort_flag)) break;
       tc_fence_after();
-      const int gr = row0 + 32 * q;
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int hc = 0; hc < 2 * (BN / 32); ++hc) {
+        const int h = hc / (BN / 32), c = hc % (BN / 32);
+        const int gr = row0 + 128 * h + 32 * q;
         const int gc = col0 + 32 * c;
         if (gr >= p.d || gc >= p.d || gr < gc) continue;  // out of range, or strictly above the diagonal
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * BN + 32 * c), r);
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)(h * BN + 32 * c), r);
         tmem_ld_wait();
         uint8_t* dbox = wbuf;
         uint8_t* mbox = dbox + EPI_BOX_BYTES;
@@ -256,8 +261,8 @@ k_hessian_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ C
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[0]));
+      acc_phase ^= 1;
     }
     if (lane == 0) bulk_wait<0>();
   }
@@ -385,10 +390,7 @@ int llmc_hessian_accumulate(const void* x, int64_t n_tokens, int64_t d, int64_t 
   p.d = d;
   p.n_tokens = n_tokens;
   p.mb = (int)((d + BM - 1) / BM);
-  {
-    int m = p.mb >> 1;  // tiles_before(mb)
-    p.num_tiles = (p.mb & 1) ? (m + 1) * (m + 1) : m * (m + 1);
-  }
+  p.num_tiles = p.mb * (p.mb + 1) / 2;
   p.alpha = alpha;
   p.status = status;
   p.num_samples = num_samples;
@@ -411,8 +413,8 @@ int llmc_hessian_accumulate(const void* x, int64_t n_tokens, int64_t d, int64_t 
 }
 
 int llmc_hessian_tiles(int64_t d) {
-  int64_t mb = (d + BM - 1) / BM, m = mb >> 1;
-  return (int)((mb & 1) ? (m + 1) * (m + 1) : m * (m + 1));
+  int64_t mb = (d + BM - 1) / BM;
+  return (int)(mb * (mb + 1) / 2);
 }
 
 }  // extern "C"

@@ -372,3 +372,21 @@ def modelfree_quantize_batch(ws: list[torch.Tensor], args,
         if zp is not None:
             res["weight_zero_point"] = pack_zero_point(zp, args.num_bits)
     return res
+
+
+def pack_int4_to_int8(t: torch.Tensor) -> torch.Tensor:
+    """``_pack_int4_to_int8`` of the checkpoint repacker
+    (S/utils/pack_int4_to_int8.py:13-28): int8 (rows, cols) holding int4
+    values -> int8 (rows, cols/2), the even column in the low nibble."""
+    require_cuda(t)
+    if t.ndim != 2:
+        raise ValueError(f"Expected 2D tensor, but got {t.ndim}D")
+    rows, cols = t.shape
+    if cols % 2 != 0:
+        raise ValueError(f"Expected even number of columns for int4 packing, but got shape {t.shape}")
+    if t.dtype != torch.int8:
+        raise NotImplementedError(f"dtype {t.dtype}: the repacker takes int8")
+    t = t.contiguous()
+    out = torch.empty(rows, cols // 2, dtype=torch.int8, device=t.device)
+    check(lib().llmc_pack_int4_to_int8(ptr(t), rows, cols, ptr(out), stream_ptr(t.device)), "pack_int4_to_int8")
+    return out

@@ -177,3 +177,12 @@ def nvfp4_global_scale(weights: list[np.ndarray]) -> np.float32:
     """Shared global scale of a fused set (q/k/v, gate/up): S/observers/base.py:78-96."""
     args = SCHEMES["NVFP4A16"]
     return generate_gparam(fused_absmax([minmax(w, args) for w in weights]))
+
+
+def pack_int4_to_int8(t: np.ndarray) -> np.ndarray:
+    """``_pack_int4_to_int8`` (S/utils/pack_int4_to_int8.py:13-28): int8 (rows,
+    cols) -> int8 (rows, cols/2), low nibble = even column, high = odd."""
+    t = np.asarray(t, dtype=np.int8)
+    lo = t[:, 0::2].astype(np.int16) & 0x0F
+    hi = t[:, 1::2].astype(np.int16) & 0x0F
+    return ((hi << 4) | lo).astype(np.uint8).view(np.int8)

@@ -12,6 +12,7 @@ seeded synthetic inputs and stores inputs and outputs as ``.npz`` files:
   ``S/observers/base.py:99-123``).
 * ``mse_<case>.npz`` -- the ``memoryless_mse`` grid-search observer
   (``S/observers/mse.py``, ``S/observers/mse_quant.py``) and its qparams.
+* ``repack_int4_int8.npz`` -- the checkpoint repacker's ``_pack_int4_to_int8``.
 * ``hessian.npz`` -- ``accumulate_hessian`` over several calls
   (``S/modifiers/gptq/gptq_quantize.py:63-97``).
 * ``gptq_<case>.npz`` -- ``quantize_weight``
@@ -259,6 +260,20 @@ def gen_mse_observers():
         print("mse", name, tuple(mn.shape), qp["scale"].dtype)
 
 
+def gen_repack():
+    """``_pack_int4_to_int8`` (S/utils/pack_int4_to_int8.py:13-28) on int4 codes
+    and on arbitrary int8 values (the & 0x0F masking)."""
+    from llmcompressor.utils.pack_int4_to_int8 import _pack_int4_to_int8
+
+    g = torch.Generator().manual_seed(41)
+    codes = torch.randint(-8, 8, (48, 96), generator=g, dtype=torch.int8)
+    wild = torch.randint(-128, 128, (16, 64), generator=g, dtype=torch.int8)
+    np.savez_compressed(os.path.join(HERE, "repack_int4_int8.npz"), codes=codes.numpy(),
+                        codes_packed=_pack_int4_to_int8(codes).numpy(), wild=wild.numpy(),
+                        wild_packed=_pack_int4_to_int8(wild).numpy())
+    print("repack", tuple(codes.shape))
+
+
 # --------------------------------------------------------------------------
 # Hessian + GPTQ
 # --------------------------------------------------------------------------
@@ -345,8 +360,12 @@ if __name__ == "__main__":
     if sys.argv[1:] == ["mse"]:
         gen_mse_observers()
         sys.exit(0)
+    if sys.argv[1:] == ["repack"]:
+        gen_repack()
+        sys.exit(0)
     gen_observers()
     gen_mse_observers()
+    gen_repack()
     gen_modelfree()
     gen_nvfp4_fused()
     gen_hessian()

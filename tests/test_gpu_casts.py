@@ -271,3 +271,17 @@ def test_modelfree_batch_matches_single(scheme):
         assert set(got[i]) == set(ref)
         for k in ref:
             np.testing.assert_array_equal(bits(got[i][k]), bits(ref[k]), err_msg=f"{scheme}[{i}]:{k}")
+
+
+def test_repack_int4_int8_golden_and_large():
+    g = load("repack_int4_int8")
+    for k in ("codes", "wild"):
+        got = ops.pack_int4_to_int8(torch.from_numpy(g[k]).cuda())
+        np.testing.assert_array_equal(got.cpu().numpy(), g[f"{k}_packed"])
+    gen = torch.Generator().manual_seed(5)
+    for rows, cols in ((4096, 14336), (33, 1000)):  # vector path, then the bytewise path
+        t = torch.randint(-128, 128, (rows, cols), generator=gen, dtype=torch.int8)
+        got = ops.pack_int4_to_int8(t.cuda())
+        np.testing.assert_array_equal(got.cpu().numpy(), ocasts.pack_int4_to_int8(t.numpy()))
+    with pytest.raises(ValueError):
+        ops.pack_int4_to_int8(torch.zeros(4, 3, dtype=torch.int8, device="cuda"))

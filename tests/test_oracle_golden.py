@@ -221,3 +221,10 @@ def test_reference_mse_known_answers(strategy, symmetric, exp_loss):
                                     args, dtype="f32")
     loss = float(np.sum(np.abs(f - q) ** 2) / t.size)
     assert loss == pytest.approx(exp_loss, abs=1e-10)
+
+
+def test_repack_int4_int8_bit_exact():
+    """S/utils/pack_int4_to_int8.py:13-28 on int4 codes and on arbitrary int8 values."""
+    g = load("repack_int4_int8")
+    np.testing.assert_array_equal(casts.pack_int4_to_int8(g["codes"]), g["codes_packed"])
+    np.testing.assert_array_equal(casts.pack_int4_to_int8(g["wild"]), g["wild_packed"])
