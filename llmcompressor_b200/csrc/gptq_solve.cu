@@ -487,6 +487,7 @@ __global__ void k_copy2d(const float* __restrict__ src, int64_t lds, float* __re
 // ---------------------------------------------------------------------------
 constexpr int QB = 128;     // GPTQ block size handled by the kernel
 constexpr int SUB = 32;     // sub-block held in registers
+constexpr int CH = 8;       // columns per unrolled chunk of the sub-block
 constexpr int ROWS = 64;    // rows (threads) per CTA
 constexpr int QS_LD = QB + 1;
 
@@ -621,35 +622,49 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
     bool sfast = false;
     int64_t next_g = -1;  // first column of the next scale group
     for (int s0 = 0; s0 < cnt; s0 += SUB) {
+      // w[j]: column s0 + c8 + j of this row (a window that shifts left by CH
+      // columns per chunk), e: the sub-block's errors in column order.  The
+      // chunk body is the same for every c8, which keeps the code small
+      // enough for the instruction cache.
       float w[SUB], e[SUB];
 #pragma unroll
-      for (int j = 0; j < SUB; ++j) w[j] = QS[t * QS_LD + s0 + j];
+      for (int j = 0; j < SUB; ++j) { w[j] = QS[t * QS_LD + s0 + j]; e[j] = 0.f; }
       const int n = min(SUB, cnt - s0);
+      for (int c8 = 0; c8 < SUB; c8 += CH) {
+        float ebuf[CH];
 #pragma unroll
-      for (int ii = 0; ii < SUB; ++ii) {
-        e[ii] = 0.f;
-        if (ii < n) {
-          const int i = s0 + ii;
-          const int col = a.i1 + i;
-          if (col >= next_g) {
-            scale_of(a, row, col, s, z);
-            rs = __frcp_rn(s);
-            sfast = recip_ok(rs);
-            next_g = (a.strategy == LLMC_STRAT_GROUP) ? (col / a.gs + 1) * a.gs : (int64_t)1 << 62;
+        for (int k = 0; k < CH; ++k) {
+          const int ii = c8 + k;
+          float err = 0.f;
+          if (ii < n) {
+            const int i = s0 + ii;
+            const int col = a.i1 + i;
+            if (col >= next_g) {
+              scale_of(a, row, col, s, z);
+              rs = __frcp_rn(s);
+              sfast = recip_ok(rs);
+              next_g = (a.strategy == LLMC_STRAT_GROUP) ? (col / a.gs + 1) * a.gs : (int64_t)1 << 62;
+            }
+            const float d = U1[i * QB + i];
+            const float wi = w[k];
+            const float q = fake_quant(wi, s, rs, sfast, z, a.qmin, a.qmax);
+            QS[t * QS_LD + i] = q;
+            const float diff = wi - q;
+            const bool dfast = recip_ok(RD[i]) && recip_ok(RD2[i]);
+            const float dd = __fmul_rn(diff, diff);
+            loss += dfast ? div_mk(dd, D2[i], RD2[i]) : __fdiv_rn(dd, D2[i]);
+            err = dfast ? div_mk(diff, d, RD[i]) : __fdiv_rn(diff, d);
+            const float* urow = U1 + i * QB + s0 + c8;
+#pragma unroll
+            for (int j = k + 1; j < SUB; ++j)
+              if (c8 + j < SUB) w[j] -= err * urow[j];
           }
-          const float d = U1[i * QB + i];
-          const float wi = w[ii];
-          const float q = fake_quant(wi, s, rs, sfast, z, a.qmin, a.qmax);
-          QS[t * QS_LD + i] = q;
-          const float diff = wi - q;
-          const bool dfast = recip_ok(RD[i]) && recip_ok(RD2[i]);
-          const float dd = __fmul_rn(diff, diff);
-          loss += dfast ? div_mk(dd, D2[i], RD2[i]) : __fdiv_rn(dd, D2[i]);
-          const float err = dfast ? div_mk(diff, d, RD[i]) : __fdiv_rn(diff, d);
-          e[ii] = err;
-#pragma unroll
-          for (int j = ii + 1; j < SUB; ++j) w[j] -= err * U1[i * QB + s0 + j];
+          ebuf[k] = err;
         }
+#pragma unroll
+        for (int j = 0; j < SUB - CH; ++j) { w[j] = w[j + CH]; e[j] = e[j + CH]; }
+#pragma unroll
+        for (int k = 0; k < CH; ++k) { w[SUB - CH + k] = 0.f; e[SUB - CH + k] = ebuf[k]; }
       }
       // this sub-block's errors, row-major (rows x 128), as the K-major operand of the trailing update
       float4* erow = (float4*)(a.err + row * QB + s0);
