@@ -270,56 +270,53 @@ constexpr int PB = 128;
 constexpr int PLD = PB + 1;  // padded row stride of the shared-memory blocks
 // 16 warps: warp w walks rows (w, w+16, ...), its lanes walk the columns of a row.
 // Cholesky factor and inverse of the 32x32 diagonal sub-block at (o, o) of S
-// (row stride PLD) by one warp, written back as L into S and as L^-1 into X.
-// Lane i keeps a window of its row, a[m] = S[o+i][o+j+m], that shifts left as
-// the column j advances, so the loop body is the same for every j and the
-// code stays small (a fully unrolled 32x32 factorisation does not fit the
-// instruction cache).  The inverse is the same kind of loop: lane c carries
-// the right-hand side of column c of L^-1 in a shifting window t[].
-__device__ __forceinline__ void warp_chol_inv32(float* S, float* X, int o, int lane, int sz, bool& bad) {
-  float a[32];
-#pragma unroll
-  for (int l = 0; l < 32; ++l) a[l] = (lane < sz && l <= lane) ? S[(o + lane) * PLD + o + l] : 0.f;
+// (row stride PLD) by all 512 threads of the CTA, written back as L into S
+// and as L^-1 into X.
+//   factor:  right-looking, one column per step; thread t owns the two
+//            elements (t / 16, 2 (t % 16) + {0, 1}) of the block;
+//   inverse: warp w solves columns w and w + 16 of L^-1 by forward
+//            substitution, lane = row, the solved value broadcast by shuffle.
+__device__ __forceinline__ void cta_chol_inv32(float* S, float* X, int o, int sz, int* bad) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int r = t >> 4, c0 = (t & 15) * 2;
   for (int j = 0; j < sz; ++j) {
-    float p = __shfl_sync(0xffffffffu, a[0], j);
-    if (!(p > 0.0f)) { bad = true; p = 1.0f; }
+    __syncthreads();
+    float p = S[(o + j) * PLD + o + j];
+    if (!(p > 0.0f)) { if (t == 0) *bad = 1; p = 1.0f; }
     const float piv = sqrtf(p);
-    float a0 = a[0];
-    if (lane == j) a0 = piv;
-    else if (lane > j) a0 = __fdiv_rn(a0, piv);
-    if (lane >= j && lane < sz) S[(o + lane) * PLD + o + j] = a0;  // column j of L
+    if (r > j && r < sz && (c0 == j || c0 + 1 == j)) S[(o + r) * PLD + o + j] = __fdiv_rn(S[(o + r) * PLD + o + j], piv);
+    __syncthreads();
+    if (t == 0) S[(o + j) * PLD + o + j] = piv;
+    if (r < sz) {
+      const float lrj = S[(o + r) * PLD + o + j];
 #pragma unroll
-    for (int m = 1; m < 32; ++m) {
-      const float lmj = __shfl_sync(0xffffffffu, a0, min(j + m, 31));
-      if (lane >= j + m) a[m] -= a0 * lmj;
+      for (int u = 0; u < 2; ++u) {
+        const int c = c0 + u;
+        if (c > j && c <= r) S[(o + r) * PLD + o + c] -= lrj * S[(o + c) * PLD + o + j];
+      }
     }
-#pragma unroll
-    for (int m = 0; m < 31; ++m) a[m] = a[m + 1];
-    a[31] = 0.f;
   }
-  __syncwarp();
-  // column `lane` of X = L^-1 by forward substitution: t[m] = rhs of row j + m
-  float t[32];
+  __syncthreads();
+  // column c of X = L^-1: t_r = rhs of row r; x_l = t_l / L_ll, then t_r -= L_rl x_l
 #pragma unroll
-  for (int m = 0; m < 32; ++m) t[m] = (m == lane) ? 1.0f : 0.0f;
-  for (int j = 0; j < sz; ++j) {
-    const float xj = __fdiv_rn(t[0], S[(o + j) * PLD + o + j]);
-    if (lane < sz) X[(o + j) * PLD + o + lane] = (j >= lane) ? xj : 0.0f;
-#pragma unroll
-    for (int m = 1; m < 32; ++m)
-      if (j + m < sz) t[m] -= S[(o + j + m) * PLD + o + j] * xj;
-#pragma unroll
-    for (int m = 0; m < 31; ++m) t[m] = t[m + 1];
-    t[31] = 0.f;
+  for (int h = 0; h < 2; ++h) {
+    const int c = warp + 16 * h;
+    if (c >= sz) continue;
+    float tr = (lane == c) ? 1.0f : 0.0f;
+    for (int l = c; l < sz; ++l) {
+      const float xl = __shfl_sync(0xffffffffu, __fdiv_rn(tr, S[(o + l) * PLD + o + l]), l);
+      if (lane == l) X[(o + l) * PLD + o + c] = xl;
+      if (lane > l && lane < sz) tr -= S[(o + lane) * PLD + o + l] * xl;
+    }
   }
 }
 
 __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_t k0, int n, float* Linv,
                                                     int* status) {
-  // Blocked in 32-column sub-steps: warp 0 factors and inverts each 32x32
-  // diagonal sub-block in registers (shuffles), then all 16 warps apply the
-  // panel solve and the trailing update; the off-diagonal blocks of the
-  // inverse follow block-row by block-row.
+  // Blocked in 32-column sub-steps: the CTA factors and inverts each 32x32
+  // diagonal sub-block (cta_chol_inv32), then all 16 warps apply the panel
+  // solve and the trailing update; the off-diagonal blocks of the inverse
+  // follow block-row by block-row.
   extern __shared__ float sm[];
   float* S = sm;             // [PB][PLD]  L of this block (lower)
   float* X = sm + PB * PLD;  // [PB][PLD]  its inverse (lower)
@@ -350,11 +347,7 @@ __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_
   const int nsub = (n + SB - 1) / SB;
   for (int kb = 0; kb < nsub; ++kb) {
     const int o = kb * SB, sz = min(SB, n - o);
-    if (warp == 0) {
-      bool b = false;
-      warp_chol_inv32(S, X, o, lane, sz, b);
-      if (b) bad = 1;
-    }
+    cta_chol_inv32(S, X, o, sz, &bad);
     __syncthreads();
     const int r0 = o + sz, rem = n - r0;
     if (rem <= 0) break;
