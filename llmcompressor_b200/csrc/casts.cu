@@ -701,38 +701,126 @@ __device__ __forceinline__ void stream_span(const CastParams& p, int64_t e0, boo
   else st_v8((uint8_t*)p.out + e0, o);
 }
 
-template <int FMT, int BITS, int GROUP, int MODE>
-__global__ void __launch_bounds__(256, 3) k_stream(CastParams p) {
-  const int lane = threadIdx.x & 31;
-  const int64_t n = p.rows * p.cols;
-  const int64_t steps = (n + 1023) >> 10;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  int64_t it = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// Two ways to keep a warp's next spans in flight while it quantizes one.
+//
+// span_regs: the next span is loaded into registers (double buffer); one span
+// in flight per warp.  Cheapest when the per-group work is short (groups of
+// 64 or 128 values).
+//
+// span_ring: asynchronous copies into a per-warp ring of NBUF spans in shared
+// memory (2 KB each), NBUF - 1 spans in flight per warp without holding them
+// in registers.  Pays off for groups of 16 / 32 values, whose scale
+// arithmetic per span is longest.  A lane copies and later reads back only
+// its own 64 bytes (so no warp barrier is needed); its four 16-byte chunks
+// are stored in an order rotated by lane so that the reads are free of bank
+// conflicts.
+//
+// Both walk work units u = it, it + nwarps, ...; src(u, ptr) gives the
+// lane's 32 values of unit u (false past the end of its tensor: nothing is
+// read) and proc(u, w) quantizes them (it knows itself which lanes lie past
+// the end; their words are not used).  Each is called once per unit, in
+// increasing u, so either may keep a cursor.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int SPAN_WORDS = 512;  // 1024 bf16 values
+constexpr int NBUF = 3;
+template <int GROUP>
+constexpr bool use_ring() { return GROUP == 16 || GROUP == 32; }
+// resident CTAs per SM (the ring takes 48 KB of shared memory per CTA;
+// quantizing with stored qparams needs more than 64 registers a thread)
+template <int GROUP, int MODE>
+constexpr int stream_ctas() { return use_ring<GROUP>() && MODE != MODE_GIVEN ? 4 : 3; }
+
+template <class Src, class Proc>
+__device__ __forceinline__ void span_regs(int64_t it, int64_t units, int64_t nwarps, Src src, Proc proc) {
   uint32_t a[16], b[16];
-  auto load = [&](int64_t step, uint32_t* buf) {
-    int64_t e0 = (step << 10) + lane * 32;
-    if (e0 < n) {
-      ld_v8(p.w + e0, buf);
-      ld_v8(p.w + e0 + 16, buf + 8);
+  auto load = [&](int64_t u, uint32_t* buf) {
+    const uint16_t* ptr = nullptr;
+    if (src(u, ptr)) {
+      ld_v8(ptr, buf);
+      ld_v8(ptr + 16, buf + 8);
     } else {
 #pragma unroll
       for (int k = 0; k < 16; ++k) buf[k] = 0u;
     }
   };
-  if (it < steps) load(it, a);
-  while (it < steps) {
+  if (it < units) load(it, a);
+  while (it < units) {
     int64_t nx = it + nwarps;
-    if (nx < steps) load(nx, b);
-    int64_t e0 = (it << 10) + lane * 32;
-    stream_span<FMT, BITS, GROUP, MODE>(p, e0, e0 < n, a);
+    if (nx < units) load(nx, b);
+    proc(it, a);
     it = nx;
-    if (it >= steps) break;
+    if (it >= units) break;
     nx = it + nwarps;
-    if (nx < steps) load(nx, a);
-    e0 = (it << 10) + lane * 32;
-    stream_span<FMT, BITS, GROUP, MODE>(p, e0, e0 < n, b);
+    if (nx < units) load(nx, a);
+    proc(it, b);
     it = nx;
   }
+}
+
+template <class Src, class Proc>
+__device__ __forceinline__ void span_ring(int64_t it, int64_t units, int64_t nwarps, Src src, Proc proc) {
+  __shared__ __align__(16) uint32_t ring[8][NBUF][SPAN_WORDS];  // 48 KB for 8 warps
+  const int lane = threadIdx.x & 31;
+  const int rot = (lane >> 1) & 3;
+  uint32_t* mine = &ring[threadIdx.x >> 5][0][0] + lane * 16;
+  auto issue = [&](int64_t u, int slot) {
+    const uint16_t* ptr = nullptr;
+    if (u < units && src(u, ptr)) {
+      uint32_t* dst = mine + slot * SPAN_WORDS;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cp_async16(dst + ((k ^ rot) << 2), ptr + 8 * k);
+    }
+    cp_async_commit();  // one group per span, empty or not, so the counts stay aligned
+  };
+#pragma unroll
+  for (int s = 0; s < NBUF; ++s) issue(it + s * nwarps, s);
+  int slot = 0;
+  for (; it < units; it += nwarps) {
+    cp_async_wait_group<NBUF - 1>();  // this span's copies have landed
+    const uint32_t* from = mine + slot * SPAN_WORDS;
+    uint32_t w[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 v = *(const uint4*)(from + ((k ^ rot) << 2));
+      w[4 * k] = v.x; w[4 * k + 1] = v.y; w[4 * k + 2] = v.z; w[4 * k + 3] = v.w;
+    }
+    proc(it, w);
+    issue(it + NBUF * nwarps, slot);  // the slot is free again: its values are consumed
+    slot = (slot + 1 == NBUF) ? 0 : slot + 1;
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+template <int GROUP, class Src, class Proc>
+__device__ __forceinline__ void span_loop(int64_t units, Src src, Proc proc) {
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t it = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if constexpr (use_ring<GROUP>()) span_ring(it, units, nwarps, src, proc);
+  else span_regs(it, units, nwarps, src, proc);
+}
+
+template <int FMT, int BITS, int GROUP, int MODE>
+__global__ void __launch_bounds__(256, stream_ctas<GROUP, MODE>()) k_stream(CastParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = p.rows * p.cols;
+  auto src = [&](int64_t u, const uint16_t*& ptr) {
+    const int64_t e0 = (u << 10) + lane * 32;
+    ptr = p.w + e0;
+    return e0 < n;
+  };
+  auto proc = [&](int64_t u, const uint32_t* w) {
+    const int64_t e0 = (u << 10) + lane * 32;
+    stream_span<FMT, BITS, GROUP, MODE>(p, e0, e0 < n, w);
+  };
+  span_loop<GROUP>((n + 1023) >> 10, src, proc);
 }
 
 // ------------------------------------------------------------------------
@@ -986,40 +1074,30 @@ __device__ __forceinline__ CastParams job_params(const CastBatch& b, int j) {
 }
 
 template <int FMT, int BITS, int GROUP>
-__global__ void __launch_bounds__(256, 3) k_stream_batch(const __grid_constant__ CastBatch b) {
+__global__ void __launch_bounds__(256, stream_ctas<GROUP, MODE_FUSED>()) k_stream_batch(const __grid_constant__ CastBatch b) {
   const int lane = threadIdx.x & 31;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  int64_t it = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  uint32_t a[16], c[16];
-  int ja = 0, jc = 0;
-  int64_t ea = 0, ec = 0;
-  auto load = [&](int64_t u, uint32_t* buf, int& j, int64_t& e0) {
-    j = find_job(b, u);
-    const CastJob& jb = b.job[j];
-    e0 = ((u - jb.first) << 10) + lane * 32;
-    if (e0 < jb.rows * jb.cols) {
-      ld_v8(jb.w + e0, buf);
-      ld_v8(jb.w + e0 + 16, buf + 8);
-    }
+  // job cursors: units arrive in increasing order, so the job index only
+  // moves forward (one comparison per unit instead of a search)
+  const int64_t u0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int j0 = u0 < b.units ? find_job(b, u0) : 0;
+  int js = j0, jp = j0;
+  auto advance = [&](int& j, int64_t u) {
+    while (j + 1 < b.njobs && b.job[j + 1].first <= u) ++j;
   };
-  if (it < b.units) load(it, a, ja, ea);
-  while (it < b.units) {
-    int64_t nx = it + nwarps;
-    if (nx < b.units) load(nx, c, jc, ec);
-    {
-      const CastParams p = job_params(b, ja);
-      stream_span<FMT, BITS, GROUP, MODE_FUSED>(p, ea, ea < p.rows * p.cols, a);
-    }
-    it = nx;
-    if (it >= b.units) break;
-    nx = it + nwarps;
-    if (nx < b.units) load(nx, a, ja, ea);
-    {
-      const CastParams p = job_params(b, jc);
-      stream_span<FMT, BITS, GROUP, MODE_FUSED>(p, ec, ec < p.rows * p.cols, c);
-    }
-    it = nx;
-  }
+  auto src = [&](int64_t u, const uint16_t*& ptr) {
+    advance(js, u);
+    const CastJob& jb = b.job[js];
+    const int64_t e0 = ((u - jb.first) << 10) + lane * 32;
+    ptr = jb.w + e0;
+    return e0 < jb.rows * jb.cols;
+  };
+  auto proc = [&](int64_t u, const uint32_t* w) {
+    advance(jp, u);
+    const CastParams p = job_params(b, jp);
+    const int64_t e0 = ((u - b.job[jp].first) << 10) + lane * 32;
+    stream_span<FMT, BITS, GROUP, MODE_FUSED>(p, e0, e0 < p.rows * p.cols, w);
+  };
+  span_loop<GROUP>(b.units, src, proc);
 }
 
 // 128-thread CTAs, one group at a time without prefetch: several CTAs per SM
@@ -1181,13 +1259,14 @@ static int validate(const CastParams& p) {
 template <int FMT, int BITS, int MODE>
 static bool launch_stream(const CastParams& p, int64_t group, cudaStream_t st) {
   const int64_t steps = (p.rows * p.cols + 1023) / 1024;
-  dim3 g((unsigned)std::max<int64_t>(1, std::min<int64_t>((steps + 7) / 8, 148 * 3))), b(256);
+  const auto grid = [&](int ctas) { return dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>((steps + 7) / 8, 148 * ctas))); };
+  const dim3 b(256);
   constexpr bool fp4 = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4);
-  if (group == 16) k_stream<FMT, BITS, 16, MODE><<<g, b, 0, st>>>(p);
-  else if (group == 32) k_stream<FMT, BITS, 32, MODE><<<g, b, 0, st>>>(p);
+  if (group == 16) k_stream<FMT, BITS, 16, MODE><<<grid(stream_ctas<16, MODE>()), b, 0, st>>>(p);
+  else if (group == 32) k_stream<FMT, BITS, 32, MODE><<<grid(stream_ctas<32, MODE>()), b, 0, st>>>(p);
   else if constexpr (fp4) return false;
-  else if (group == 64) k_stream<FMT, BITS, 64, MODE><<<g, b, 0, st>>>(p);
-  else if (group == 128) k_stream<FMT, BITS, 128, MODE><<<g, b, 0, st>>>(p);
+  else if (group == 64) k_stream<FMT, BITS, 64, MODE><<<grid(stream_ctas<64, MODE>()), b, 0, st>>>(p);
+  else if (group == 128) k_stream<FMT, BITS, 128, MODE><<<grid(stream_ctas<128, MODE>()), b, 0, st>>>(p);
   else return false;
   llmc::note_launch();
   return true;
@@ -1354,14 +1433,15 @@ static bool launch_batch_fmt(CastBatch& b, cudaStream_t st) {
   b.units = units;
   if (units == 0) return true;
   if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
-    dim3 g((unsigned)std::max<int64_t>(1, std::min<int64_t>((units + 7) / 8, 148 * 3))), bl(256);
+    const auto grid = [&](int ctas) { return dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>((units + 7) / 8, 148 * ctas))); };
+    const dim3 bl(256);
     constexpr bool fp4 = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4);
     const int64_t group = a.group;
-    if (group == 16) k_stream_batch<FMT, BITS, 16><<<g, bl, 0, st>>>(b);
-    else if (group == 32) k_stream_batch<FMT, BITS, 32><<<g, bl, 0, st>>>(b);
+    if (group == 16) k_stream_batch<FMT, BITS, 16><<<grid(stream_ctas<16, MODE_FUSED>()), bl, 0, st>>>(b);
+    else if (group == 32) k_stream_batch<FMT, BITS, 32><<<grid(stream_ctas<32, MODE_FUSED>()), bl, 0, st>>>(b);
     else if constexpr (fp4) return false;
-    else if (group == 64) k_stream_batch<FMT, BITS, 64><<<g, bl, 0, st>>>(b);
-    else if (group == 128) k_stream_batch<FMT, BITS, 128><<<g, bl, 0, st>>>(b);
+    else if (group == 64) k_stream_batch<FMT, BITS, 64><<<grid(stream_ctas<64, MODE_FUSED>()), bl, 0, st>>>(b);
+    else if (group == 128) k_stream_batch<FMT, BITS, 128><<<grid(stream_ctas<128, MODE_FUSED>()), bl, 0, st>>>(b);
     else return false;
     llmc::note_launch();
     return true;
