@@ -117,6 +117,15 @@ int llmc_global_scale(const float* absmax_f32, float* global_scale_f32, void* st
 int llmc_calculate_qparams(const void* min_bf16, const void* max_bf16, int64_t n, const LlmcQuantArgs* args,
                            const float* global_scale, void* scale_out, void* zp_out, void* stream);
 
+/* llmc_calculate_qparams with the statistics' dtype given: f32_stats != 0
+ * evaluates calculate_qparams for statistics of a float32 tensor (every
+ * step in float32, float32 eps for zero scales, float32 scale_out) -- the
+ * re-observation of the permuted float32 weight under activation ordering
+ * GROUP (S/modifiers/gptq/gptq_quantize.py:141-145).  The min/max values
+ * still come as bf16 (the weight's values, exact in bf16).  Not for MX. */
+int llmc_calculate_qparams_ex(const void* min_bf16, const void* max_bf16, int64_t n, const LlmcQuantArgs* args,
+                              const float* global_scale, int f32_stats, void* scale_out, void* zp_out, void* stream);
+
 /* ---------------------------------------------------------------- casts
  * Quantize a bf16 weight with given parameters and pack it in a
  * compressed-tensors format: `compress` of PackedQuantizationCompressor
@@ -202,8 +211,8 @@ int llmc_hessian_tiles(int64_t d);
  *      (:189-196, round-to-nearest fallback).  workspace: see
  *      llmc_gptq_hinv_workspace_size.
  *   3. llmc_gptq_quantize: the blockwise column loop (:199-277) for one weight
- *      (rows x cols bf16) with stored bf16 scales / int8 zero points (TENSOR,
- *      CHANNEL or GROUP; blocksize 128), writing the fake-quantized bf16
+ *      (rows x cols bf16) with stored bf16 scales / int8 zero points (int
+ *      types; TENSOR, CHANNEL, GROUP or BLOCK; other options below), writing the fake-quantized bf16
  *      weight and the summed loss (float32 scalar).  Dead columns are zeroed
  *      first (:38).  HinvT (optional) is the transposed factor from step 2.  workspace: see llmc_gptq_quantize_workspace_size.
  * Nothing synchronises; *status is read by the caller when it needs it. */
@@ -216,6 +225,55 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
                        const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp,
                        int64_t blocksize, void* wq_bf16, float* loss, void* workspace, const int* status,
                        void* stream);
+
+/* Activation ordering and the other quantization options of the block loop
+ * (S/modifiers/gptq/gptq_quantize.py:120-166,209-256,279-293).
+ *
+ * llmc_gptq_actorder_perm: perm = argsort(diag(H), descending) -- equal
+ *   diagonal values keep index order (torch's sort leaves their order
+ *   unspecified).  d int32 outputs.
+ * llmc_gptq_permute_hessian: Hp = H[perm][:, perm] (Hp must not alias H).
+ *   The permuted Hessian then goes through llmc_gptq_prepare_hessian and
+ *   llmc_gptq_hinv as usual (dead columns and damping in the permuted order).
+ * llmc_permute_columns_bf16: dst[:, j] = src[:, perm[j]] -- the permuted
+ *   weight that activation ordering GROUP re-observes (:141-145).
+ * llmc_gptq_quantize_ex: llmc_gptq_quantize for TENSOR, CHANNEL, GROUP,
+ *   TENSOR_GROUP and BLOCK strategies, int (2..8 bits), FP8 (E4M3) and FP4
+ *   (E2M1) types, any block size >= 1 (blocks of more than 128 columns run
+ *   as 128-column steps, the same arithmetic in exact terms), with:
+ *     perm          solve column j is weight column perm[j] (order != 0); the
+ *                   output weight is in the weight's own column order.  perm
+ *                   must be a permutation of 0..cols-1 (entries outside
+ *                   [0, cols) are clamped, giving wrong results, not faults);
+ *     order         0: none; 1: WEIGHT / STATIC -- solve column j uses the
+ *                   scales of weight column perm[j]'s group (g_idx[perm]);
+ *                   2: GROUP -- solve column j uses group j / group_size
+ *                   (scales observed on the permuted weight) and g_idx_out
+ *                   receives weight column c's group (cols int32);
+ *     scale_is_f32  scales are float32 and dequantization runs in float32
+ *                   (else bf16 scales, bf16 products);
+ *     global_scale  TENSOR_GROUP (NVFP4): float32 device scalar; the
+ *                   effective scale is scale / global_scale in float32 and
+ *                   scales are float32.
+ *   Scale layouts: TENSOR (1), CHANNEL (rows), GROUP / TENSOR_GROUP
+ *   (rows, cols / group_size), BLOCK (ceil(rows / block_rows),
+ *   ceil(cols / block_cols)).  zp: int8, asymmetric int types only.
+ *   cx may be NULL (no ordering, bf16 scales). */
+typedef struct {
+  const int32_t* perm;
+  int32_t order;
+  int32_t scale_is_f32;
+  const float* global_scale;
+  int32_t* g_idx_out;
+} LlmcGptqColumns;
+int llmc_gptq_actorder_perm(const float* H, int64_t d, int32_t* perm, void* stream);
+int llmc_gptq_permute_hessian(const float* H, int64_t d, const int32_t* perm, float* Hp, void* stream);
+int llmc_permute_columns_bf16(const void* src, int64_t rows, int64_t cols, const int32_t* perm, void* dst,
+                              void* stream);
+int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
+                          const uint8_t* dead, const LlmcQuantArgs* args, const void* scale, const int8_t* zp,
+                          const LlmcGptqColumns* cx, int64_t blocksize, void* wq_bf16, float* loss,
+                          void* workspace, const int* status, void* stream);
 
 /* Float32-accurate GEMM on the tensor cores (3xTF32 split):
  *   C (m x n, ldc) = A*B^T (mode 0), C - A*B^T (mode 1) or -A*B^T (mode 2),

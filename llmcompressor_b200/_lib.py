@@ -85,6 +85,7 @@ _SIGS = {
     "llmc_absmax_accumulate": [_P, _I64, _P, _P],
     "llmc_global_scale": [_P, _P, _P],
     "llmc_calculate_qparams": [_P, _P, _I64, _QA, _P, _P, _P, _P],
+    "llmc_calculate_qparams_ex": [_P, _P, _I64, _QA, _P, ctypes.c_int, _P, _P, _P],
     "llmc_quantize_pack": [_P, _I64, _I64, _QA, _P, _I32, _P, _P, _I32, _P, _P],
     "llmc_modelfree_quantize": [_P, _I64, _I64, _QA, _P, _I32, _P, _P, _P, _P],
     "llmc_pack_zero_point": [_P, _I64, _I64, _I32, _P, _P],

@@ -1157,13 +1157,14 @@ __global__ void k_absmax(const uint16_t* w, int64_t n, float* out) {
 __global__ void k_global_scale(const float* absmax, float* gs) { *gs = global_scale_from_absmax(*absmax); }
 
 __global__ void k_qparams(const uint16_t* mn, const uint16_t* mx, int64_t n, QArgs a, const float* gs,
-                          void* scale_out, void* zp_out) {
+                          void* scale_out, void* zp_out, int f32stats) {
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float zp;
   bool has_gs = gs != nullptr;
-  float s = group_qparams(bf16_to_f(mn[i]), bf16_to_f(mx[i]), a, has_gs, has_gs ? *gs : 0.f, &zp);
-  bool f32out = has_gs;  // otherwise the statistics' dtype (bf16), as round_to_quantized_type_dtype casts back
+  float s = group_qparams(bf16_to_f(mn[i]), bf16_to_f(mx[i]), a, has_gs, has_gs ? *gs : 0.f, &zp, f32stats != 0);
+  // otherwise the statistics' dtype (bf16), as round_to_quantized_type_dtype casts back
+  bool f32out = has_gs || f32stats;
   if (f32out) ((float*)scale_out)[i] = s;
   else ((uint16_t*)scale_out)[i] = f_to_bf16(s);
   if (zp_out) {
@@ -1555,15 +1556,22 @@ int llmc_global_scale(const float* absmax, float* gs, void* stream) {
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
-int llmc_calculate_qparams(const void* mn, const void* mx, int64_t n, const LlmcQuantArgs* args, const float* gs,
-                           void* scale_out, void* zp_out, void* stream) {
+int llmc_calculate_qparams_ex(const void* mn, const void* mx, int64_t n, const LlmcQuantArgs* args, const float* gs,
+                              int f32stats, void* scale_out, void* zp_out, void* stream) {
   if (!mn || !mx || !args || !scale_out || n < 0) return LLMC_EINVAL_ARG;
   QArgs a = to_qargs(*args);
   if (a.is_float && !a.symmetric && a.bits == 4) return LLMC_ENOSUPPORT;
+  if (f32stats && a.is_mx()) return LLMC_ENOSUPPORT;  // MX exponents are taken from bf16 bit patterns
   if (n == 0) return LLMC_OK;
   k_qparams<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint16_t*)mn, (const uint16_t*)mx,
-                                                                            n, a, gs, scale_out, zp_out); llmc::note_launch();
+                                                                            n, a, gs, scale_out, zp_out, f32stats);
+  llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_calculate_qparams(const void* mn, const void* mx, int64_t n, const LlmcQuantArgs* args, const float* gs,
+                           void* scale_out, void* zp_out, void* stream) {
+  return llmc_calculate_qparams_ex(mn, mx, n, args, gs, 0, scale_out, zp_out, stream);
 }
 
 int llmc_quantize_pack(const void* w, int64_t rows, int64_t cols, const LlmcQuantArgs* args, const void* scale,

@@ -484,6 +484,9 @@ constexpr int CH = 8;       // columns per unrolled chunk of the sub-block
 constexpr int ROWS = 64;    // rows (threads) per CTA
 constexpr int QS_LD = QB + 1;
 
+// quantized value types of the fake-quantization step
+enum { QF_INT = 0, QF_FP8 = 1, QF_FP4 = 2 };
+
 struct BlockArgs {
   float* W;            // r x c float32 working weight
   int64_t r, c;
@@ -497,6 +500,15 @@ struct BlockArgs {
   float* err;          // rows x QB row-major errors of this block
   float* loss;         // r per-row losses
   const int* status;   // ENOT_PD -> identity
+  // per-column variant (k_gptq_block<true>) only:
+  const float* scale_f;   // float32 scales instead of `scale`
+  const float* gsc;       // global scale (device scalar): effective scale = scale / gsc
+  int qf;                 // QF_*
+  int f32deq;             // dequantize in float32 (float32 scales) instead of bf16
+  const int32_t* perm;    // activation ordering WEIGHT: the group of solve column j is that of perm[j]
+  int64_t gdiv;           // columns per scale column (group size, block width; 0: one scale column)
+  int64_t rdiv;           // rows per scale row (1, block height; 0: one scale row)
+  int64_t sld;            // scale columns per scale row
 };
 
 __device__ __forceinline__ void scale_of(const BlockArgs& a, int64_t row, int col, float& s, float& z) {
@@ -529,6 +541,37 @@ __device__ __forceinline__ float fake_quant(float w, float s, float rs, bool fas
   return rbf(deq * s);
 }
 
+// perm[j], kept inside [0, c) so that a caller's malformed permutation
+// cannot send a load or store out of bounds (it gives wrong results instead)
+__device__ __forceinline__ int64_t perm_at(const int32_t* perm, int64_t j, int64_t c) {
+  const int64_t p = perm[j];
+  return p < 0 ? 0 : (p >= c ? c - 1 : p);
+}
+
+// E2M1 grid value of a code from e2m1_code (magnitude index, sign bit 8)
+__device__ __forceinline__ float fp4_grid(uint32_t code) {
+  const uint32_t m = code & 7u;
+  const float v = (m < 4u) ? 0.5f * (float)m : (m == 4u) ? 2.0f : (m == 5u) ? 3.0f : (m == 6u) ? 4.0f : 6.0f;
+  return (code & 8u) ? -v : v;
+}
+
+// fake_quantize of one float32 value for every quantized type
+// (CT forward_helpers.py _quantize_dequantize): float32 quotient, + zp,
+// clamp, round (half-even integer, RNE E4M3 cast, cast_to_fp4 thresholds),
+// back to the scale's dtype, - zp, times the scale: bf16 products for bf16
+// scales, float32 for float32 scales (NVFP4's effective scale
+// scale / global_scale, or statistics observed in float32).
+__device__ __forceinline__ float fake_quant_any(float w, float s, float rs, bool fast, float z, float qmin, float qmax,
+                                               int qf, bool f32deq) {
+  float q = (fast ? div_mk(w, s, rs) : __fdiv_rn(w, s)) + z;
+  q = fminf(fmaxf(q, qmin), qmax);
+  if (qf == QF_INT) q = rintf(q);
+  else if (qf == QF_FP8) q = round_e4m3(q);
+  else q = fp4_grid(e2m1_code(q));
+  if (f32deq) return __fmul_rn(q - z, s);
+  return rbf(rbf(q - z) * s);
+}
+
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
                "l"(gsrc)
@@ -541,6 +584,12 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // the rows of W with batched vector loads, so staging costs a few memory
 // round trips; the 32 columns of a sub-block live in registers with every
 // index known at compile time; divisions use per-column reciprocals.
+//
+// PERCOL = true: every column looks up its own scale and zero point (loaded
+// eight columns ahead), for activation ordering, block scales, float32
+// scales and the FP8 / FP4 types; PERCOL = false: integer types with bf16
+// scales in column order, the scale reloaded only where a group starts.
+template <bool PERCOL>
 __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
   extern __shared__ float sm[];
   float* U1 = sm;                  // [QB][QB]
@@ -548,6 +597,7 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
   float* RD = QS + ROWS * QS_LD;   // [QB]  RN(1/d)
   float* D2 = RD + QB;             // [QB]  RN(d*d)
   float* RD2 = D2 + QB;            // [QB]  RN(1/(d*d))
+  int* G = (int*)(RD2 + QB);       // [QB]  scale column of each column (PERCOL)
   const int t = threadIdx.x;
   const int64_t row0 = (int64_t)blockIdx.x * ROWS;
   const int64_t row = row0 + t;
@@ -606,6 +656,11 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
     RD[i] = __frcp_rn(d);
     D2[i] = d2;
     RD2[i] = __frcp_rn(d2);
+    if (PERCOL) {
+      const int64_t col = a.i1 + i;
+      const int64_t src = (a.perm && col < a.c) ? perm_at(a.perm, col, a.c) : col;
+      G[i] = a.gdiv > 0 ? (int)(src / a.gdiv) : 0;
+    }
   }
   __syncthreads();
 
@@ -614,6 +669,8 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
     float s = 0.f, z = 0.f, rs = 0.f;
     bool sfast = false;
     int64_t next_g = -1;  // first column of the next scale group
+    const int64_t rowpart = PERCOL ? (a.rdiv > 0 ? row / a.rdiv : 0) * a.sld : 0;
+    const float gsv = (PERCOL && a.gsc) ? *a.gsc : 1.0f;
     for (int s0 = 0; s0 < cnt; s0 += SUB) {
       // w[j]: column s0 + c8 + j of this row (a window that shifts left by CH
       // columns per chunk), e: the sub-block's errors in column order.  The
@@ -625,6 +682,22 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
       const int n = min(SUB, cnt - s0);
       for (int c8 = 0; c8 < SUB; c8 += CH) {
         float ebuf[CH];
+        float sk[CH], zk[CH];
+        if (PERCOL) {  // this chunk's scales, all loads in flight together
+#pragma unroll
+          for (int k = 0; k < CH; ++k) {
+            sk[k] = 1.0f; zk[k] = 0.0f;
+            if (c8 + k < n) {
+              const int64_t idx = rowpart + G[s0 + c8 + k];
+              sk[k] = a.scale_f ? a.scale_f[idx] : bf16_to_f(a.scale[idx]);
+              zk[k] = a.zp ? (float)a.zp[idx] : 0.0f;
+            }
+          }
+          if (a.gsc) {
+#pragma unroll
+            for (int k = 0; k < CH; ++k) sk[k] = __fdiv_rn(sk[k], gsv);
+          }
+        }
 #pragma unroll
         for (int k = 0; k < CH; ++k) {
           const int ii = c8 + k;
@@ -632,15 +705,23 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
           if (ii < n) {
             const int i = s0 + ii;
             const int col = a.i1 + i;
-            if (col >= next_g) {
-              scale_of(a, row, col, s, z);
-              rs = __frcp_rn(s);
-              sfast = recip_ok(rs);
-              next_g = (a.strategy == LLMC_STRAT_GROUP) ? (col / a.gs + 1) * a.gs : (int64_t)1 << 62;
-            }
             const float d = U1[i * QB + i];
             const float wi = w[k];
-            const float q = fake_quant(wi, s, rs, sfast, z, a.qmin, a.qmax);
+            float q;
+            if (PERCOL) {
+              s = sk[k]; z = zk[k];
+              rs = __frcp_rn(s);
+              sfast = s > 0.0f && recip_ok(rs);
+              q = fake_quant_any(wi, s, rs, sfast, z, a.qmin, a.qmax, a.qf, a.f32deq != 0);
+            } else {
+              if (col >= next_g) {
+                scale_of(a, row, col, s, z);
+                rs = __frcp_rn(s);
+                sfast = recip_ok(rs);
+                next_g = (a.strategy == LLMC_STRAT_GROUP) ? (col / a.gs + 1) * a.gs : (int64_t)1 << 62;
+              }
+              q = fake_quant(wi, s, rs, sfast, z, a.qmin, a.qmax);
+            }
             QS[t * QS_LD + i] = q;
             const float diff = wi - q;
             const bool dfast = recip_ok(RD[i]) && recip_ok(RD2[i]);
@@ -691,18 +772,87 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
   }
 }
 
+// W (float32, solve column order) from the bf16 weight; solve column j is
+// weight column perm[j] (activation ordering) and dead columns are zero.
 __global__ void k_init_w(const uint16_t* __restrict__ w, float* __restrict__ W, int64_t r, int64_t c,
-                         const uint8_t* dead) {
+                         const uint8_t* dead, const int32_t* perm) {
   const int64_t n = r * c;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t col = i % c;
-    W[i] = (dead && dead[col]) ? 0.0f : bf16_to_f(w[i]);
+    const int64_t src = perm ? (i - col) + perm_at(perm, col, c) : i;
+    W[i] = (dead && dead[col]) ? 0.0f : bf16_to_f(w[src]);
   }
 }
 
 __global__ void k_finish(const float* __restrict__ W, uint16_t* __restrict__ out, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = f_to_bf16(W[i]);
+}
+
+// back to the weight's column order: out[:, perm[j]] = W[:, j]
+__global__ void k_finish_perm(const float* __restrict__ W, uint16_t* __restrict__ out, int64_t r, int64_t c,
+                              const int32_t* __restrict__ perm) {
+  const int64_t n = r * c;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t col = i % c;
+    out[(i - col) + perm_at(perm, col, c)] = f_to_bf16(W[i]);
+  }
+}
+
+// g_idx of activation ordering GROUP (S/modifiers/gptq/gptq_quantize.py:166,292-293):
+// weight column perm[j] belongs to group j / gs
+__global__ void k_gidx_group(const int32_t* __restrict__ perm, int64_t c, int64_t gs, int32_t* __restrict__ g_idx) {
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < c; j += (int64_t)gridDim.x * blockDim.x)
+    g_idx[perm_at(perm, j, c)] = (int32_t)(j / gs);
+}
+
+// Activation order (S/modifiers/gptq/gptq_quantize.py:299-310,
+// torch.argsort(diag(H), descending=True)): perm[rank] = i with rank = the
+// number of diagonal entries that sort before entry i -- larger values
+// first, equal values in index order.  Keys are the float bits made
+// monotonic (every value, NaN included, gets a distinct total order), so
+// the ranks are a permutation of 0..d-1.
+__device__ __forceinline__ uint32_t desc_key(float f) {
+  if (f == 0.0f) f = 0.0f;  // -0 ties with +0
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__global__ void __launch_bounds__(256) k_actorder_perm(const float* __restrict__ H, int64_t d, int32_t* __restrict__ perm) {
+  __shared__ uint32_t keys[256];
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t ki = i < d ? desc_key(H[i * d + i]) : 0u;
+  int64_t rank = 0;
+  for (int64_t t0 = 0; t0 < d; t0 += 256) {
+    __syncthreads();
+    const int64_t j = t0 + threadIdx.x;
+    keys[threadIdx.x] = j < d ? desc_key(H[j * d + j]) : 0u;
+    __syncthreads();
+    const int m = (d - t0) < 256 ? (int)(d - t0) : 256;
+    for (int jj = 0; jj < m; ++jj) {
+      const uint32_t kj = keys[jj];
+      rank += (kj > ki) || (kj == ki && t0 + jj < i);
+    }
+  }
+  if (i < d) perm[rank] = (int32_t)i;
+}
+
+// Hp = H[perm][:, perm]
+__global__ void k_permute_sym(const float* __restrict__ H, int64_t d, const int32_t* __restrict__ perm,
+                              float* __restrict__ Hp) {
+  const int64_t i = blockIdx.y;
+  const float* src = H + perm_at(perm, i, d) * d;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < d; j += (int64_t)gridDim.x * blockDim.x)
+    Hp[i * d + j] = src[perm_at(perm, j, d)];
+}
+
+// dst[:, j] = src[:, perm[j]] for 2-byte elements
+__global__ void k_permute_cols16(const uint16_t* __restrict__ src, int64_t r, int64_t c, const int32_t* __restrict__ perm,
+                                 uint16_t* __restrict__ dst) {
+  const int64_t n = r * c;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t col = i % c;
+    dst[i] = src[(i - col) + perm_at(perm, col, c)];
+  }
 }
 
 __global__ void k_sum(const float* __restrict__ x, int64_t n, float* out) {
@@ -816,41 +966,78 @@ int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes
   return LLMC_OK;
 }
 
-int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
-                       const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp,
-                       int64_t blocksize, void* wq_bf16, float* loss_out, void* workspace, const int* status,
-                       void* stream) {
-  if (!args || !Hinv || !loss_out || !workspace || rows < 0 || cols <= 0) return LLMC_EINVAL_ARG;
-  if (blocksize != QB) return LLMC_ENOSUPPORT;
+int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
+                          const uint8_t* dead, const LlmcQuantArgs* args, const void* scale, const int8_t* zp,
+                          const LlmcGptqColumns* cx, int64_t blocksize, void* wq_bf16, float* loss_out,
+                          void* workspace, const int* status, void* stream) {
+  if (!args || !Hinv || !loss_out || !workspace || rows < 0 || cols <= 0 || blocksize < 1) return LLMC_EINVAL_ARG;
+  const LlmcGptqColumns none = {};
+  const LlmcGptqColumns& x = cx ? *cx : none;
   QArgs q = to_qargs(*args);
-  if (q.is_float) return LLMC_ENOSUPPORT;
-  if (q.strategy != LLMC_STRAT_TENSOR && q.strategy != LLMC_STRAT_CHANNEL && q.strategy != LLMC_STRAT_GROUP)
+  if (q.strategy != LLMC_STRAT_TENSOR && q.strategy != LLMC_STRAT_CHANNEL && q.strategy != LLMC_STRAT_GROUP &&
+      q.strategy != LLMC_STRAT_TENSOR_GROUP && q.strategy != LLMC_STRAT_BLOCK)
     return LLMC_ENOSUPPORT;
-  if (q.strategy == LLMC_STRAT_GROUP && (q.group <= 0 || cols % q.group)) return LLMC_EINVAL_SHAPE;
+  if (q.is_float && (q.bits != 8 && q.bits != 4)) return LLMC_ENOSUPPORT;
+  if (!q.is_float && (q.bits < 2 || q.bits > 8)) return LLMC_ENOSUPPORT;
+  if (q.is_float && !q.symmetric && q.bits == 4) return LLMC_ENOSUPPORT;  // asymmetric FP4
+  const bool grouped = q.strategy == LLMC_STRAT_GROUP || q.strategy == LLMC_STRAT_TENSOR_GROUP;
+  if (grouped && (q.group <= 0 || cols % q.group)) return LLMC_EINVAL_SHAPE;
+  if (q.strategy == LLMC_STRAT_BLOCK && (q.bh <= 0 || q.bw <= 0)) return LLMC_EINVAL_ARG;
+  if (q.strategy == LLMC_STRAT_TENSOR_GROUP && !x.global_scale) return LLMC_EINVAL_ARG;
+  if (x.order < 0 || x.order > 2 || (x.order != 0 && !x.perm)) return LLMC_EINVAL_ARG;
+  if (x.order == 2 && (!grouped || !x.g_idx_out)) return LLMC_EINVAL_ARG;
+  if (!scale && rows > 0) return LLMC_EINVAL_ARG;
   cudaStream_t st = (cudaStream_t)stream;
+  if (x.order == 2) {
+    k_gidx_group<<<grid_for(cols), 256, 0, st>>>(x.perm, cols, q.group, x.g_idx_out); llmc::note_launch();
+  }
   if (rows == 0) {
     return cudaMemsetAsync(loss_out, 0, sizeof(float), st) == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
   }
   if ((uintptr_t)workspace % 16) return LLMC_EINVAL_ARG;
+  // the per-column kernel for everything but integer types with bf16 scales in column order
+  const bool percol = q.is_float || x.order != 0 || x.scale_is_f32 || x.global_scale ||
+                      q.strategy == LLMC_STRAT_TENSOR_GROUP || q.strategy == LLMC_STRAT_BLOCK;
   float* W = (float*)workspace;
   float* E = W + ((rows * cols + 3) & ~(int64_t)3);  // 16-byte aligned rows for the vector stores
   float* L = E + (int64_t)QB * rows;
-  k_init_w<<<grid_for(rows * cols), 256, 0, st>>>((const uint16_t*)w_bf16, W, rows, cols, dead); llmc::note_launch();
+  k_init_w<<<grid_for(rows * cols), 256, 0, st>>>((const uint16_t*)w_bf16, W, rows, cols, dead, x.perm);
+  llmc::note_launch();
   if (cudaMemsetAsync(L, 0, sizeof(float) * rows, st) != cudaSuccess) return LLMC_ECUDA;
-  static uint64_t attr_mask = 0;
-  const int smem = (QB * QB + ROWS * QS_LD + 3 * QB) * (int)sizeof(float);
-  if (!set_smem_attr(k_gptq_block, smem, &attr_mask)) return LLMC_ECUDA;
-  BlockArgs ba;
+  static uint64_t attr_mask[2] = {0, 0};
+  const int smem = (QB * QB + ROWS * QS_LD + 4 * QB) * (int)sizeof(float);
+  if (!set_smem_attr(k_gptq_block<false>, smem, &attr_mask[0])) return LLMC_ECUDA;
+  if (!set_smem_attr(k_gptq_block<true>, smem, &attr_mask[1])) return LLMC_ECUDA;
+  BlockArgs ba = {};
   ba.W = W; ba.r = rows; ba.c = cols; ba.U = Hinv;
-  ba.scale = (const uint16_t*)scale_bf16; ba.zp = q.symmetric ? nullptr : zp;
+  ba.zp = q.symmetric ? nullptr : zp;
   ba.strategy = q.strategy; ba.gs = q.group > 0 ? q.group : 1;
   ba.qmin = q.qmin(); ba.qmax = q.qmax();
   ba.err = E; ba.loss = L; ba.status = status;
+  const bool f32s = x.scale_is_f32 || x.global_scale;
+  ba.scale = f32s ? nullptr : (const uint16_t*)scale;
+  ba.scale_f = f32s ? (const float*)scale : nullptr;
+  ba.gsc = x.global_scale;
+  ba.qf = !q.is_float ? QF_INT : (q.bits == 8 ? QF_FP8 : QF_FP4);
+  ba.f32deq = f32s ? 1 : 0;
+  ba.perm = x.order == 1 ? x.perm : nullptr;  // GROUP ordering: scale groups follow the solve order
+  switch (q.strategy) {
+    case LLMC_STRAT_TENSOR: ba.gdiv = 0; ba.rdiv = 0; ba.sld = 0; break;
+    case LLMC_STRAT_CHANNEL: ba.gdiv = 0; ba.rdiv = 1; ba.sld = 1; break;
+    case LLMC_STRAT_BLOCK: ba.gdiv = q.bw; ba.rdiv = q.bh; ba.sld = (cols + q.bw - 1) / q.bw; break;
+    default: ba.gdiv = q.group; ba.rdiv = 1; ba.sld = cols / q.group; break;
+  }
+  // blocks of min(blocksize, 128) columns: for blocksize > 128 the lazy
+  // updates are applied in more steps, which is the same arithmetic in
+  // exact terms (GPTQ's result does not depend on the block size)
+  const int64_t step = std::min<int64_t>(blocksize, QB);
   const unsigned nblk = (unsigned)((rows + ROWS - 1) / ROWS);
-  for (int64_t i1 = 0; i1 < cols; i1 += QB) {
-    const int cnt = (int)std::min<int64_t>(QB, cols - i1);
+  for (int64_t i1 = 0; i1 < cols; i1 += step) {
+    const int cnt = (int)std::min<int64_t>(step, cols - i1);
     ba.i1 = (int)i1; ba.count = cnt;
-    k_gptq_block<<<nblk, ROWS, smem, st>>>(ba); llmc::note_launch();
+    if (percol) k_gptq_block<true><<<nblk, ROWS, smem, st>>>(ba);
+    else k_gptq_block<false><<<nblk, ROWS, smem, st>>>(ba);
+    llmc::note_launch();
     const int64_t i2 = i1 + cnt;
     if (i2 < cols) {
       // W[:, i2:] -= Err1 * Hinv[i1:i2, i2:]   (Err1 row-major: rows x QB).  With the
@@ -867,8 +1054,42 @@ int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const flo
       }
     }
   }
-  k_finish<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows * cols); llmc::note_launch();
+  if (x.perm) k_finish_perm<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows, cols, x.perm);
+  else k_finish<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows * cols);
+  llmc::note_launch();
   k_sum<<<1, 1024, 0, st>>>(L, rows, loss_out); llmc::note_launch();
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
+                       const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp,
+                       int64_t blocksize, void* wq_bf16, float* loss_out, void* workspace, const int* status,
+                       void* stream) {
+  return llmc_gptq_quantize_ex(w_bf16, rows, cols, Hinv, HinvT, dead, args, scale_bf16, zp, nullptr, blocksize,
+                               wq_bf16, loss_out, workspace, status, stream);
+}
+
+int llmc_gptq_actorder_perm(const float* H, int64_t d, int32_t* perm, void* stream) {
+  if (!H || !perm || d <= 0) return LLMC_EINVAL_ARG;
+  k_actorder_perm<<<(unsigned)((d + 255) / 256), 256, 0, (cudaStream_t)stream>>>(H, d, perm); llmc::note_launch();
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_gptq_permute_hessian(const float* H, int64_t d, const int32_t* perm, float* Hp, void* stream) {
+  if (!H || !perm || !Hp || d <= 0 || d > 0x7FFFFFFF || H == Hp) return LLMC_EINVAL_ARG;
+  dim3 g((unsigned)std::min<int64_t>((d + 255) / 256, 8), (unsigned)d);
+  k_permute_sym<<<g, 256, 0, (cudaStream_t)stream>>>(H, d, perm, Hp); llmc::note_launch();
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_permute_columns_bf16(const void* src, int64_t rows, int64_t cols, const int32_t* perm, void* dst,
+                              void* stream) {
+  if (!perm || rows < 0 || cols <= 0 || ((!src || !dst) && rows > 0) || (src == dst && rows > 0))
+    return LLMC_EINVAL_ARG;
+  if (rows == 0) return LLMC_OK;
+  k_permute_cols16<<<grid_for(rows * cols), 256, 0, (cudaStream_t)stream>>>((const uint16_t*)src, rows, cols, perm,
+                                                                            (uint16_t*)dst);
+  llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 

@@ -141,30 +141,33 @@ __device__ __forceinline__ float e8m0_to_f(uint32_t e) {
   return __uint_as_float(1u << (k + 149));    // subnormal (k = -127)
 }
 
-// Scale/zero-point of one group from its bf16 min/max: compressed-tensors
-// calculate_qparams with the reference's dtype semantics.  has_gs: a float32
-// global scale multiplies the bf16 scale (the product is float32).
+// Scale/zero-point of one group from its min/max: compressed-tensors
+// calculate_qparams with the reference's dtype semantics.  The statistics
+// are bf16 (the observed weight's dtype; every step rounds to bf16) unless
+// f32stats (a float32 observed tensor: every step stays float32).  has_gs: a
+// float32 global scale multiplies the scale (the product is float32).
 // Returns the scale as a float value on the grid of the stored scale dtype;
 // *zp_out gets the zero point (already rounded to its integer dtype).
 __device__ __forceinline__ float group_qparams(float mn, float mx, const QArgs& a, bool has_gs, float gs,
-                                               float* zp_out) {
+                                               float* zp_out, bool f32stats = false) {
   mn = fminf(mn, 0.0f);
   mx = fmaxf(mx, 0.0f);
   float qmin = a.qmin(), qmax = a.qmax();
   float br = qmax - qmin;
   float scale, zp = 0.0f;
-  bool f32dtype = false;
+  bool f32dtype = f32stats;
+  auto R = [f32stats](float v) { return f32stats ? v : rbf(v); };
   if (a.symmetric) {
     float mvp = fmaxf(fabsf(mn), fabsf(mx));
     if (a.is_mx()) {
       uint32_t e = mx_e8m0_from_absmax(mvp, a.bits);
       scale = (float)e;  // the bf16 exponent value, converted below
     } else {
-      scale = rbf(__fdiv_rn(mvp, br * 0.5f));
+      scale = R(__fdiv_rn(mvp, br * 0.5f));
     }
   } else {
-    scale = rbf(__fdiv_rn(rbf(mx - mn), br));
-    zp = rbf(qmin - rbf(__fdiv_rn(mn, scale)));
+    scale = R(__fdiv_rn(R(mx - mn), br));
+    zp = R(qmin - R(__fdiv_rn(mn, scale)));
     if (!isnan(zp)) zp = fminf(fmaxf(zp, qmin), qmax);
   }
   if (has_gs) { scale = gs * scale; f32dtype = true; }

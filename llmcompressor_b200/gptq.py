@@ -107,6 +107,75 @@ _lib.extend_signatures(
 )
 
 
+class GptqColumns(ctypes.Structure):
+    """LlmcGptqColumns (include/llmc_b200.h)."""
+
+    _fields_ = [
+        ("perm", ctypes.c_void_p),
+        ("order", ctypes.c_int32),
+        ("scale_is_f32", ctypes.c_int32),
+        ("global_scale", ctypes.c_void_p),
+        ("g_idx_out", ctypes.c_void_p),
+    ]
+
+
+_lib.extend_signatures(
+    {
+        "llmc_gptq_actorder_perm": [_P, _I64, _P, _P],
+        "llmc_gptq_permute_hessian": [_P, _I64, _P, _P, _P],
+        "llmc_permute_columns_bf16": [_P, _I64, _I64, _P, _P, _P],
+        "llmc_gptq_quantize_ex": [_P, _I64, _I64, _P, _P, _P, ctypes.POINTER(_lib.QuantArgs), _P, _P,
+                                  ctypes.POINTER(GptqColumns), _I64, _P, _P, _P, _P, _P],
+    }
+)
+
+_ORDER_CODE = {None: 0, "weight": 1, "group": 2}
+
+
+def resolve_actorder(actorder) -> str | None:
+    """The ordering ``quantize_weight`` applies (S/modifiers/gptq/gptq_quantize.py:120-166):
+    None, "weight" (WEIGHT, and STATIC -- its alias) or "group" (GROUP, and
+    DYNAMIC -- its alias)."""
+    a = getattr(actorder, "value", actorder)
+    table = {None: None, "static": "weight", "weight": "weight", "dynamic": "group", "group": "group"}
+    if a not in table:
+        raise ValueError(f"unknown activation ordering {actorder!r}")
+    return table[a]
+
+
+def actorder_perm(H: torch.Tensor) -> torch.Tensor:
+    """``torch.argsort(torch.diag(H), descending=True)``
+    (S/modifiers/gptq/gptq_quantize.py:299-310) on the GPU; equal diagonal
+    values keep index order.  int32 (d,)."""
+    require_cuda(H)
+    d = H.shape[0]
+    perm = torch.empty(d, dtype=torch.int32, device=H.device)
+    check(lib().llmc_gptq_actorder_perm(ptr(H), d, ptr(perm), stream_ptr(H.device)), "gptq_actorder_perm")
+    return perm
+
+
+def permute_hessian(H: torch.Tensor, perm: torch.Tensor) -> torch.Tensor:
+    """``H[perm][:, perm]`` into a new tensor."""
+    require_cuda(H, perm)
+    d = H.shape[0]
+    out = torch.empty_like(H)
+    check(lib().llmc_gptq_permute_hessian(ptr(H), d, ptr(perm), ptr(out), stream_ptr(H.device)),
+          "gptq_permute_hessian")
+    return out
+
+
+def permute_columns(w: torch.Tensor, perm: torch.Tensor) -> torch.Tensor:
+    """``w[:, perm]`` of a bf16 weight into a new tensor."""
+    require_cuda(w, perm)
+    if w.dtype != torch.bfloat16:
+        raise NotImplementedError(f"weights of dtype {w.dtype}: the GPTQ kernels take bf16 weights")
+    w = w.contiguous()
+    out = torch.empty_like(w)
+    check(lib().llmc_permute_columns_bf16(ptr(w), w.shape[0], w.shape[1], ptr(perm), ptr(out),
+                                          stream_ptr(w.device)), "permute_columns")
+    return out
+
+
 def _ws_bytes(fn, *args) -> int:
     out = ctypes.c_int64(0)
     check(fn(*args, ctypes.byref(out)), fn.__name__)
@@ -116,23 +185,30 @@ def _ws_bytes(fn, *args) -> int:
 class InverseHessian:
     """Damped, dead-masked inverse-Hessian factor shared by every module that
     consumes the same Hessian (q/k/v, gate/up).  ``status`` stays on the
-    device; ``ok()`` reads it (one host sync)."""
+    device; ``ok()`` reads it (one host sync).  ``perm``: the activation
+    order the factor was built in (None: column order)."""
 
     def __init__(self, hinv: torch.Tensor, dead: torch.Tensor, status: torch.Tensor,
-                 hinv_t: torch.Tensor | None = None):
-        self.hinv, self.dead, self.status, self.hinv_t = hinv, dead, status, hinv_t
+                 hinv_t: torch.Tensor | None = None, perm: torch.Tensor | None = None):
+        self.hinv, self.dead, self.status, self.hinv_t, self.perm = hinv, dead, status, hinv_t, perm
 
     def ok(self) -> bool:
         return int(self.status.item()) != _lib.ENOT_PD
 
 
-def inverse_hessian(H: torch.Tensor, percdamp: float = 0.01) -> InverseHessian:
+def inverse_hessian(H: torch.Tensor, percdamp: float = 0.01, actorder=None) -> InverseHessian:
     """Dead-column mask, damping and the upper Cholesky factor of H^-1
-    (S/modifiers/gptq/gptq_quantize.py:35-38,177-196).  ``H`` is clobbered."""
+    (S/modifiers/gptq/gptq_quantize.py:35-38,177-196).  ``H`` is clobbered.
+    With an activation ordering the factor is built for H[perm][:, perm],
+    perm = argsort(diag(H), descending) (:148-149,299-310)."""
     require_cuda(H)
     if H.dtype != torch.float32 or H.ndim != 2 or H.shape[0] != H.shape[1]:
         raise ValueError("hessian must be a float32 (d, d) tensor")
     H = H.contiguous()
+    perm = None
+    if resolve_actorder(actorder):
+        perm = actorder_perm(H)
+        H = permute_hessian(H, perm)
     d = H.shape[0]
     dev = H.device
     st = stream_ptr(dev)
@@ -143,44 +219,80 @@ def inverse_hessian(H: torch.Tensor, percdamp: float = 0.01) -> InverseHessian:
     hinv = torch.empty(d, d, dtype=torch.float32, device=dev)
     hinv_t = torch.empty(d, d, dtype=torch.float32, device=dev)
     check(lib().llmc_gptq_hinv(ptr(H), d, ptr(hinv), ptr(hinv_t), ptr(ws), ptr(status), st), "gptq_hinv")
-    return InverseHessian(hinv, dead, status, hinv_t)
+    return InverseHessian(hinv, dead, status, hinv_t, perm)
 
 
 def _strategy(args) -> str:
     return getattr(args.strategy, "value", args.strategy)
 
 
-def weight_qparams(module: torch.nn.Module, quant_args) -> tuple[torch.Tensor, torch.Tensor]:
+def _qtype(args) -> str:
+    return getattr(args.type, "value", args.type)
+
+
+def _fused_weights(module: torch.nn.Module) -> list[torch.Tensor]:
+    """The weights that share this module's NVFP4 global scale: its own and
+    those of the modules its observer is fused with (S/observers/fusion.py,
+    ``FusionHandler``)."""
+    ws = [module.weight]
+    obs = getattr(module, "weight_observer", None)
+    handler = getattr(obs, "fusion_handler", None)
+    for h in getattr(handler, "_group", None) or []:
+        mod = getattr(h, "module", None)
+        if mod is not None and mod is not module:
+            ws.append(mod.weight)
+    return ws
+
+
+def weight_qparams(module: torch.nn.Module, quant_args, weight: torch.Tensor | None = None,
+                   stats_dtype: torch.dtype = torch.bfloat16):
     """The weight observer's qparams (S/modifiers/gptq/gptq_quantize.py:168-173).
 
     Weights are always observed memorylessly (S/modifiers/quantization/calibration.py:64-78);
-    the statistics of the unmodified weight are recomputed on the GPU: min-max, or
-    the MSE grid search when the attached observer is an MSE observer.
+    the statistics of the unmodified weight (or of ``weight``, the permuted
+    float32 weight under activation ordering GROUP, with ``stats_dtype``
+    float32) are recomputed on the GPU: min-max, or the MSE grid search when
+    the attached observer is an MSE observer.  TENSOR_GROUP: the global scale
+    from the absmax over the observer's fused set (S/observers/base.py:78-96).
     An attached observer's statistics are released as ``get_qparams`` does.
+    Returns ``(scale, zero_point, global_scale or None)``.
     """
     from . import ops
 
+    w = module.weight if weight is None else weight
     obs = getattr(module, "weight_observer", None)
     if obs is not None and "mse" in type(obs).__name__.lower():
+        if stats_dtype != torch.bfloat16:
+            raise NotImplementedError("MSE observer statistics of a float32 weight (activation ordering GROUP)")
         # S/observers/mse.py: the grid search on the GPU with the observer's knobs
-        mn, mx = ops.observe_mse(module.weight, quant_args, getattr(obs, "maxshrink", None),
+        mn, mx = ops.observe_mse(w, quant_args, getattr(obs, "maxshrink", None),
                                  getattr(obs, "patience", None), getattr(obs, "grid", None),
                                  getattr(obs, "norm", None))
     else:
-        mn, mx = ops.observe_minmax(module.weight, quant_args)
-    scale, zp = ops.calculate_qparams(mn, mx, quant_args)
+        mn, mx = ops.observe_minmax(w, quant_args)
+    gs = None
+    if _strategy(quant_args) == "tensor_group":
+        gs = ops.fused_global_scale(_fused_weights(module))
+    scale, zp = ops.calculate_qparams(mn, mx, quant_args, gs, stats_dtype=stats_dtype)
     if obs is not None and hasattr(obs, "delete_statistics"):
         try:
             obs.delete_statistics()
         except Exception:  # an observer without statistics: nothing to release
             pass
-    return scale, zp
+    return scale, zp, gs
 
 
 def quantize_with_inverse(weight: torch.Tensor, quant_args, hinv: InverseHessian, scale: torch.Tensor,
-                          zero_point: torch.Tensor | None, blocksize: int = 128) -> tuple[torch.Tensor, torch.Tensor]:
+                          zero_point: torch.Tensor | None, blocksize: int = 128, actorder=None,
+                          global_scale: torch.Tensor | None = None,
+                          g_idx_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """GPTQ block loop for one bf16 weight with a prepared inverse factor.
-    Returns (fake-quantized bf16 weight, loss as a float32 device scalar)."""
+    Returns (fake-quantized bf16 weight, loss as a float32 device scalar).
+
+    ``actorder`` must match the ordering ``hinv`` was built with; with GROUP
+    ordering ``scale`` holds the groups of the permuted weight (float32) and
+    ``g_idx_out`` (int32, cols) receives each column's group.  ``global_scale``:
+    TENSOR_GROUP; ``scale`` is then float32."""
     require_cuda(weight, scale)
     if weight.dtype != torch.bfloat16:
         raise NotImplementedError(f"weights of dtype {weight.dtype}: the GPTQ kernels take bf16 weights")
@@ -188,19 +300,27 @@ def quantize_with_inverse(weight: torch.Tensor, quant_args, hinv: InverseHessian
     rows, cols = w.shape
     if hinv.hinv.shape[0] != cols:
         raise ValueError(f"Hessian size {hinv.hinv.shape[0]} != weight columns {cols}")
+    order = resolve_actorder(actorder)
+    if bool(order) != (hinv.perm is not None):
+        raise ValueError("the inverse factor was built for a different activation ordering")
+    if order == "group" and g_idx_out is None:
+        raise ValueError("activation ordering GROUP needs g_idx_out")
     dev = w.device
     qa = _lib.qargs_struct(quant_args)
     zp = None
-    if not quant_args.symmetric:
+    if not quant_args.symmetric and _qtype(quant_args) == "int":
         zp = zero_point.to(torch.int8).contiguous()
-    scale_bf16 = scale.to(torch.bfloat16).contiguous()
+    scale_f32 = scale.dtype == torch.float32
+    sc = scale.contiguous() if scale_f32 else scale.to(torch.bfloat16).contiguous()
+    gsc = global_scale.to(torch.float32).contiguous() if global_scale is not None else None
+    cx = GptqColumns(ptr(hinv.perm), _ORDER_CODE[order], int(scale_f32), ptr(gsc), ptr(g_idx_out))
     ws = torch.empty(_ws_bytes(lib().llmc_gptq_quantize_workspace_size, rows, cols), dtype=torch.uint8, device=dev)
     out = torch.empty_like(w)
     loss = torch.empty(1, dtype=torch.float32, device=dev)
-    check(lib().llmc_gptq_quantize(ptr(w), rows, cols, ptr(hinv.hinv), ptr(hinv.hinv_t), ptr(hinv.dead),
-                                   ctypes.byref(qa),
-                                   ptr(scale_bf16), ptr(zp), int(blocksize), ptr(out), ptr(loss), ptr(ws),
-                                   ptr(hinv.status), stream_ptr(dev)), "gptq_quantize")
+    check(lib().llmc_gptq_quantize_ex(ptr(w), rows, cols, ptr(hinv.hinv), ptr(hinv.hinv_t), ptr(hinv.dead),
+                                      ctypes.byref(qa), ptr(sc), ptr(zp), ctypes.byref(cx), int(blocksize),
+                                      ptr(out), ptr(loss), ptr(ws), ptr(hinv.status), stream_ptr(dev)),
+          "gptq_quantize")
     return out, loss
 
 
@@ -225,19 +345,36 @@ def quantize_weight(
     """``quantize_weight`` (S/modifiers/gptq/gptq_quantize.py:100-296).
 
     :return: (loss, q_param_dict) with ``weight`` (weight dtype),
-        ``weight_scale`` (weight dtype) and ``weight_zero_point`` (zp_dtype).
+        ``weight_scale`` (weight dtype), ``weight_zero_point`` (zp_dtype),
+        ``weight_global_scale`` (TENSOR_GROUP) and ``weight_g_idx``
+        (activation ordering GROUP).
     """
-    actorder = getattr(quant_args, "actorder", None)
-    actorder = getattr(actorder, "value", actorder)
-    if actorder:
-        raise NotImplementedError("activation ordering is not implemented on this path; pass actorder=None")
     strategy = _strategy(quant_args)
-    if strategy not in ("tensor", "channel", "group"):
+    order = resolve_actorder(getattr(quant_args, "actorder", None))
+    if order == "group" and strategy not in ("group", "tensor_group"):
+        from loguru import logger
+
+        logger.warning(
+            "ActivationOrdering.GROUP requires a grouped quantization strategy; "
+            "falling back to actorder=None for this module."
+        )
+        order = None
+    if strategy not in ("tensor", "channel", "group", "tensor_group", "block"):
         raise ValueError(f"Quantization strategy is not supported for GPTQ: {strategy}")
+    if order == "group" and (strategy == "tensor_group" or _qtype(quant_args) == "float"):
+        raise NotImplementedError("activation ordering GROUP with float types: scales from float32 statistics "
+                                  "are only built for integer types")
     final_dtype = module.weight.dtype
-    scale, zp = weight_qparams(module, quant_args)
-    hinv = inverse_hessian(hessian, percdamp)
-    wq, loss = quantize_with_inverse(module.weight, quant_args, hinv, scale, zp, blocksize)
+    hinv = inverse_hessian(hessian, percdamp, order)
+    g_idx = None
+    if order == "group":
+        # re-observe the permuted (float32) weight for the groups of the new order (:141-145)
+        wp = permute_columns(module.weight, hinv.perm)
+        scale, zp, gs = weight_qparams(module, quant_args, weight=wp, stats_dtype=torch.float32)
+        g_idx = torch.empty(module.weight.shape[1], dtype=torch.int32, device=module.weight.device)
+    else:
+        scale, zp, gs = weight_qparams(module, quant_args)
+    wq, loss = quantize_with_inverse(module.weight, quant_args, hinv, scale, zp, blocksize, order, gs, g_idx)
     if not hinv.ok():
         _warn_fallback()
     zp_dtype = getattr(quant_args, "zp_dtype", None) or torch.int8
@@ -246,4 +383,8 @@ def quantize_weight(
         "weight_scale": scale.to(dtype=final_dtype),
         "weight_zero_point": zp.to(dtype=zp_dtype),
     }
+    if gs is not None:
+        q_param_dict["weight_global_scale"] = gs.to(dtype=final_dtype)
+    if g_idx is not None:
+        q_param_dict["weight_g_idx"] = g_idx
     return float(loss.item()), q_param_dict

@@ -26,6 +26,8 @@ def quantize_with_inverse_noalloc(weight: torch.Tensor, quant_args, hinv, scale:
                                   blocksize: int = 128) -> None:
     """Fill ``out`` (bf16, weight-shaped) and ``loss`` (float32, 1 element) --
     both provided by the caller -- without allocating anything on the device."""
+    if getattr(hinv, "perm", None) is not None:
+        raise ValueError("the no-allocation entry point takes factors without activation ordering")
     rows, cols = weight.shape
     qa = _lib.qargs_struct(quant_args)
     zp = None if quant_args.symmetric else zero_point

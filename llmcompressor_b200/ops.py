@@ -179,8 +179,14 @@ def fused_global_scale(weights: list[torch.Tensor]) -> torch.Tensor:
     return global_scale_from_absmax(acc)
 
 
-def calculate_qparams(mn: torch.Tensor, mx: torch.Tensor, args, global_scale: torch.Tensor | None = None):
-    """calculate_qparams (CT/quantization/utils/helpers.py:50-137) on the GPU."""
+def calculate_qparams(mn: torch.Tensor, mx: torch.Tensor, args, global_scale: torch.Tensor | None = None,
+                      stats_dtype: torch.dtype = torch.bfloat16):
+    """calculate_qparams (CT/quantization/utils/helpers.py:50-137) on the GPU.
+
+    ``stats_dtype``: the dtype of the observed tensor the statistics came
+    from -- bf16 for weights; float32 for the permuted float32 weight that
+    activation ordering GROUP re-observes (the values are passed as bf16,
+    where they are exact; the arithmetic and the scale are float32)."""
     require_cuda(mn, mx)
     if mn.dtype != torch.bfloat16 or mx.dtype != torch.bfloat16:
         raise NotImplementedError("statistics must be bf16 (the observed weight's dtype)")
@@ -188,7 +194,8 @@ def calculate_qparams(mn: torch.Tensor, mx: torch.Tensor, args, global_scale: to
     qa = qargs_struct(args)
     if global_scale is not None:
         global_scale = global_scale.to(torch.float32).contiguous()
-    scale = torch.empty(mn.shape, dtype=torch.float32 if global_scale is not None else torch.bfloat16,
+    f32stats = stats_dtype == torch.float32
+    scale = torch.empty(mn.shape, dtype=torch.float32 if (global_scale is not None or f32stats) else torch.bfloat16,
                         device=mn.device)
     zp_dtype = args.zp_dtype if getattr(args, "zp_dtype", None) is not None else torch.int8
     if zp_dtype == torch.float8_e4m3fn:
@@ -197,8 +204,9 @@ def calculate_qparams(mn: torch.Tensor, mx: torch.Tensor, args, global_scale: to
     else:
         zp = torch.empty(mn.shape, dtype=zp_dtype, device=mn.device)
         zp_out = zp
-    check(lib().llmc_calculate_qparams(ptr(mn), ptr(mx), mn.numel(), ctypes.byref(qa), ptr(global_scale),
-                                       ptr(scale), ptr(zp_out), stream_ptr(mn.device)), "calculate_qparams")
+    check(lib().llmc_calculate_qparams_ex(ptr(mn), ptr(mx), mn.numel(), ctypes.byref(qa), ptr(global_scale),
+                                          int(f32stats), ptr(scale), ptr(zp_out), stream_ptr(mn.device)),
+          "calculate_qparams")
     if scale.ndim == 0:
         scale, zp = scale.reshape(1), zp.reshape(1)
     return scale, zp

@@ -125,6 +125,12 @@ def solve_layer(
     before this function returns, so results are ordered on it as usual."""
     rank, ws = world()
     dims = hessians.dims
+    # activation ordering WEIGHT / STATIC permutes each Hessian's columns;
+    # GROUP would also regroup the packed codes (g_idx), which this layer
+    # API does not write
+    act = gptq.resolve_actorder(getattr(quant_args, "actorder", None))
+    if act == "group":
+        raise NotImplementedError("activation ordering GROUP in the layer solve; use gptq.quantize_weight")
     rows_of: dict[str, int] = {}
     for s in specs:
         rows_of[s.input_key] = rows_of.get(s.input_key, 0) + s.out_features
@@ -144,13 +150,14 @@ def solve_layer(
         st.wait_stream(main)
         with torch.cuda.stream(st):
             if owners[key] == rank:
-                inv[key] = gptq.inverse_hessian(hessians.H[key], percdamp)
+                inv[key] = gptq.inverse_hessian(hessians.H[key], percdamp, act)
             else:
                 inv[key] = gptq.InverseHessian(
                     torch.empty(d, d, dtype=torch.float32, device=dev),
                     torch.empty(d, dtype=torch.uint8, device=dev),
                     torch.empty(1, dtype=torch.int32, device=dev),
                     torch.empty(d, d, dtype=torch.float32, device=dev),
+                    torch.empty(d, dtype=torch.int32, device=dev) if act else None,
                 )
             ev = torch.cuda.Event()
             ev.record(st)
@@ -158,7 +165,8 @@ def solve_layer(
     if ws > 1:
         for ev in ready.values():
             main.wait_event(ev)
-        broadcast_inverse({k: [v.hinv, v.dead, v.status, v.hinv_t] for k, v in inv.items()}, owners)
+        broadcast_inverse({k: [v.hinv, v.dead, v.status, v.hinv_t] + ([v.perm] if act else [])
+                           for k, v in inv.items()}, owners)
         bcast = torch.cuda.Event()
         bcast.record(main)
         ready = {k: bcast for k in ready}
@@ -179,7 +187,7 @@ def solve_layer(
                 wl = weights[s.name][r0:r1]
                 mn, mx = ops.observe_minmax(wl, quant_args)
                 scale, zp = ops.calculate_qparams(mn, mx, quant_args)
-                wq, loss = gptq.quantize_with_inverse(wl, quant_args, inv[s.input_key], scale, zp, blocksize)
+                wq, loss = gptq.quantize_with_inverse(wl, quant_args, inv[s.input_key], scale, zp, blocksize, act)
                 if pack_events is not None:
                     e0 = torch.cuda.Event(enable_timing=True)
                     e0.record(st)
@@ -204,7 +212,7 @@ def solve_layer(
     for ev in done:
         main.wait_event(ev)
     for v in inv.values():
-        for t in (v.hinv, v.dead, v.status, v.hinv_t):
+        for t in (v.hinv, v.dead, v.status, v.hinv_t, v.perm):
             if t is not None:
                 t.record_stream(main)
 

@@ -296,7 +296,7 @@ def gen_hessian():
     print("hessian", H.shape, float(n))
 
 
-def gptq_case(name, rows, cols, args, dead_cols=(), seed=11, tokens=512):
+def gptq_case(name, rows, cols, args, dead_cols=(), seed=11, tokens=512, blocksize=128, late_actorder=None):
     g = torch.Generator().manual_seed(seed)
     w = make_weight(rows, cols, seed=seed + 1)
     lin = torch.nn.Linear(cols, rows, bias=False, dtype=torch.bfloat16)
@@ -317,16 +317,27 @@ def gptq_case(name, rows, cols, args, dead_cols=(), seed=11, tokens=512):
     initialize_module_for_quantization(lin, scheme, force_zero_point=False)
     initialize_observer(lin, "weight")
     observe(lin, base_name="weight")
-    loss, qd = quantize_weight(lin, args, Hn.clone(), blocksize=128, percdamp=0.01)
+    if late_actorder is not None:
+        # the installed compressed-tensors only accepts an ordering with group
+        # strategies when args and schemes are validated, while quantize_weight
+        # handles it for every strategy: set it on the args it reads
+        args = args.model_copy()
+        args.actorder = late_actorder
+    loss, qd = quantize_weight(lin, args, Hn.clone(), blocksize=blocksize, percdamp=0.01)
     arrays = {
         "weight": to_np(w),
         "x": np.stack(xs),
         "hessian": to_np(Hn),
         "loss": np.array(loss, dtype=np.float64),
+        "blocksize": np.array(blocksize),
         "out_weight": to_np(qd["weight"]),
         "out_scale": to_np(qd["weight_scale"]),
         "out_zero_point": to_np(qd["weight_zero_point"]),
     }
+    if "weight_g_idx" in qd:
+        arrays["out_g_idx"] = qd["weight_g_idx"].numpy().astype(np.int32)
+    if "weight_global_scale" in qd:
+        arrays["out_global_scale"] = to_np(qd["weight_global_scale"])
     np.savez_compressed(os.path.join(HERE, f"gptq_{name}.npz"), **arrays)
     print("gptq", name, loss)
 
@@ -355,8 +366,57 @@ def gen_gptq():
     )
 
 
+def gen_gptq_orderings():
+    """Activation ordering, block strategy, float formats and a block size
+    other than 128 (T/llmcompressor/modifiers/gptq/test_gptq_quantize.py
+    covers the same options on toy shapes)."""
+    from compressed_tensors.quantization import ActivationOrdering
+
+    def nvfp4_args():
+        return preset_name_to_scheme("NVFP4A16", ["Linear"]).weights
+
+    def mxfp4_args():
+        return preset_name_to_scheme("MXFP4A16", ["Linear"]).weights
+
+    cases = [
+        ("int4_group128_actweight", 128, 384,
+         QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=128,
+                          actorder=ActivationOrdering.WEIGHT), {}),
+        ("int4_group32_actgroup", 96, 256,
+         QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=32,
+                          actorder=ActivationOrdering.GROUP), {"seed": 41}),
+        ("int4_channel_actstatic", 64, 256,
+         QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="channel"),
+         {"seed": 51, "dead_cols": (7, 200), "actorder": ActivationOrdering.STATIC}),
+        ("int8_block32x64_bs64", 96, 320,
+         QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="block", block_structure=[32, 64],
+                          actorder=None), {"seed": 61, "blocksize": 64}),
+        ("int8_block48x96_actweight", 100, 320,
+         QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="block", block_structure=[48, 96]),
+         {"seed": 71, "actorder": ActivationOrdering.WEIGHT}),
+        ("fp8_channel", 64, 256,
+         QuantizationArgs(num_bits=8, type="float", symmetric=True, strategy="channel", actorder=None),
+         {"seed": 81}),
+        ("nvfp4_actweight", 64, 256, None, {"seed": 91, "args_fn": nvfp4_args, "actorder": ActivationOrdering.WEIGHT}),
+        ("mxfp4", 64, 256, None, {"seed": 101, "args_fn": mxfp4_args}),
+    ]
+    only = set(sys.argv[2:])
+    for name, rows, cols, args, kw in cases:
+        if only and name not in only:
+            continue
+        kw = dict(kw)
+        fn = kw.pop("args_fn", None)
+        order = kw.pop("actorder", None)
+        if fn is not None:
+            args = fn()
+        gptq_case(name, rows, cols, args, late_actorder=order, **kw)
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
+    if sys.argv[1:2] == ["gptq_orderings"]:
+        gen_gptq_orderings()
+        sys.exit(0)
     if sys.argv[1:] == ["mse"]:
         gen_mse_observers()
         sys.exit(0)
@@ -370,3 +430,4 @@ if __name__ == "__main__":
     gen_nvfp4_fused()
     gen_hessian()
     gen_gptq()
+    gen_gptq_orderings()

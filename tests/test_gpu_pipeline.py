@@ -110,3 +110,25 @@ def test_solve_layer_vs_oracle():
         assert agree >= CODE_AGREE, (s.name, agree)
         lg, lo = float(res[s.name].loss.reshape(())), float(loss_o)
         assert abs(lg - lo) <= REL * abs(lo), (s.name, lg, lo)
+
+
+def test_solve_layer_weight_ordering_matches_module_api():
+    """Activation ordering WEIGHT (the reference's default STATIC) through the
+    layer solve: bit-identical to the drop-in quantize_weight per module,
+    whose parity with the reference is pinned by its own fixtures."""
+    from compressed_tensors.quantization import ActivationOrdering
+
+    qa = QA.model_copy()
+    qa.actorder = ActivationOrdering.WEIGHT
+    specs, dims, w, x, hess, _ = _layer(7, hidden=256, intermediate=512, heads=4, kv_heads=2, head_dim=64)
+    H = {k: h.clone() for k, h in hess.H.items()}
+    res = solve_layer(w, specs, hess, qa)
+    torch.cuda.synchronize()
+    for s in specs:
+        lin = torch.nn.Linear(s.in_features, s.out_features, bias=False, dtype=torch.bfloat16, device="cuda")
+        lin.weight.data.copy_(w[s.name])
+        loss, qd = gptq.quantize_weight(lin, qa, H[s.input_key].clone())
+        packed = ops.quantize_pack(qd["weight"], qa, qd["weight_scale"], None, fmt=_lib.FMT_PACK_INT32)
+        np.testing.assert_array_equal(bits(res[s.name].weight_packed), bits(packed), err_msg=s.name)
+        np.testing.assert_array_equal(bits(res[s.name].weight_scale), bits(qd["weight_scale"]), err_msg=s.name)
+        assert float(res[s.name].loss.reshape(())) == loss, s.name

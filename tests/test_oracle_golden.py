@@ -68,24 +68,42 @@ def test_hessian_matches_reference():
     assert rel <= 1e-5, rel
 
 
+# case -> (args, actorder); block size from the fixture
 GPTQ_CASES = {
-    "int4_group128": QArgs(4, "int", True, "group", 128),
-    "int4_channel_dead": QArgs(4, "int", True, "channel", None),
-    "int8_group64_asym": QArgs(8, "int", False, "group", 64),
+    "int4_group128": (QArgs(4, "int", True, "group", 128), None),
+    "int4_channel_dead": (QArgs(4, "int", True, "channel", None), None),
+    "int8_group64_asym": (QArgs(8, "int", False, "group", 64), None),
+    "int4_group128_actweight": (QArgs(4, "int", True, "group", 128), "weight"),
+    "int4_group32_actgroup": (QArgs(4, "int", True, "group", 32), "group"),
+    "int4_channel_actstatic": (QArgs(4, "int", True, "channel", None), "static"),
+    "int8_block32x64_bs64": (QArgs(8, "int", True, "block", None, (32, 64)), None),
+    "int8_block48x96_actweight": (QArgs(8, "int", True, "block", None, (48, 96)), "weight"),
+    "fp8_channel": (QArgs(8, "float", True, "channel", None, zp_dtype="fp8"), None),
+    "nvfp4_actweight": (QArgs(4, "float", True, "tensor_group", 16, scale_dtype="fp8", zp_dtype="fp8"), "weight"),
+    "mxfp4": (QArgs(4, "float", True, "group", 32, scale_dtype="uint8", zp_dtype="uint8"), None),
 }
 
 
 @pytest.mark.parametrize("case", sorted(GPTQ_CASES))
 def test_gptq_oracle_matches_reference(case):
     g = load(f"gptq_{case}")
-    args = GPTQ_CASES[case]
+    args, order = GPTQ_CASES[case]
     w = bf16(g["weight"])
-    loss, wq, scale, zp, ok = gptq.quantize_weight(w, g["hessian"], args)
+    bs = int(g["blocksize"]) if "blocksize" in g else 128
+    res = gptq.quantize_weight(w, g["hessian"], args, blocksize=bs, actorder=order)
+    loss, wq, scale, zp, ok = res[:5]
+    extra = res[5] if len(res) > 5 else {}
     assert ok
     np.testing.assert_array_equal(numerics.f32_to_bf16_bits(scale), g["out_scale"].reshape(scale.shape))
+    g_idx = extra.get("g_idx")
+    if "out_g_idx" in g:
+        np.testing.assert_array_equal(g_idx, g["out_g_idx"])
+    gs = extra.get("global_scale")
+    if "out_global_scale" in g:
+        np.testing.assert_array_equal(numerics.f32_to_bf16_bits(np.float32(gs)).reshape(-1), g["out_global_scale"].reshape(-1))
     ref_wq = bf16(g["out_weight"])
-    codes = gptq.codes_from_weight(wq, scale, zp, args)
-    ref_codes = gptq.codes_from_weight(ref_wq, scale, zp, args)
+    codes = gptq.codes_from_weight(wq, scale, zp, args, g_idx, gs)
+    ref_codes = gptq.codes_from_weight(ref_wq, scale, zp, args, g_idx, gs)
     agree = float(np.mean(codes == ref_codes))
     assert agree >= 0.99, agree
     assert abs(loss - float(g["loss"])) <= 0.01 * abs(float(g["loss"]))
