@@ -26,6 +26,7 @@
 #include "tc32.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace llmc {
 namespace gq {
@@ -50,6 +51,7 @@ struct GemmArgs {
   int mode;  // 0: C = AB, 1: C = C - AB, 2: C = -AB
   int tri, b_lower;
   const int* skip;
+  int max_ctas;  // tensor-core path: at most this many CTAs (0: one per SM)
 };
 
 constexpr int GBM = 128, GBN = 128, GBK = 8;
@@ -184,11 +186,11 @@ static int launch_gemm(bool ta, bool tb, const GemmArgs& g, cudaStream_t st) {
   // Wide updates go to the tensor cores (3xTF32, float32 accuracy); small or
   // TMA-unaligned ones stay on the CUDA cores.
   if (g_use_tc32 && !g.b_lower && (int64_t)g.m * g.n * g.k >= (int64_t)128 * 128 * 128) {
-    tc32::Gemm t;
+    tc32::Gemm t = {};
     t.m = g.m; t.n = g.n; t.k = g.k;
     t.A = g.A; t.lda = g.lda; t.a_mn = ta;
     t.B = g.B; t.ldb = g.ldb; t.b_mn = !tb;
-    t.C = g.C; t.ldc = g.ldc; t.mode = g.mode; t.tri = g.tri; t.skip = g.skip;
+    t.C = g.C; t.ldc = g.ldc; t.mode = g.mode; t.tri = g.tri; t.skip = g.skip; t.max_ctas = g.max_ctas;
     const int s = tc32::gemm(t, st);
     if (s != LLMC_ENOSUPPORT) return s;
   }
@@ -891,11 +893,11 @@ using namespace llmc::gq;
 
 extern "C" {
 
-// workspace: Cholesky working copy B (d*d) + inverse X (d*d) + diag inverses (d*128) + panel (d*128)
+// workspace: Cholesky working copy B (d*d) + inverse X (d*d) + diag inverses (d*128) + two panels (2 * d*128)
 int llmc_gptq_hinv_workspace_size(int64_t d, int64_t* bytes) {
   if (!bytes || d <= 0) return LLMC_EINVAL_ARG;
   const int64_t nbp = ((d + PB - 1) / PB) * PB;
-  *bytes = (int64_t)sizeof(float) * (2 * d * d + 2 * nbp * PB) + 256;
+  *bytes = (int64_t)sizeof(float) * (2 * d * d + 3 * nbp * PB) + 256;
   return LLMC_OK;
 }
 
@@ -905,6 +907,85 @@ int llmc_gptq_prepare_hessian(float* H, int64_t d, float percdamp, uint8_t* dead
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 
+}  // extern "C"
+
+namespace llmc {
+namespace gq {
+
+// A side stream of the current device for the lookahead of the
+// factorisation (a few per device, handed out in turn so that concurrent
+// factorisations on different streams rarely share one).  NULL if none can
+// be made: the caller then runs everything on its own stream.
+static cudaStream_t side_stream() {
+  static std::mutex mu;
+  static cudaStream_t pool[64][4] = {};
+  static unsigned next[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  const unsigned i = next[dev]++ & 3u;
+  if (!pool[dev][i] && cudaStreamCreateWithFlags(&pool[dev][i], cudaStreamNonBlocking) != cudaSuccess) {
+    pool[dev][i] = nullptr;
+    return nullptr;
+  }
+  return pool[dev][i];
+}
+
+// CTAs of a side-stream GEMM: the persistent GEMM keeps one CTA per SM, so
+// a full grid would leave no SM for the diagonal kernel and the skinny
+// panel GEMMs of the caller's stream until it ends.
+constexpr int kSideCtas = 148 - 12;
+
+// Fork/join helper: work put on `side` is ordered after everything already
+// on `main`; `join` makes `main` wait for all of it.
+struct Lookahead {
+  cudaStream_t main = nullptr, side = nullptr;
+  cudaEvent_t ev_main = nullptr, ev_side = nullptr;
+  bool ok() const { return side != nullptr; }
+  int open(cudaStream_t st) {
+    main = st;
+    side = side_stream();
+    if (!side) return LLMC_OK;
+    if (cudaEventCreateWithFlags(&ev_main, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_side, cudaEventDisableTiming) != cudaSuccess)
+      return LLMC_ECUDA;
+    if (cudaEventRecord(ev_main, main) != cudaSuccess || cudaStreamWaitEvent(side, ev_main, 0) != cudaSuccess)
+      return LLMC_ECUDA;
+    return LLMC_OK;
+  }
+  // main waits for the side work enqueued so far
+  int main_waits_side() {
+    if (!side) return LLMC_OK;
+    return cudaStreamWaitEvent(main, ev_side, 0) == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+  }
+  // side waits for the main work enqueued so far
+  int side_waits_main() {
+    if (!side) return LLMC_OK;
+    if (cudaEventRecord(ev_main, main) != cudaSuccess) return LLMC_ECUDA;
+    return cudaStreamWaitEvent(side, ev_main, 0) == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+  }
+  int side_done() {
+    if (!side) return LLMC_OK;
+    return cudaEventRecord(ev_side, side) == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+  }
+  cudaStream_t side_or_main() const { return side ? side : main; }
+  int close() {
+    int r = LLMC_OK;
+    if (side) {
+      if (side_done() || main_waits_side()) r = LLMC_ECUDA;
+    }
+    if (ev_main) cudaEventDestroy(ev_main);
+    if (ev_side) cudaEventDestroy(ev_side);
+    ev_main = ev_side = nullptr;
+    return r;
+  }
+};
+
+}  // namespace gq
+}  // namespace llmc
+
+extern "C" {
+
 int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* workspace, int* status,
                    void* stream) {
   if (!A || !Hinv || !workspace || !status || d <= 0) return LLMC_EINVAL_ARG;
@@ -913,47 +994,80 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* w
   float* B = (float*)workspace;
   float* X = B + d * d;
   float* LinvD = X + d * d;             // nb blocks of PB x PB
-  float* T = LinvD + nb * PB * PB;      // panel scratch, up to d x PB
+  float* T0 = LinvD + nb * PB * PB;     // panel scratch, up to d x PB, double-buffered
+  float* T1 = T0 + nb * PB * PB;
   static uint64_t attr_mask = 0;
   if (!set_smem_attr(k_potrf_diag, 2 * PB * (PB + 1) * (int)sizeof(float), &attr_mask)) return LLMC_ECUDA;
   dim3 rg((unsigned)((d + 255) / 256), (unsigned)d);
   k_reverse<<<rg, 256, 0, st>>>(A, B, d); llmc::note_launch();
-  // blocked lower Cholesky of B = J A J
-  for (int64_t kb0 = 0; kb0 < d; kb0 += PB) {
+  // Blocked lower Cholesky of B = J A J with a lookahead of one panel: after
+  // panel k is solved, the caller's stream updates only the next block
+  // column (a) and goes on to factor it, while the rest of the trailing
+  // update (b) runs on a side stream.  (a) of panel k + 1 waits for (b) of
+  // panel k (both write the block column after it); the panel buffers
+  // alternate so that (b) still reads its own panel.
+  Lookahead la;
+  if (la.open(st)) return LLMC_ECUDA;
+  int k = 0;
+  for (int64_t kb0 = 0; kb0 < d; kb0 += PB, ++k) {
     const int kb = (int)std::min<int64_t>(PB, d - kb0);
     float* Ld = LinvD + (kb0 / PB) * PB * PB;
+    float* T = (k & 1) ? T1 : T0;
     k_potrf_diag<<<1, 512, 2 * PB * (PB + 1) * sizeof(float), st>>>(B, d, kb0, kb, Ld, status); llmc::note_launch();
     const int rem = (int)(d - kb0 - kb);
     if (rem > 0) {
-      // T = B[kb0+kb:, kb0:kb0+kb] * Linv_kk^T
+      // T = B[kb0+kb:, kb0:kb0+kb] * Linv_kk^T, then the panel back into B
       GemmArgs g1 = {rem, kb, kb, B + (kb0 + kb) * d + kb0, d, Ld, PB, T, PB, 0, 0, 0, nullptr};
       if (launch_gemm(false, true, g1, st)) return LLMC_ECUDA;
-      // B22 -= T T^T (lower tiles)
-      GemmArgs g2 = {rem, rem, kb, T, PB, T, PB, B + (kb0 + kb) * d + kb0 + kb, d, 1, 1, 0, nullptr};
-      if (launch_gemm(false, true, g2, st)) return LLMC_ECUDA;
-      // panel back into B
       k_copy2d<<<dim3(1, rem), 128, 0, st>>>(T, PB, B + (kb0 + kb) * d + kb0, d, rem, kb); llmc::note_launch();
+      // (a) the next block column: B[kb0+kb:, kb0+kb : +kn] -= T T[:kn]^T
+      const int kn = std::min(PB, rem);
+      if (la.main_waits_side()) return LLMC_ECUDA;
+      GemmArgs ga = {rem, kn, kb, T, PB, T, PB, B + (kb0 + kb) * d + kb0 + kb, d, 1, 0, 0, nullptr};
+      if (launch_gemm(false, true, ga, st)) return LLMC_ECUDA;
+      // (b) the rest of the lower trailing block, on the side stream
+      if (rem > kn) {
+        if (la.side_waits_main()) return LLMC_ECUDA;
+        const int64_t o = kb0 + kb + kn;
+        GemmArgs gb = {rem - kn, rem - kn, kb, T + (int64_t)kn * PB, PB, T + (int64_t)kn * PB, PB, B + o * d + o, d,
+                       1, 1, 0, nullptr, kSideCtas};
+        if (launch_gemm(false, true, gb, la.side_or_main())) return LLMC_ECUDA;
+        if (la.side_done()) return LLMC_ECUDA;
+      }
     }
   }
   // Xt = L^-T (upper), by right-looking blocked substitution on column blocks of Xt = I:
   //   Xt[:, i] = Xt[:, i] * Linv_ii^T,   Xt[:, >i] -= Xt[:, i] * L[>i, i]^T
   // -- every update is an A * B^T product with K = 128 (both operands K-major).
+  // The same lookahead: the next column block is updated on the caller's
+  // stream, the remaining columns on the side stream.
   float* Xt = X;
+  if (la.main_waits_side()) return LLMC_ECUDA;
   if (cudaMemsetAsync(Xt, 0, sizeof(float) * d * d, st) != cudaSuccess) return LLMC_ECUDA;
   k_eye<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(Xt, d); llmc::note_launch();
   for (int64_t i0 = 0; i0 < d; i0 += PB) {
     const int ib = (int)std::min<int64_t>(PB, d - i0);
     const int nc = (int)(i0 + ib);  // rows of Xt that can be non-zero in these columns
     const float* Ld = LinvD + (i0 / PB) * PB * PB;
-    k_copy2d<<<dim3(1, nc), 128, 0, st>>>(Xt + i0, d, T, PB, nc, ib); llmc::note_launch();
-    GemmArgs g1 = {nc, ib, ib, T, PB, Ld, PB, Xt + i0, d, 0, 0, 0, nullptr};
+    k_copy2d<<<dim3(1, nc), 128, 0, st>>>(Xt + i0, d, T0, PB, nc, ib); llmc::note_launch();
+    GemmArgs g1 = {nc, ib, ib, T0, PB, Ld, PB, Xt + i0, d, 0, 0, 0, nullptr};
     if (launch_gemm(false, true, g1, st)) return LLMC_ECUDA;
     const int rem = (int)(d - i0 - ib);
     if (rem > 0) {
-      GemmArgs g2 = {nc, rem, ib, Xt + i0, d, B + (i0 + ib) * d + i0, d, Xt + i0 + ib, d, 1, 0, 0, nullptr};
-      if (launch_gemm(false, true, g2, st)) return LLMC_ECUDA;
+      const int kn = std::min(PB, rem);
+      if (la.main_waits_side()) return LLMC_ECUDA;
+      GemmArgs ga = {nc, kn, ib, Xt + i0, d, B + (i0 + ib) * d + i0, d, Xt + i0 + ib, d, 1, 0, 0, nullptr};
+      if (launch_gemm(false, true, ga, st)) return LLMC_ECUDA;
+      if (rem > kn) {
+        if (la.side_waits_main()) return LLMC_ECUDA;
+        const int64_t o = i0 + ib + kn;
+        GemmArgs gb = {nc, rem - kn, ib, Xt + i0, d, B + o * d + i0, d, Xt + o, d, 1, 0, 0, nullptr, kSideCtas};
+        if (launch_gemm(false, true, gb, la.side_or_main())) return LLMC_ECUDA;
+        if (la.side_done()) return LLMC_ECUDA;
+      }
     }
   }
+  if (la.close()) return LLMC_ECUDA;
   k_xt_to_u<<<dim3((unsigned)((d + 31) / 32), (unsigned)((d + 31) / 32)), dim3(32, 8), 0, st>>>(Xt, Hinv, d);
   llmc::note_launch();
   if (HinvT) { k_xt_to_ut<<<rg, 256, 0, st>>>(Xt, HinvT, d); llmc::note_launch(); }

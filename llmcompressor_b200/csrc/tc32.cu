@@ -346,7 +346,7 @@ int gemm(const Gemm& g, cudaStream_t st) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  const int grid = std::min(p.num_tiles, sms);
+  const int grid = std::min(p.num_tiles, g.max_ctas > 0 ? std::min(g.max_ctas, sms) : sms);
   k_gemm_tc32<<<grid, THREADS, SMEM_TOTAL, st>>>(am, bm, cm, p, g.skip); llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
@@ -360,7 +360,7 @@ extern "C" int llmc_gemm_f32_nt(int64_t m, int64_t n, int64_t k, const float* A,
   if (mode < 0 || mode > 2) return LLMC_EINVAL_ARG;
   if (m == 0 || n == 0) return LLMC_OK;
   if (!A || !B || !C) return LLMC_EINVAL_ARG;
-  llmc::tc32::Gemm g;
+  llmc::tc32::Gemm g = {};
   g.m = (int)m; g.n = (int)n; g.k = (int)k;
   g.A = A; g.lda = lda; g.a_mn = false;
   g.B = B; g.ldb = ldb; g.b_mn = false;

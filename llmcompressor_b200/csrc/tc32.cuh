@@ -20,6 +20,7 @@ struct Gemm {
   int mode;  // 0: C = AB, 1: C = C - AB, 2: C = -AB
   int tri;   // only output tiles touching the lower triangle (row >= col)
   const int* skip;  // optional device flag: do nothing when set
+  int max_ctas;     // > 0: at most this many CTAs (leaves SMs to concurrent work); else one per SM
 };
 
 // Launches the tensor-core GEMM; returns LLMC_ENOSUPPORT (launching nothing)
