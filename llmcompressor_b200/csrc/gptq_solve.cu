@@ -271,52 +271,72 @@ __global__ void k_xt_to_ut(const float* __restrict__ Xt, float* __restrict__ Ut,
 constexpr int PB = 128;
 constexpr int PLD = PB + 1;  // padded row stride of the shared-memory blocks
 // 16 warps: warp w walks rows (w, w+16, ...), its lanes walk the columns of a row.
-// Cholesky factor and inverse of the 32x32 diagonal sub-block at (o, o) of S
-// (row stride PLD) by all 512 threads of the CTA, written back as L into S
-// and as L^-1 into X.
-//   factor:  right-looking, one column per step; thread t owns the two
-//            elements (t / 16, 2 (t % 16) + {0, 1}) of the block;
-//   inverse: warp w solves columns w and w + 16 of L^-1 by forward
-//            substitution, lane = row, the solved value broadcast by shuffle.
-__device__ __forceinline__ void cta_chol_inv32(float* S, float* X, int o, int sz, int* bad) {
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int r = t >> 4, c0 = (t & 15) * 2;
-  for (int j = 0; j < sz; ++j) {
-    __syncthreads();
-    float p = S[(o + j) * PLD + o + j];
-    if (!(p > 0.0f)) { if (t == 0) *bad = 1; p = 1.0f; }
+// Step J of the warp's 32x32 Cholesky (lane = row): pivot, column J solved,
+// rank-1 update of the columns after J.  A template chain, so that every
+// register index is a compile-time constant.
+template <int J>
+__device__ __forceinline__ void chol_col(float (&a)[32], int lane, bool& failed) {
+  if constexpr (J < 32) {
+    float p = __shfl_sync(0xffffffffu, a[J], J);
+    if (!(p > 0.0f)) { failed = true; p = 1.0f; }
     const float piv = sqrtf(p);
-    if (r > j && r < sz && (c0 == j || c0 + 1 == j)) S[(o + r) * PLD + o + j] = __fdiv_rn(S[(o + r) * PLD + o + j], piv);
-    __syncthreads();
-    if (t == 0) S[(o + j) * PLD + o + j] = piv;
-    if (r < sz) {
-      const float lrj = S[(o + r) * PLD + o + j];
+    const float l = lane > J ? __fdiv_rn(a[J], piv) : (lane == J ? piv : a[J]);
+    a[J] = l;
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int c = c0 + u;
-        if (c > j && c <= r) S[(o + r) * PLD + o + c] -= lrj * S[(o + c) * PLD + o + j];
-      }
+    for (int c = J + 1; c < 32; ++c) {
+      const float lcj = __shfl_sync(0xffffffffu, l, c);
+      if (lane >= c) a[c] -= l * lcj;
     }
+    chol_col<J + 1>(a, lane, failed);
   }
-  __syncthreads();
-  // column c of X = L^-1: t_r = rhs of row r; x_l = t_l / L_ll, then t_r -= L_rl x_l
+}
+
+// Cholesky factor and inverse of the 32x32 diagonal sub-block at (o, o) of S
+// (row stride PLD) by one warp, written back as L into S and as L^-1 into X.
+//   factor:  lane i holds row i in registers (every index known at compile
+//            time); right-looking, one column per step, the pivot and the
+//            solved column broadcast by shuffles -- no barriers;
+//   inverse: lane c solves column c of L^-1 by forward substitution, reading
+//            the rows of L from shared memory (every lane the same address).
+// Both follow the element-wise order of the textbook loops (each element's
+// updates in increasing column order), and rows / columns >= sz are padded
+// with the identity.
+__device__ __forceinline__ void warp_chol_inv32(float* S, float* X, int o, int sz, int* bad) {
+  const int lane = threadIdx.x & 31;
+  float a[32];
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int c = warp + 16 * h;
-    if (c >= sz) continue;
-    float tr = (lane == c) ? 1.0f : 0.0f;
-    for (int l = c; l < sz; ++l) {
-      const float xl = __shfl_sync(0xffffffffu, __fdiv_rn(tr, S[(o + l) * PLD + o + l]), l);
-      if (lane == l) X[(o + l) * PLD + o + c] = xl;
-      if (lane > l && lane < sz) tr -= S[(o + lane) * PLD + o + l] * xl;
-    }
+  for (int c = 0; c < 32; ++c)
+    a[c] = (lane < sz && c < sz) ? (c <= lane ? S[(o + lane) * PLD + o + c] : 0.0f) : (lane == c ? 1.0f : 0.0f);
+  bool failed = false;
+  chol_col<0>(a, lane, failed);
+  if (failed && lane == 0) *bad = 1;
+  if (lane < sz) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c)
+      if (c <= lane) S[(o + lane) * PLD + o + c] = a[c];
+  }
+  __syncwarp();
+  // padded rows of L are the identity: read them as such
+  float x[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float acc = (i == lane) ? 1.0f : 0.0f;
+    const float* Li = S + (o + i) * PLD + o;
+#pragma unroll
+    for (int k = 0; k < i; ++k) acc -= (i < sz ? Li[k] : 0.0f) * x[k];
+    x[i] = __fdiv_rn(acc, i < sz ? Li[i] : 1.0f);
+  }
+  if (lane < sz) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i >= lane && i < sz) X[(o + i) * PLD + o + lane] = x[i];
   }
 }
 
 __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_t k0, int n, float* Linv,
                                                     int* status) {
-  // Blocked in 32-column sub-steps: the CTA factors and inverts each 32x32
-  // diagonal sub-block (cta_chol_inv32), then all 16 warps apply the panel
+  // Blocked in 32-column sub-steps: one warp factors and inverts each 32x32
+  // diagonal sub-block (warp_chol_inv32), then all 16 warps apply the panel
   // solve and the trailing update; the off-diagonal blocks of the inverse
   // follow block-row by block-row.
   extern __shared__ float sm[];
@@ -349,7 +369,7 @@ __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_
   const int nsub = (n + SB - 1) / SB;
   for (int kb = 0; kb < nsub; ++kb) {
     const int o = kb * SB, sz = min(SB, n - o);
-    cta_chol_inv32(S, X, o, sz, &bad);
+    if (warp == 0) warp_chol_inv32(S, X, o, sz, &bad);
     __syncthreads();
     const int r0 = o + sz, rem = n - r0;
     if (rem <= 0) break;
@@ -923,12 +943,15 @@ static cudaStream_t side_stream() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
-  const unsigned i = next[dev]++ & 3u;
-  if (!pool[dev][i] && cudaStreamCreateWithFlags(&pool[dev][i], cudaStreamNonBlocking) != cudaSuccess) {
-    pool[dev][i] = nullptr;
-    return nullptr;
+  if (!pool[dev][0]) {  // all at once: creating a stream inside a timed region would cost there
+    for (int k = 0; k < 4; ++k)
+      if (cudaStreamCreateWithFlags(&pool[dev][k], cudaStreamNonBlocking) != cudaSuccess) {
+        for (int m = 0; m < k; ++m) cudaStreamDestroy(pool[dev][m]);
+        for (int m = 0; m < 4; ++m) pool[dev][m] = nullptr;
+        return nullptr;
+      }
   }
-  return pool[dev][i];
+  return pool[dev][next[dev]++ & 3u];
 }
 
 // CTAs of a side-stream GEMM: the persistent GEMM keeps one CTA per SM, so
