@@ -523,7 +523,8 @@ def run_micro(args) -> None:
     """One kernel on a small case (profiling captures and per-kernel timing):
     hessian: H += alpha X^T X, X (tokens x d); gptq: factor + block loop of
     one (rows x d) weight; cast: model-free pass of --scheme over a (rows x d) weight;
-    castbatch: --tensors such weights through the batched launch."""
+    castbatch: --tensors such weights through the batched launch; actobs: one
+    activation-observer update (NVFP4 input statistics) over (tokens x d) bf16."""
     from llmcompressor_b200 import gptq, ops
 
     dev = torch.device("cuda:0")
@@ -551,6 +552,17 @@ def run_micro(args) -> None:
             return gptq.quantize_with_inverse(w, qa, inv, scale, zp)
 
         work, unit = None, "ms"
+    elif args.micro == "actobs":
+        from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
+
+        from llmcompressor_b200 import act_observers
+
+        # NVFP4 input activations: per-16 statistics over all tokens, moving average
+        aargs = preset_name_to_scheme("NVFP4", ["Linear"]).input_activations
+        obs = act_observers.MinMaxObserver("input", aargs)
+        x = torch.randn(n, d, device=dev, generator=g).to(torch.bfloat16)
+        fn = lambda: obs(x)  # noqa: E731
+        work, unit = x.numel() * 2 / 1e9, "GB/s"
     elif args.micro == "castbatch":
         from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
 
@@ -605,7 +617,7 @@ def algorithmic_per_launch() -> float:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--micro", choices=["hessian", "gptq", "hinv", "cast", "castbatch"], default=None,
+    ap.add_argument("--micro", choices=["hessian", "gptq", "hinv", "cast", "castbatch", "actobs"], default=None,
                     help="time one kernel on a small case instead of the model benchmark")
     ap.add_argument("--d", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=16384)

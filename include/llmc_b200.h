@@ -99,6 +99,32 @@ int llmc_observe_mse(const void* w_bf16, int64_t rows, int64_t cols, const LlmcQ
                      int patience, float grid, float norm, void* min_bf16, void* max_bf16, void* workspace,
                      void* stream);
 
+/* Activation observers of static activation schemes: one calibration batch
+ * folded into the running min/max statistics.  Replaces
+ * `Observer.forward` -> `update_statistics_from_observed` of
+ * MemorylessMinMaxObserver (mode 0), StaticMinMaxObserver (mode 1) and
+ * MinMaxObserver (mode 2, moving average `lerp(prev, new, c)`)
+ * (S/observers/min_max.py:16-110, S/observers/helpers.py:219-221) on the
+ * activation layouts of flatten_for_calibration
+ * (S/observers/helpers.py:104-153):
+ *   x        n_tok x hidden activations (batch and sequence flattened), bf16
+ *            (dtype 0) or float32 (dtype 1), contiguous, 16-byte aligned,
+ *            hidden % 8 == 0;
+ *   group    0: TENSOR (one statistic; also the q/k/v TENSOR layout);
+ *            > 0: GROUP / TENSOR_GROUP, hidden / group statistics, each over
+ *            `group` consecutive features of every token (group a multiple
+ *            of 8 and a power-of-two multiple up to 256);
+ *   min_io, max_io  the statistics in the activation dtype, updated in place;
+ *            has_prev = 0 when the observer holds none yet (they are then
+ *            written, whatever the mode);
+ *   avg_w0, avg_w1  mode 2: float(1 - c) and float(c) (c: averaging_constant).
+ * NaN inputs are skipped by the reduction (torch.amin would propagate them).
+ * workspace: llmc_observe_activation_workspace_size bytes of device memory. */
+int llmc_observe_activation_workspace_size(int64_t hidden, int64_t group, int64_t* bytes);
+int llmc_observe_activation(const void* x, int64_t n_tok, int64_t hidden, int dtype, int64_t group, int mode,
+                            float avg_w0, float avg_w1, int has_prev, void* min_io, void* max_io, void* workspace,
+                            void* stream);
+
 /* Absolute maximum of `n` bf16 values, max-accumulated into *absmax_f32
  * (initialise it to 0).  Used for fused-set NVFP4 global scales:
  * `Observer.get_global_scale`, S/observers/base.py:78-96. */

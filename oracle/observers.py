@@ -288,3 +288,35 @@ def mse_minmax(w: np.ndarray, args: QArgs, maxshrink: float = 0.2, patience: int
             if no_improve >= patience:
                 break
     return bmn.astype(F32), bmx.astype(F32)
+
+
+# ---------------------------------------------------------------- activation observers
+def activation_minmax(x: np.ndarray, args: QArgs) -> tuple[np.ndarray, np.ndarray]:
+    """``_get_min_max`` (S/observers/min_max.py:106-110) over the activation
+    layouts of ``flatten_for_calibration`` (S/observers/helpers.py:104-153):
+    TENSOR -> one value; GROUP / TENSOR_GROUP -> one value per feature group
+    over all tokens.  ``x``: (..., features) values as float32."""
+    x = np.asarray(x, F32)
+    if args.strategy == "tensor":
+        return np.array([x.min()], F32), np.array([x.max()], F32)
+    gs = args.group_size
+    v = x.reshape(-1, x.shape[-1] // gs, gs)
+    return v.min(axis=(0, 2)).astype(F32), v.max(axis=(0, 2)).astype(F32)
+
+
+def update_activation_minmax(prev_min, prev_max, new_min, new_max, observer: str,
+                             averaging_constant: float = 0.01, dtype: str = "bf16"):
+    """One observer update of (min_vals, max_vals); ``prev_*`` None before the
+    first batch."""
+    R = rb if dtype == "bf16" else (lambda v: np.asarray(v, F32))
+    if prev_min is None or observer == "memoryless_minmax" or (
+            observer == "minmax" and float(averaging_constant) == 1.0):
+        return R(new_min), R(new_max)
+    if observer == "static_minmax":
+        return np.minimum(prev_min, new_min).astype(F32), np.maximum(prev_max, new_max).astype(F32)
+    w0, w1 = F32(1.0 - averaging_constant), F32(averaging_constant)
+
+    def lerp(a, b):
+        return R(R(np.asarray(a, F32) * w0) + R(np.asarray(b, F32) * w1))
+
+    return lerp(prev_min, new_min), lerp(prev_max, new_max)

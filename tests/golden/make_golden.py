@@ -13,6 +13,9 @@ seeded synthetic inputs and stores inputs and outputs as ``.npz`` files:
 * ``mse_<case>.npz`` -- the ``memoryless_mse`` grid-search observer
   (``S/observers/mse.py``, ``S/observers/mse_quant.py``) and its qparams.
 * ``repack_int4_int8.npz`` -- the checkpoint repacker's ``_pack_int4_to_int8``.
+* ``actobs_<case>.npz`` -- the activation observers of static activation
+  schemes (``S/observers/min_max.py:16-110``): statistics after each of four
+  batches, then ``get_qparams``.
 * ``hessian.npz`` -- ``accumulate_hessian`` over several calls
   (``S/modifiers/gptq/gptq_quantize.py:63-97``).
 * ``gptq_<case>.npz`` -- ``quantize_weight``
@@ -412,8 +415,53 @@ def gen_gptq_orderings():
         gptq_case(name, rows, cols, args, late_actorder=order, **kw)
 
 
+def gen_act_observers():
+    """Activation observers of static activation schemes
+    (S/observers/min_max.py:16-110) over several calibration batches: the
+    statistics after every batch, then ``get_qparams``."""
+    nvfp4_in = preset_name_to_scheme("NVFP4", ["Linear"]).input_activations
+    cases = [
+        ("minmax_int8_tensor", "minmax", "input", (2, 48, 256),
+         QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="tensor", dynamic=False, observer="minmax")),
+        ("static_int8_asym_tensor", "static_minmax", "input", (2, 48, 256),
+         QuantizationArgs(num_bits=8, type="int", symmetric=False, strategy="tensor", dynamic=False,
+                          observer="static_minmax")),
+        ("minmax_nvfp4_tensor_group", "minmax", "input", (2, 48, 256), nvfp4_in),
+        ("memoryless_int8_group128", "memoryless_minmax", "input", (3, 40, 512),
+         QuantizationArgs(num_bits=8, type="int", symmetric=False, strategy="group", group_size=128, dynamic=False,
+                          observer="memoryless_minmax")),
+        ("static_fp8_kv_tensor", "static_minmax", "k", (2, 4, 24, 64),
+         QuantizationArgs(num_bits=8, type="float", symmetric=True, strategy="tensor", dynamic=False,
+                          observer="static_minmax")),
+        ("minmax_c05_fp8_tensor", "minmax", "output", (2, 32, 256),
+         QuantizationArgs(num_bits=8, type="float", symmetric=True, strategy="tensor", dynamic=False,
+                          observer="minmax", observer_kwargs={"averaging_constant": 0.5})),
+    ]
+    for name, obs_name, base, shape, args in cases:
+        g = torch.Generator().manual_seed(sum(map(ord, name)))
+        obs = Observer.load_from_registry(obs_name, base_name=base, args=args)
+        arrays = {}
+        for b, mul in enumerate([1.0, 3.0, 0.5, 2.0]):
+            feat = torch.exp(0.7 * torch.randn(shape[-1], generator=g))
+            x = (mul * torch.randn(*shape, generator=g) * feat + 0.3 * mul).to(torch.bfloat16)
+            obs(x)
+            arrays[f"x{b}"] = to_np(x)
+            arrays[f"min{b}"] = to_np(obs.min_vals.to(torch.bfloat16))
+            arrays[f"max{b}"] = to_np(obs.max_vals.to(torch.bfloat16))
+        q = obs.get_qparams()
+        arrays["scale"] = to_np(q["scale"])
+        arrays["zero_point"] = to_np(q["zero_point"])
+        if q.get("global_scale") is not None:
+            arrays["global_scale"] = to_np(q["global_scale"])
+        np.savez_compressed(os.path.join(HERE, f"actobs_{name}.npz"), **arrays)
+        print("actobs", name, arrays["min3"][:4], arrays["max3"][:4], arrays["scale"].reshape(-1)[:2])
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
+    if sys.argv[1:2] == ["act_observers"]:
+        gen_act_observers()
+        sys.exit(0)
     if sys.argv[1:2] == ["gptq_orderings"]:
         gen_gptq_orderings()
         sys.exit(0)
@@ -431,3 +479,4 @@ if __name__ == "__main__":
     gen_hessian()
     gen_gptq()
     gen_gptq_orderings()
+    gen_act_observers()

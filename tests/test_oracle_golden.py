@@ -246,3 +246,65 @@ def test_repack_int4_int8_bit_exact():
     g = load("repack_int4_int8")
     np.testing.assert_array_equal(casts.pack_int4_to_int8(g["codes"]), g["codes_packed"])
     np.testing.assert_array_equal(casts.pack_int4_to_int8(g["wild"]), g["wild_packed"])
+
+
+# --- activation observers of static activation schemes ------------------------
+# case -> (observer, QArgs, averaging constant)
+ACT_OBS_CASES = {
+    "minmax_int8_tensor": ("minmax", QArgs(8, "int", True, "tensor", None), 0.01),
+    "static_int8_asym_tensor": ("static_minmax", QArgs(8, "int", False, "tensor", None), 0.01),
+    "minmax_nvfp4_tensor_group": ("minmax", QArgs(4, "float", True, "tensor_group", 16, scale_dtype="fp8",
+                                                  zp_dtype="fp8"), 0.01),
+    "memoryless_int8_group128": ("memoryless_minmax", QArgs(8, "int", False, "group", 128), 0.01),
+    "static_fp8_kv_tensor": ("static_minmax", QArgs(8, "float", True, "tensor", None, zp_dtype="fp8"), 0.01),
+    "minmax_c05_fp8_tensor": ("minmax", QArgs(8, "float", True, "tensor", None, zp_dtype="fp8"), 0.5),
+}
+
+
+@pytest.mark.parametrize("case", sorted(ACT_OBS_CASES))
+def test_activation_observers_oracle_matches_reference(case):
+    from oracle.observers import (activation_minmax, calculate_qparams, fused_absmax, generate_gparam,
+                                  update_activation_minmax)
+
+    g = load(f"actobs_{case}")
+    obs, args, c = ACT_OBS_CASES[case]
+    mn = mx = None
+    for b in range(4):
+        nmn, nmx = activation_minmax(bf16(g[f"x{b}"]), args)
+        mn, mx = update_activation_minmax(mn, mx, nmn, nmx, obs, c)
+        np.testing.assert_array_equal(numerics.f32_to_bf16_bits(mn), g[f"min{b}"], err_msg=f"min after batch {b}")
+        np.testing.assert_array_equal(numerics.f32_to_bf16_bits(mx), g[f"max{b}"], err_msg=f"max after batch {b}")
+    gs = generate_gparam(fused_absmax([(mn, mx)])) if args.strategy == "tensor_group" else None
+    scale, zp = calculate_qparams(mn, mx, args, global_scale=gs)
+    if gs is not None:
+        np.testing.assert_array_equal(np.float32(gs).reshape(-1), g["global_scale"].reshape(-1))
+        np.testing.assert_array_equal(scale.astype(np.float32).reshape(-1), g["scale"].reshape(-1))
+    else:
+        np.testing.assert_array_equal(numerics.f32_to_bf16_bits(scale).reshape(-1), g["scale"].reshape(-1))
+    if args.type == "int":
+        np.testing.assert_array_equal(np.asarray(zp).astype(np.int64).reshape(-1),
+                                      g["zero_point"].astype(np.int64).reshape(-1))
+    else:
+        assert not np.any(g["zero_point"])
+
+
+def test_activation_minmax_observer_known_answers():
+    """T/llmcompressor/observers/test_min_max.py:48-86 (minmax on a tensor
+    input, moving average with the default constant 0.01), float32 stats."""
+    from oracle.observers import activation_minmax, update_activation_minmax
+
+    args = QArgs(8, "int", True, "tensor", None)
+    base = [1, 1, 1, 1, 1]
+    seq = [base, base, [127, 1, 1, 1, 1], base, [-128, 1, 1, 1, 1]]
+    mn = mx = None
+    cur_min, cur_max = 1.0, 1.0
+    for i, row in enumerate(seq):
+        nmn, nmx = activation_minmax(np.array([row], np.float32), args)
+        mn, mx = update_activation_minmax(mn, mx, nmn, nmx, "minmax", 0.01, dtype="f32")
+        cur_max, cur_min = max(float(mx[0]), cur_max), min(float(mn[0]), cur_min)
+        if i < 2:
+            assert cur_max == 1 and cur_min == 1
+        elif i < 4:
+            assert abs(cur_max - 2.26) < 1e-6 and cur_min == 1
+        else:
+            assert abs(cur_max - 2.26) < 1e-6 and abs(cur_min - (-0.29)) < 1e-6
