@@ -948,7 +948,7 @@ __device__ __forceinline__ void tile_process(const CastParams& p, int64_t gi, co
 // THR threads per CTA; 128-thread CTAs holding a whole 128x128 block (NP = 8)
 // put four blocks in flight per SM without prefetch registers.
 template <int FMT, int BITS, int MODE, int NP, bool PF, int THR = 256>
-__global__ void __launch_bounds__(THR, PF ? 2 : (THR == 128 ? (NP <= 4 ? 6 : 4) : 1)) k_tile(CastParams p, int64_t ng) {
+__global__ void __launch_bounds__(THR, PF ? 2 : (THR == 128 ? (NP <= 4 ? 6 : 4) : 2)) k_tile(CastParams p, int64_t ng) {
   __shared__ float sh[32];
   int64_t gi = blockIdx.x;
   if (!PF) {
@@ -1299,7 +1299,7 @@ static bool launch_tile(const CastParams& p, int64_t pieces, cudaStream_t st) {
       k_tile<FMT, BITS, MODE, 4, false, 128><<<(unsigned)std::min<int64_t>(ng, 148 * 16), 128, 0, st>>>(p, ng);
     else if (pieces <= 1024)
       k_tile<FMT, BITS, MODE, 8, false, 128><<<(unsigned)std::min<int64_t>(ng, 148 * 16), 128, 0, st>>>(p, ng);
-    else if (pieces <= 2048) k_tile<FMT, BITS, MODE, 8, false><<<(unsigned)std::min<int64_t>(ng, 148 * 8), 256, 0, st>>>(p, ng);
+    else if (pieces <= 2048) k_tile<FMT, BITS, MODE, 8, false><<<(unsigned)std::min<int64_t>(ng, 148 * 16), 256, 0, st>>>(p, ng);
     else return false;
   }
   llmc::note_launch();
