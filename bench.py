@@ -287,7 +287,7 @@ def measure_casts(layers, reps: int = 3) -> dict:
     return res
 
 
-def modelfree_layers(device, reps: int = 3) -> dict:
+def modelfree_layers(device, reps: int = 10) -> dict:
     """Device-resident model-free passes at BASELINE configs[3] / configs[4]
     shapes, one layer (or expert sample) each, timed with CUDA events:
 
