@@ -320,7 +320,7 @@ int llmc_gemm_f32_nt(int64_t m, int64_t n, int64_t k, const float* A, int64_t ld
  * the process exits.  No counterpart in the reference.
  *  - Size limit: returns LLMC_EINVAL_SHAPE, launching nothing, when
  *    llmc_gptq_quantize_workspace_size(rows, cols) exceeds the array
- *    (rows*cols*4 + rows*516 + 272 bytes > 32 MiB; e.g. 1024 x 4096 fits,
+ *    (rows*cols*4 + rows*2052 + 272 bytes > 32 MiB; e.g. 1024 x 4096 fits,
  *    4096 x 4096 does not).
  *  - The first call on a device looks up the array's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call

@@ -501,6 +501,12 @@ __global__ void k_copy2d(const float* __restrict__ src, int64_t lds, float* __re
 // GPTQ column loop over one 128-column block
 // ---------------------------------------------------------------------------
 constexpr int QB = 128;     // GPTQ block size handled by the kernel
+// Columns whose errors are applied together beyond them: after each QB-column
+// block only the rest of its QOB-column outer block is updated; the columns
+// after the outer block get one update with K = QOB (the same lazy-batch
+// argument that lets GPTQ defer updates across blocks: exact in exact terms),
+// which reads and writes the rest of W a quarter as often.
+constexpr int QOB = 4 * QB;
 constexpr int SUB = 32;     // sub-block held in registers
 constexpr int CH = 8;       // columns per unrolled chunk of the sub-block
 constexpr int ROWS = 64;    // rows (threads) per CTA
@@ -519,7 +525,8 @@ struct BlockArgs {
   int strategy;
   int64_t gs;
   float qmin, qmax;
-  float* err;          // rows x QB row-major errors of this block
+  float* err;          // row-major errors (row stride eld); this block's start at column ecol
+  int64_t eld, ecol;
   float* loss;         // r per-row losses
   const int* status;   // ENOT_PD -> identity
   // per-column variant (k_gptq_block<true>) only:
@@ -763,7 +770,7 @@ __global__ void __launch_bounds__(ROWS, 2) k_gptq_block(BlockArgs a) {
         for (int k = 0; k < CH; ++k) { w[SUB - CH + k] = 0.f; e[SUB - CH + k] = ebuf[k]; }
       }
       // this sub-block's errors, row-major (rows x 128), as the K-major operand of the trailing update
-      float4* erow = (float4*)(a.err + row * QB + s0);
+      float4* erow = (float4*)(a.err + row * a.eld + a.ecol + s0);
 #pragma unroll
       for (int j = 0; j < SUB / 4; ++j) erow[j] = make_float4(e[4 * j], e[4 * j + 1], e[4 * j + 2], e[4 * j + 3]);
       // lazy update of the later columns of this block, four columns at a time
@@ -1099,7 +1106,7 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* w
 
 int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes) {
   if (!bytes || rows < 0 || cols < 0) return LLMC_EINVAL_ARG;
-  *bytes = (int64_t)sizeof(float) * (rows * cols + (int64_t)QB * rows + rows + 4) + 256;
+  *bytes = (int64_t)sizeof(float) * (rows * cols + (int64_t)QOB * rows + rows + 4) + 256;
   return LLMC_OK;
 }
 
@@ -1137,7 +1144,7 @@ int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const 
                       q.strategy == LLMC_STRAT_TENSOR_GROUP || q.strategy == LLMC_STRAT_BLOCK;
   float* W = (float*)workspace;
   float* E = W + ((rows * cols + 3) & ~(int64_t)3);  // 16-byte aligned rows for the vector stores
-  float* L = E + (int64_t)QB * rows;
+  float* L = E + (int64_t)QOB * rows;
   k_init_w<<<grid_for(rows * cols), 256, 0, st>>>((const uint16_t*)w_bf16, W, rows, cols, dead, x.perm);
   llmc::note_launch();
   if (cudaMemsetAsync(L, 0, sizeof(float) * rows, st) != cudaSuccess) return LLMC_ECUDA;
@@ -1168,28 +1175,39 @@ int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const 
   // updates are applied in more steps, which is the same arithmetic in
   // exact terms (GPTQ's result does not depend on the block size)
   const int64_t step = std::min<int64_t>(blocksize, QB);
+  // outer blocks of QOB columns for 128-column blocks; other block sizes
+  // update everything after each block, as the reference does
+  const int64_t ostep = step == QB ? QOB : step;
   const unsigned nblk = (unsigned)((rows + ROWS - 1) / ROWS);
-  for (int64_t i1 = 0; i1 < cols; i1 += step) {
-    const int cnt = (int)std::min<int64_t>(step, cols - i1);
-    ba.i1 = (int)i1; ba.count = cnt;
-    if (percol) k_gptq_block<true><<<nblk, ROWS, smem, st>>>(ba);
-    else k_gptq_block<false><<<nblk, ROWS, smem, st>>>(ba);
-    llmc::note_launch();
-    const int64_t i2 = i1 + cnt;
-    if (i2 < cols) {
-      // W[:, i2:] -= Err1 * Hinv[i1:i2, i2:]   (Err1 row-major: rows x QB).  With the
-      // transposed factor the product is A * B^T on the tensor cores.  The identity
-      // fallback has no off-diagonal Hinv, so the reference's update is a no-op there.
-      if (HinvT) {
-        GemmArgs g = {(int)rows, (int)(cols - i2), cnt, E, QB, HinvT + i2 * cols + i1, cols, W + i2, cols, 1, 0, 0,
-                      status};
-        if (launch_gemm(false, true, g, st)) return LLMC_ECUDA;
-      } else {
-        GemmArgs g = {(int)rows, (int)(cols - i2), cnt, E, QB, Hinv + i1 * cols + i2, cols, W + i2, cols, 1, 0, 0,
-                      status};
-        if (launch_gemm(false, false, g, st)) return LLMC_ECUDA;
-      }
+  ba.eld = QOB;
+  // W[:, n0:n1] -= E[:, e0:e0+k] * Hinv[h0:h0+k, n0:n1].  With the transposed
+  // factor the product is A * B^T on the tensor cores.  The identity fallback
+  // has no off-diagonal Hinv (`status` makes the GEMM a no-op), so the
+  // reference's update is a no-op there.
+  auto update = [&](int64_t n0, int64_t n1, int64_t e0, int64_t h0, int k) -> bool {
+    if (HinvT) {
+      GemmArgs g = {(int)rows, (int)(n1 - n0), k, E + e0, QOB, HinvT + n0 * cols + h0, cols, W + n0, cols, 1, 0, 0,
+                    status};
+      return launch_gemm(false, true, g, st) == LLMC_OK;
     }
+    GemmArgs g = {(int)rows, (int)(n1 - n0), k, E + e0, QOB, Hinv + h0 * cols + n0, cols, W + n0, cols, 1, 0, 0,
+                  status};
+    return launch_gemm(false, false, g, st) == LLMC_OK;
+  };
+  for (int64_t o1 = 0; o1 < cols; o1 += ostep) {
+    const int64_t o2 = std::min<int64_t>(o1 + ostep, cols);
+    for (int64_t i1 = o1; i1 < o2; i1 += step) {
+      const int cnt = (int)std::min<int64_t>(step, o2 - i1);
+      ba.i1 = (int)i1; ba.count = cnt; ba.ecol = i1 - o1;
+      if (percol) k_gptq_block<true><<<nblk, ROWS, smem, st>>>(ba);
+      else k_gptq_block<false><<<nblk, ROWS, smem, st>>>(ba);
+      llmc::note_launch();
+      const int64_t i2 = i1 + cnt;
+      // the rest of this outer block, from this block's errors
+      if (i2 < o2 && !update(i2, o2, i1 - o1, i1, cnt)) return LLMC_ECUDA;
+    }
+    // everything after the outer block, from all of its errors at once
+    if (o2 < cols && !update(o2, cols, 0, o1, (int)(o2 - o1))) return LLMC_ECUDA;
   }
   if (x.perm) k_finish_perm<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows, cols, x.perm);
   else k_finish<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows * cols);
