@@ -79,6 +79,29 @@ __device__ __forceinline__ uint32_t quant_code(float x, const ElemQ& e) {
   return (uint32_t)(int32_t)rintf(q);  // INT8 / PACK_INT32: signed code
 }
 
+// x / y correctly rounded from r = RN(1/y) (Markstein's correction: one fma
+// residual, one fma step) while the quotient stays in the normal range;
+// IEEE division otherwise (zeros, subnormals, huge values).
+__device__ __forceinline__ float div_by_recip(float x, float y, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float aq = fabsf(q0);
+  if (aq > 1.0e-30f && aq < 1.0e30f && fabsf(r) > 1.0e-30f && fabsf(r) < 1.0e30f) {
+    const float e = __fmaf_rn(-q0, y, x);
+    return __fmaf_rn(e, r, q0);
+  }
+  return __fdiv_rn(x, y);
+}
+
+// NVFP4 group scale (group_qparams for symmetric E2M1 with a float32 global
+// scale and FP8 scales): rbf(amax / 6) * gs rounded to E4M3 (0 -> 0.125),
+// with the division by 6 as a multiplication by RN(1/6) plus correction.
+__device__ __forceinline__ float nvfp4_group_scale(float mn, float mx, float gs) {
+  const float mvp = fmaxf(fabsf(fminf(mn, 0.0f)), fabsf(fmaxf(mx, 0.0f)));
+  float scale = rbf(div_by_recip(mvp, 6.0f, __uint_as_float(0x3E2AAAABu)));  // RN(1/6)
+  scale = round_e4m3(fminf(fmaxf(gs * scale, -448.0f), 448.0f));
+  return scale == 0.0f ? 0.125f : scale;
+}
+
 // Per-group qparams -> ElemQ (+ the stored scale bits) in FUSED mode.
 template <int FMT>
 __device__ __forceinline__ ElemQ make_elemq_fused(const CastParams& p, float mn, float mx, float* s_store,
@@ -86,7 +109,22 @@ __device__ __forceinline__ ElemQ make_elemq_fused(const CastParams& p, float mn,
   ElemQ e;
   bool has_gs = (FMT == LLMC_FMT_NVFP4);
   float gs = has_gs ? *p.gs : 0.0f;
-  float zp;
+  float zp = 0.0f;
+  if constexpr (FMT == LLMC_FMT_NVFP4) {
+    if (p.a.symmetric && p.a.is_float && p.a.bits == 4 && p.a.scale_dtype == LLMC_SCALE_FP8) {
+      const float s = nvfp4_group_scale(mn, mx, gs);
+      *s_store = s;
+      *zp_store = 0.0f;
+      e.s = div_by_recip(s, gs, __frcp_rn(gs));  // the effective scale s / gs
+      e.r = scale_recip(e.s, &e.fast);
+      e.zp = 0.0f;
+      e.has_zp = false;
+      e.f32q = false;
+      e.qmin = p.a.qmin();
+      e.qmax = p.a.qmax();
+      return e;
+    }
+  }
   float s = group_qparams(mn, mx, p.a, has_gs, gs, &zp);
   *s_store = s;
   *zp_store = zp;
