@@ -523,7 +523,8 @@ def run_micro(args) -> None:
     """One kernel on a small case (profiling captures and per-kernel timing):
     hessian: H += alpha X^T X, X (tokens x d); gptq: factor + block loop of
     one (rows x d) weight; cast: model-free pass of --scheme over a (rows x d) weight;
-    castbatch: --tensors such weights through the batched launch; actobs: one
+    castbatch: --tensors such weights through the batched launch; hessianhook:
+    --tokens in 2048-token calls through gptq.BatchedHessian; actobs: one
     activation-observer update (NVFP4 input statistics) over (tokens x d) bf16."""
     from llmcompressor_b200 import gptq, ops
 
@@ -552,6 +553,19 @@ def run_micro(args) -> None:
             return gptq.quantize_with_inverse(w, qa, inv, scale, zp)
 
         work, unit = None, "ms"
+    elif args.micro == "hessianhook":
+        # --tokens of calibration in calls of 2048 tokens (one sample each), as the
+        # reference's forward hook delivers them, through gptq.BatchedHessian
+        calls = max(1, n // 2048)
+        xs = [torch.randn(1, 2048, d, device=dev, generator=g).to(torch.bfloat16) for _ in range(calls)]
+
+        def fn():
+            bh = gptq.BatchedHessian(d, dev)
+            for x in xs:
+                bh.add(x)
+            return bh.finalize()
+
+        work, unit = calls * 2048 * d * (d + 1) / 1e12, "TFLOP/s"
     elif args.micro == "actobs":
         from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
 
@@ -617,7 +631,7 @@ def algorithmic_per_launch() -> float:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--micro", choices=["hessian", "gptq", "hinv", "cast", "castbatch", "actobs"], default=None,
+    ap.add_argument("--micro", choices=["hessian", "hessianhook", "gptq", "hinv", "cast", "castbatch", "actobs"], default=None,
                     help="time one kernel on a small case instead of the model benchmark")
     ap.add_argument("--d", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=16384)
