@@ -83,3 +83,36 @@ def test_batched_hessian_default_chunk_accuracy():
     c = float((h * exact).sum() / (h * h).sum())  # best uniform scale
     rel_scaled = float(torch.linalg.norm(c * h - exact) / torch.linalg.norm(exact))
     assert rel_scaled <= 1e-5, (rel, rel_scaled)
+
+
+def test_gptq_from_16384_token_launches_meets_gptq_bar():
+    """The layer API's launch size at a realistic token count: GPTQ from H
+    accumulated in 16384-token launches against GPTQ from the exact sum
+    (float64, rounded to float32) -- codes >= 99% identical, loss within 1%."""
+    from compressed_tensors.quantization import QuantizationArgs
+
+    from llmcompressor_b200 import ops
+
+    d, rows, tokens = 2048, 512, 65536
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    x = (torch.randn(tokens, d, device="cuda", generator=gen)
+         * torch.exp(0.5 * torch.randn(d, device="cuda", generator=gen))).to(torch.bfloat16)
+    w = (0.02 * torch.randn(rows, d, device="cuda", generator=gen)).to(torch.bfloat16)
+    bh = gptq.BatchedHessian(d, "cuda")
+    bh.add(x.unsqueeze(0))
+    Hb, _ = bh.finalize()
+    xd = x.double()
+    He = (2.0 * xd.T @ xd).float()
+    qa = QuantizationArgs(num_bits=4, type="int", symmetric=True, strategy="group", group_size=128, actorder=None)
+    mn, mx = ops.observe_minmax(w, qa)
+    scale, zp = ops.calculate_qparams(mn, mx, qa)
+    out = {}
+    for name, H in (("batched", Hb), ("exact", He)):
+        inv = gptq.inverse_hessian(H.clone() / tokens, 0.01)
+        wq, loss = gptq.quantize_with_inverse(w, qa, inv, scale, zp)
+        codes = torch.round(wq.float() / scale.float().repeat_interleave(128, dim=1))
+        out[name] = (codes, float(loss))
+    agree = float((out["batched"][0] == out["exact"][0]).float().mean())
+    assert agree >= 0.99, agree
+    lb, le = out["batched"][1], out["exact"][1]
+    assert abs(lb - le) <= 0.01 * abs(le), (lb, le)
