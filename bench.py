@@ -192,8 +192,12 @@ def run_ours(args, rank, world, device):
     for i in range(args.warmup):
         step(i, False)
     barrier()
-    clocks = ClockSampler(os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out"))
-                                       else "_work", f"clocks_rank{rank}.csv")) if rank == 0 else None
+    clock_dir = os.path.join(ROOT, "gpurun_out")
+    if not os.path.isdir(clock_dir):
+        import tempfile
+
+        clock_dir = tempfile.gettempdir()
+    clocks = ClockSampler(os.path.join(clock_dir, f"clocks_rank{rank}.csv")) if rank == 0 else None
     if clocks:
         clocks.start()
     launches0 = _lib.kernel_launches()

@@ -23,8 +23,8 @@ seeded synthetic inputs and stores inputs and outputs as ``.npz`` files:
   seeded activations.
 
 bf16 tensors are stored as ``uint16`` bit patterns, fp8 as ``uint8``.
-Only run in a container that holds the reference checkout:
-``python tests/golden/make_golden.py``.
+Only run where a reference checkout exists:
+``LLMC_REFERENCE_SRC=<checkout>/src python tests/golden/make_golden.py``.
 """
 from __future__ import annotations
 

@@ -18,7 +18,8 @@ import os
 import sys
 import types
 
-REFERENCE_SRC = os.environ.get("LLMC_REFERENCE_SRC", "/root/reference/src")
+# the reference checkout's `src` directory (the fixture generator's input)
+REFERENCE_SRC = os.environ.get("LLMC_REFERENCE_SRC", "")
 
 
 def _stub(name: str, **attrs):
@@ -84,5 +85,7 @@ def install() -> None:
     if "accelerate" not in sys.modules:
         _stub("accelerate")
         _stub("accelerate.accelerator", get_state_dict_offloaded_model=lambda m: m.state_dict())
+    if not REFERENCE_SRC or not os.path.isdir(REFERENCE_SRC):
+        raise RuntimeError("set LLMC_REFERENCE_SRC to the `src` directory of a reference llm-compressor checkout")
     if REFERENCE_SRC not in sys.path:
         sys.path.insert(0, REFERENCE_SRC)
