@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_
   float* X = sm + PB * PLD;  // [PB][PLD]  its inverse (lower)
   __shared__ int bad;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  constexpr int NW = 16, NT = 512, SB = 32;
+  constexpr int NW = 16, SB = 32;
   if (t == 0) bad = 0;
   // stage the lower triangle: all of a thread's loads are issued before its stores
   {
