@@ -109,3 +109,32 @@ def test_failed_rank_surfaces_as_error_not_hang():
     out = spawn(_rank_fails)
     assert "stopped between steps" in out[1]
     assert out[0] != "no error"
+
+
+def _observer_sync(rank, world):
+    """sync_activation_stats of the static observer (S/observers/base.py:146-165):
+    MIN / MAX reductions of the rank-local statistics; the memoryless observer
+    has nothing to sync."""
+    from compressed_tensors.quantization import QuantizationArgs
+
+    from llmcompressor_b200 import act_observers as ao
+
+    args = QuantizationArgs(num_bits=8, type="int", symmetric=True, strategy="group", group_size=16, dynamic=False)
+    obs = ao.StaticMinMaxObserver("input", args)
+    obs.min_vals = torch.tensor([-1.0 - rank, -2.0 + rank, -0.5], dtype=torch.bfloat16)
+    obs.max_vals = torch.tensor([1.0 + rank, 2.0 - rank, 0.25 * (rank + 1)], dtype=torch.bfloat16)
+    for w in obs.sync_activation_stats():
+        w.wait()
+    mem = ao.MemorylessMinMaxObserver("input", args)
+    mem.min_vals = torch.zeros(3, dtype=torch.bfloat16)
+    mem.max_vals = torch.zeros(3, dtype=torch.bfloat16)
+    assert mem.sync_activation_stats() == []
+    return obs.min_vals.float().tolist(), obs.max_vals.float().tolist()
+
+
+def test_activation_observer_stats_sync_over_ranks():
+    got = spawn(_observer_sync)
+    for r in range(2):
+        mn, mx = got[r]
+        assert mn == [-2.0, -2.0, -0.5], got
+        assert mx == [2.0, 2.0, 0.5], got
