@@ -72,6 +72,11 @@ int llmc_version(void);
 int64_t llmc_kernel_launches(void);
 /* Static description of a status code. */
 const char* llmc_status_string(int status);
+/* The CUDA call that last made an entry point of this library return
+ * LLMC_ECUDA on the calling host thread, with CUDA's error string ("" if
+ * none).  No counterpart in the reference (its errors are Python
+ * exceptions carrying torch's message). */
+const char* llmc_last_cuda_error(void);
 
 /* ---------------------------------------------------------------- observers
  * Memoryless min-max statistics of a bf16 weight (rows x cols):
@@ -212,14 +217,41 @@ int llmc_pack_zero_point(const int8_t* zp, int64_t rows, int64_t groups, int num
  * `accumulate_hessian` / `_hessian_update` (S/modifiers/gptq/gptq_quantize.py:22-32,
  * 63-97; alpha = 2 reproduces the sqrt(2) input scaling).  Tensor cores
  * (tcgen05, TMEM accumulators, TMA) when d and ld are multiples of 8; a
- * CUDA-core kernel otherwise.  If num_samples is non-NULL, *num_samples +=
- * num_add on the device in the same stream (the reference's batch count,
- * `:70-73,91`).  status (optional device int) receives LLMC_ETIMEOUT if a
- * bounded wait in the kernel ran out. */
+ * CUDA-core kernel otherwise.  The tensor-core accumulators are drained into
+ * float32 running sums every LLMC_HESSIAN_FOLD_TOKENS tokens, so the error
+ * against the exact sum does not grow with the tokens of one call.  If
+ * num_samples is non-NULL, *num_samples += num_add on the device in the same
+ * stream (the reference's batch count, `:70-73,91`).  status (optional device
+ * int) receives LLMC_ETIMEOUT if a bounded wait in the kernel ran out (the
+ * kernel then stops early and H holds a partial sum). */
 int llmc_hessian_accumulate(const void* x_bf16, int64_t n_tokens, int64_t d, int64_t ld, float* H, float alpha,
                             float* num_samples, float num_add, int* status, void* stream);
 
-/* Number of 128x256 output tiles the tensor-core Hessian computes for size d
+#define LLMC_HESSIAN_FOLD_TOKENS 1024
+
+/* Options of llmc_hessian_accumulate_grouped (zero fields take the defaults). */
+typedef struct LlmcHessianOpts {
+  int64_t fold_tokens;  /* tokens per tensor-core partial sum (a multiple of 64); 0: LLMC_HESSIAN_FOLD_TOKENS */
+  int64_t wait_ns;      /* limit of every bounded device-side wait; 0: 4 s                                   */
+  int32_t test_stall;   /* 1: the MMA issuer waits on a barrier nothing arrives on, so the launch ends with
+                           LLMC_ETIMEOUT after wait_ns (tests of the timeout path; H is left unchanged)     */
+  int32_t reserved;
+} LlmcHessianOpts;
+
+/* Block-diagonal Hessians of `ngroups` column groups of X in one launch:
+ * group g accumulates H_g += alpha * X_g^T X_g with X_g = columns
+ * [g*d, (g+1)*d) of X (n_tokens, ngroups*d; row stride ld) into rows
+ * [g*d, (g+1)*d) of H (ngroups*d, d).  Replaces the per-expert calls of
+ * `accumulate_hessian` for the down projections of an MoE layer whose experts
+ * all see every token (S/modeling/moe/linear_experts.py:244-277 ->
+ * S/modifiers/gptq/base.py:255-289).  ngroups = 1 is llmc_hessian_accumulate
+ * with options.  Tensor cores when d % 32 == 0 (any d % 8 == 0 for one
+ * group). */
+int llmc_hessian_accumulate_grouped(const void* x_bf16, int64_t n_tokens, int64_t ngroups, int64_t d, int64_t ld,
+                                    float* H, float alpha, float* num_samples, float num_add, int* status,
+                                    const LlmcHessianOpts* opts, void* stream);
+
+/* Number of 256x256 output tiles the tensor-core Hessian computes for size d
  * (tiles touching the lower triangle). */
 int llmc_hessian_tiles(int64_t d);
 
@@ -241,7 +273,10 @@ int llmc_hessian_tiles(int64_t d);
  *      types; TENSOR, CHANNEL, GROUP or BLOCK; other options below), writing the fake-quantized bf16
  *      weight and the summed loss (float32 scalar).  Dead columns are zeroed
  *      first (:38).  HinvT (optional) is the transposed factor from step 2.  workspace: see llmc_gptq_quantize_workspace_size.
- * Nothing synchronises; *status is read by the caller when it needs it. */
+ * Nothing synchronises; *status is read by the caller when it needs it.  The
+ * tensor-core GEMMs of steps 2 and 3 raise *status to LLMC_ETIMEOUT (the
+ * largest code, so it is never masked by LLMC_ENOT_PD) if one of their
+ * bounded waits runs out; the results are then unusable. */
 int llmc_gptq_prepare_hessian(float* H, int64_t d, float percdamp, uint8_t* dead, void* stream);
 int llmc_gptq_hinv_workspace_size(int64_t d, int64_t* bytes);
 int llmc_gptq_hinv(const float* H, int64_t d, float* Hinv, float* HinvT, void* workspace, int* status,
@@ -249,7 +284,7 @@ int llmc_gptq_hinv(const float* H, int64_t d, float* Hinv, float* HinvT, void* w
 int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes);
 int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
                        const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp,
-                       int64_t blocksize, void* wq_bf16, float* loss, void* workspace, const int* status,
+                       int64_t blocksize, void* wq_bf16, float* loss, void* workspace, int* status,
                        void* stream);
 
 /* Activation ordering and the other quantization options of the block loop
@@ -299,7 +334,7 @@ int llmc_permute_columns_bf16(const void* src, int64_t rows, int64_t cols, const
 int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
                           const uint8_t* dead, const LlmcQuantArgs* args, const void* scale, const int8_t* zp,
                           const LlmcGptqColumns* cx, int64_t blocksize, void* wq_bf16, float* loss,
-                          void* workspace, const int* status, void* stream);
+                          void* workspace, int* status, void* stream);
 
 /* Float32-accurate GEMM on the tensor cores (3xTF32 split):
  *   C (m x n, ldc) = A*B^T (mode 0), C - A*B^T (mode 1) or -A*B^T (mode 2),
@@ -322,9 +357,11 @@ int llmc_gemm_f32_nt(int64_t m, int64_t n, int64_t k, const float* A, int64_t ld
  *    llmc_gptq_quantize_workspace_size(rows, cols) exceeds the array
  *    (rows*cols*4 + rows*2052 + 272 bytes > 32 MiB; e.g. 1024 x 4096 fits,
  *    4096 x 4096 does not).
- *  - The first call on a device looks up the array's device address
- *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture.
+ *  - Each call made outside stream capture looks up the array's device
+ *    address (cudaGetSymbolAddress) with the current device; a call during
+ *    capture uses the address found by the last call outside capture on that
+ *    device, so make the first call on a device before any stream capture
+ *    (a first call during capture returns LLMC_EINVAL_ARG).
  *  - Every call shares the one array: calls whose kernels overlap on the GPU
  *    (other streams, other host threads) race and corrupt each other.
  *    Calls ordered on one stream are safe; nothing from a previous call's
@@ -333,7 +370,7 @@ int llmc_gemm_f32_nt(int64_t m, int64_t n, int64_t k, const float* A, int64_t ld
 #define LLMC_GPTQ_NOALLOC_SCRATCH_BYTES (32ll << 20)
 int llmc_gptq_quantize_noalloc(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv,
                                const float* HinvT, const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16,
-                               const int8_t* zp, int64_t blocksize, void* wq_bf16, float* loss, const int* status,
+                               const int8_t* zp, int64_t blocksize, void* wq_bf16, float* loss, int* status,
                                void* stream);
 
 #ifdef __cplusplus

@@ -36,6 +36,11 @@ class NotPositiveDefinite(LlmcError):
     """The damped Hessian has no Cholesky factor (``torch._C._LinAlgError`` in the reference)."""
 
 
+class DeviceTimeout(LlmcError):
+    """A bounded wait inside a tensor-core kernel ran out; the kernel stopped
+    early and its outputs are unusable (the GPU context stays usable)."""
+
+
 class QuantArgs(ctypes.Structure):
     _fields_ = [
         ("num_bits", ctypes.c_int32),
@@ -77,6 +82,7 @@ _SIGS = {
     "llmc_version": [],
     "llmc_kernel_launches": [],
     "llmc_status_string": [_I32],
+    "llmc_last_cuda_error": [],
     "llmc_observe_minmax": [_P, _I64, _I64, _QA, _P, _P, _P],
     "llmc_observe_mse_workspace_size": [_I64, _I64, _QA, _P],
     "llmc_modelfree_quantize_batch": [ctypes.POINTER(CastJob), _I32, _QA, _I32, _P],
@@ -90,7 +96,8 @@ _SIGS = {
     "llmc_modelfree_quantize": [_P, _I64, _I64, _QA, _P, _I32, _P, _P, _P, _P],
     "llmc_pack_zero_point": [_P, _I64, _I64, _I32, _P, _P],
 }
-_RESTYPES = {"llmc_status_string": ctypes.c_char_p, "llmc_kernel_launches": ctypes.c_int64}
+_RESTYPES = {"llmc_status_string": ctypes.c_char_p, "llmc_kernel_launches": ctypes.c_int64,
+             "llmc_last_cuda_error": ctypes.c_char_p}
 
 
 def _register(lib, name, argtypes, restype=ctypes.c_int):
@@ -140,7 +147,50 @@ def check(status: int, what: str = "") -> None:
         raise NotImplementedError(msg)
     if status == ENOT_PD:
         raise NotPositiveDefinite(status, msg)
+    if status == ECUDA:
+        detail = (lib().llmc_last_cuda_error() or b"").decode()
+        if detail:
+            msg = f"{msg} ({detail})"
     raise LlmcError(status, msg)
+
+
+_error_words: dict = {}
+
+
+def error_word(device: torch.device | int | str | None = None) -> torch.Tensor:
+    """The per-device int32 status word the tensor-core kernels raise to
+    ``ETIMEOUT`` when a bounded wait runs out.  Launches never read it, so
+    passing it costs no host sync; ``check_device_errors`` reads it."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    w = _error_words.get(dev.index)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=dev)
+        _error_words[dev.index] = w
+    return w
+
+
+def check_device_errors(device: torch.device | int | str | None = None, what: str = "") -> None:
+    """Read the device's status word (one host sync); if a kernel reported a
+    timeout since the last check, clear the word and raise ``DeviceTimeout``."""
+    w = error_word(device)
+    code = int(w.item())
+    if code != OK:
+        w.zero_()
+        raise_status(code, what or "device kernel")
+
+
+def raise_status(code: int, what: str) -> None:
+    """Raise the exception for a status read back from the device."""
+    if code == OK:
+        return
+    msg = f"{what}: {lib().llmc_status_string(code).decode()}"
+    if code == ETIMEOUT:
+        raise DeviceTimeout(code, msg)
+    if code == ENOT_PD:
+        raise NotPositiveDefinite(code, msg)
+    raise LlmcError(code, msg)
 
 
 def stream_ptr(device: torch.device | None = None) -> int:

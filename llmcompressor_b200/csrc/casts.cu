@@ -14,6 +14,8 @@
 // STATS (min/max only) and GIVEN (quantize + pack with stored qparams).
 #include "llmc_common.cuh"
 
+#include <cstdio>
+
 #include <string.h>
 
 #include <algorithm>
@@ -1552,9 +1554,19 @@ static int check_fmt(const QArgs& a, int fmt) {
 
 using namespace llmc;
 
+namespace llmc {
+static thread_local char g_last_error[256] = "";
+int cuda_fail(const char* where, int e) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%d)", where, cudaGetErrorString((cudaError_t)e), e);
+  return LLMC_ECUDA;
+}
+}  // namespace llmc
+
 extern "C" {
 
 int llmc_version(void) { return 100; }
+
+const char* llmc_last_cuda_error(void) { return llmc::g_last_error; }
 
 int64_t llmc_kernel_launches(void) { return (int64_t)g_launches.load(std::memory_order_relaxed); }
 

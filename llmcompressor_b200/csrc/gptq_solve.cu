@@ -52,6 +52,7 @@ struct GemmArgs {
   int tri, b_lower;
   const int* skip;
   int max_ctas;  // tensor-core path: at most this many CTAs (0: one per SM)
+  int* status;   // tensor-core path: raised to LLMC_ETIMEOUT if a bounded wait runs out
 };
 
 constexpr int GBM = 128, GBN = 128, GBK = 8;
@@ -191,6 +192,7 @@ static int launch_gemm(bool ta, bool tb, const GemmArgs& g, cudaStream_t st) {
     t.A = g.A; t.lda = g.lda; t.a_mn = ta;
     t.B = g.B; t.ldb = g.ldb; t.b_mn = !tb;
     t.C = g.C; t.ldc = g.ldc; t.mode = g.mode; t.tri = g.tri; t.skip = g.skip; t.max_ctas = g.max_ctas;
+    t.status = g.status;
     const int s = tc32::gemm(t, st);
     if (s != LLMC_ENOSUPPORT) return s;
   }
@@ -419,7 +421,7 @@ __global__ void __launch_bounds__(512) k_potrf_diag(float* B, int64_t ld, int64_
     }
     __syncthreads();
   }
-  if (t == 0 && bad && status) atomicExch(status, LLMC_ENOT_PD);
+  if (t == 0 && bad && status) atomicMax(status, (int)LLMC_ENOT_PD);
   // off-diagonal blocks of the inverse, by block row bi:
   //   T = L[rows of bi, :oi] * X[:oi, :oi],  X[rows of bi, :oi] = -X_ii * T.
   // A thread holds 2 rows x 3 columns of the block row (16 warps x 32 lanes);
@@ -1047,20 +1049,20 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* w
     const int rem = (int)(d - kb0 - kb);
     if (rem > 0) {
       // T = B[kb0+kb:, kb0:kb0+kb] * Linv_kk^T, then the panel back into B
-      GemmArgs g1 = {rem, kb, kb, B + (kb0 + kb) * d + kb0, d, Ld, PB, T, PB, 0, 0, 0, nullptr};
+      GemmArgs g1 = {rem, kb, kb, B + (kb0 + kb) * d + kb0, d, Ld, PB, T, PB, 0, 0, 0, nullptr, 0, status};
       if (launch_gemm(false, true, g1, st)) return LLMC_ECUDA;
       k_copy2d<<<dim3(1, rem), 128, 0, st>>>(T, PB, B + (kb0 + kb) * d + kb0, d, rem, kb); llmc::note_launch();
       // (a) the next block column: B[kb0+kb:, kb0+kb : +kn] -= T T[:kn]^T
       const int kn = std::min(PB, rem);
       if (la.main_waits_side()) return LLMC_ECUDA;
-      GemmArgs ga = {rem, kn, kb, T, PB, T, PB, B + (kb0 + kb) * d + kb0 + kb, d, 1, 0, 0, nullptr};
+      GemmArgs ga = {rem, kn, kb, T, PB, T, PB, B + (kb0 + kb) * d + kb0 + kb, d, 1, 0, 0, nullptr, 0, status};
       if (launch_gemm(false, true, ga, st)) return LLMC_ECUDA;
       // (b) the rest of the lower trailing block, on the side stream
       if (rem > kn) {
         if (la.side_waits_main()) return LLMC_ECUDA;
         const int64_t o = kb0 + kb + kn;
         GemmArgs gb = {rem - kn, rem - kn, kb, T + (int64_t)kn * PB, PB, T + (int64_t)kn * PB, PB, B + o * d + o, d,
-                       1, 1, 0, nullptr, kSideCtas};
+                       1, 1, 0, nullptr, kSideCtas, status};
         if (launch_gemm(false, true, gb, la.side_or_main())) return LLMC_ECUDA;
         if (la.side_done()) return LLMC_ECUDA;
       }
@@ -1080,18 +1082,18 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* w
     const int nc = (int)(i0 + ib);  // rows of Xt that can be non-zero in these columns
     const float* Ld = LinvD + (i0 / PB) * PB * PB;
     k_copy2d<<<dim3(1, nc), 128, 0, st>>>(Xt + i0, d, T0, PB, nc, ib); llmc::note_launch();
-    GemmArgs g1 = {nc, ib, ib, T0, PB, Ld, PB, Xt + i0, d, 0, 0, 0, nullptr};
+    GemmArgs g1 = {nc, ib, ib, T0, PB, Ld, PB, Xt + i0, d, 0, 0, 0, nullptr, 0, status};
     if (launch_gemm(false, true, g1, st)) return LLMC_ECUDA;
     const int rem = (int)(d - i0 - ib);
     if (rem > 0) {
       const int kn = std::min(PB, rem);
       if (la.main_waits_side()) return LLMC_ECUDA;
-      GemmArgs ga = {nc, kn, ib, Xt + i0, d, B + (i0 + ib) * d + i0, d, Xt + i0 + ib, d, 1, 0, 0, nullptr};
+      GemmArgs ga = {nc, kn, ib, Xt + i0, d, B + (i0 + ib) * d + i0, d, Xt + i0 + ib, d, 1, 0, 0, nullptr, 0, status};
       if (launch_gemm(false, true, ga, st)) return LLMC_ECUDA;
       if (rem > kn) {
         if (la.side_waits_main()) return LLMC_ECUDA;
         const int64_t o = i0 + ib + kn;
-        GemmArgs gb = {nc, rem - kn, ib, Xt + i0, d, B + o * d + i0, d, Xt + o, d, 1, 0, 0, nullptr, kSideCtas};
+        GemmArgs gb = {nc, rem - kn, ib, Xt + i0, d, B + o * d + i0, d, Xt + o, d, 1, 0, 0, nullptr, kSideCtas, status};
         if (launch_gemm(false, true, gb, la.side_or_main())) return LLMC_ECUDA;
         if (la.side_done()) return LLMC_ECUDA;
       }
@@ -1113,7 +1115,7 @@ int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes
 int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
                           const uint8_t* dead, const LlmcQuantArgs* args, const void* scale, const int8_t* zp,
                           const LlmcGptqColumns* cx, int64_t blocksize, void* wq_bf16, float* loss_out,
-                          void* workspace, const int* status, void* stream) {
+                          void* workspace, int* status, void* stream) {
   if (!args || !Hinv || !loss_out || !workspace || rows < 0 || cols <= 0 || blocksize < 1) return LLMC_EINVAL_ARG;
   const LlmcGptqColumns none = {};
   const LlmcGptqColumns& x = cx ? *cx : none;
@@ -1187,11 +1189,11 @@ int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const 
   auto update = [&](int64_t n0, int64_t n1, int64_t e0, int64_t h0, int k) -> bool {
     if (HinvT) {
       GemmArgs g = {(int)rows, (int)(n1 - n0), k, E + e0, QOB, HinvT + n0 * cols + h0, cols, W + n0, cols, 1, 0, 0,
-                    status};
+                    status, 0, status};
       return launch_gemm(false, true, g, st) == LLMC_OK;
     }
     GemmArgs g = {(int)rows, (int)(n1 - n0), k, E + e0, QOB, Hinv + h0 * cols + n0, cols, W + n0, cols, 1, 0, 0,
-                  status};
+                  status, 0, status};
     return launch_gemm(false, false, g, st) == LLMC_OK;
   };
   for (int64_t o1 = 0; o1 < cols; o1 += ostep) {
@@ -1218,7 +1220,7 @@ int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const 
 
 int llmc_gptq_quantize(const void* w_bf16, int64_t rows, int64_t cols, const float* Hinv, const float* HinvT,
                        const uint8_t* dead, const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp,
-                       int64_t blocksize, void* wq_bf16, float* loss_out, void* workspace, const int* status,
+                       int64_t blocksize, void* wq_bf16, float* loss_out, void* workspace, int* status,
                        void* stream) {
   return llmc_gptq_quantize_ex(w_bf16, rows, cols, Hinv, HinvT, dead, args, scale_bf16, zp, nullptr, blocksize,
                                wq_bf16, loss_out, workspace, status, stream);

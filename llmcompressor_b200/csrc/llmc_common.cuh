@@ -21,6 +21,10 @@ namespace llmc {
 // Host-side count of kernel launches issued by this library (llmc_kernel_launches).
 void note_launch();
 
+// Records which CUDA runtime/driver call failed, and why, for
+// llmc_last_cuda_error (per host thread); returns LLMC_ECUDA.
+int cuda_fail(const char* where, int cuda_error);
+
 // ----------------------------------------------------------------- bf16
 __device__ __forceinline__ float bf16_to_f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
 __device__ __forceinline__ uint16_t f_to_bf16(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }

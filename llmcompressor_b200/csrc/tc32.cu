@@ -272,7 +272,7 @@ k_gemm_tc32(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CU
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
-  if (threadIdx.x == 0 && *abort_flag && p.status) atomicExch(p.status, LLMC_ETIMEOUT);
+  if (threadIdx.x == 0 && *abort_flag && p.status) atomicMax(p.status, (int)LLMC_ETIMEOUT);
 }
 
 // ------------------------------------------------------------------------ host
@@ -326,7 +326,7 @@ int gemm(const Gemm& g, cudaStream_t st) {
   p.tiles_n = (g.n + BN - 1) / BN;
   p.num_tiles = g.tri ? p.tiles_m * (p.tiles_m + 1) / 2 : p.tiles_m * p.tiles_n;
   p.mode = g.mode; p.tri = g.tri; p.a_mn = g.a_mn; p.b_mn = g.b_mn;
-  p.C = g.C; p.ldc = g.ldc; p.status = nullptr;
+  p.C = g.C; p.ldc = g.ldc; p.status = g.status;
   {
     static std::mutex mu;
     static uint64_t done = 0;

@@ -21,6 +21,7 @@ struct Gemm {
   int tri;   // only output tiles touching the lower triangle (row >= col)
   const int* skip;  // optional device flag: do nothing when set
   int max_ctas;     // > 0: at most this many CTAs (leaves SMs to concurrent work); else one per SM
+  int* status;      // optional device word: raised to LLMC_ETIMEOUT if a bounded wait runs out
 };
 
 // Launches the tensor-core GEMM; returns LLMC_ENOSUPPORT (launching nothing)

@@ -23,10 +23,23 @@ _P, _I64, _I32, _F32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_f
 _lib.extend_signatures(
     {
         "llmc_hessian_accumulate": [_P, _I64, _I64, _I64, _P, _F32, _P, _F32, _P, _P],
+        "llmc_hessian_accumulate_grouped": [_P, _I64, _I64, _I64, _I64, _P, _F32, _P, _F32, _P, _P, _P],
         "llmc_hessian_tiles": [_I64],
         "llmc_gemm_f32_nt": [_I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I64, _I32, _P],
     }
 )
+
+
+class HessianOpts(ctypes.Structure):
+    """LlmcHessianOpts (include/llmc_b200.h)."""
+
+    _fields_ = [
+        ("fold_tokens", ctypes.c_int64),
+        ("wait_ns", ctypes.c_int64),
+        ("test_stall", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+    ]
+
 
 GPTQ_PRECISION = torch.float32
 
@@ -41,48 +54,48 @@ def make_empty_hessian(module: torch.nn.Module, device: torch.device | None = No
     return torch.zeros((num_columns, num_columns), device=device, dtype=GPTQ_PRECISION)
 
 
-# Tokens per tensor-core launch of the drop-in accumulate_hessian.  The
-# tcgen05 float32 accumulation loses a little on every accumulate step, with a
-# negative bias that grows with the tokens one launch accumulates (relative
-# error against the exact sum, measured on B200: 4.4e-6 at 2048 tokens,
-# 2.6e-5 at 8192, 5.4e-5 at 16384, 1.8e-4 at 40000; launches summed into H by
-# the reduce-add epilogue add nothing measurable).  2048 tokens -- the
-# reference's per-sample hook call -- keeps H within 1e-5 of the exact sum.
-EXACT_TOKENS_PER_LAUNCH = 2048
-
-
 def hessian_update_(H: torch.Tensor, x2d: torch.Tensor, alpha: float = 2.0,
                     num_samples: torch.Tensor | None = None, num_add: float = 0.0,
-                    max_tokens: int | None = None) -> torch.Tensor:
+                    groups: int = 1, fold_tokens: int = 0, wait_ns: int = 0,
+                    status: torch.Tensor | None = None, _test_stall: bool = False) -> torch.Tensor:
     """H += alpha * x^T x for x (tokens, d) bf16 on the tensor cores; optionally
-    num_samples += num_add in the same launch.  ``max_tokens``: at most that
-    many tokens per launch (see ``EXACT_TOKENS_PER_LAUNCH``)."""
-    if max_tokens is not None and x2d.shape[0] > max_tokens:
-        n = x2d.shape[0]
-        for i, t0 in enumerate(range(0, n, max_tokens)):
-            hessian_update_(H, x2d[t0:t0 + max_tokens], alpha, num_samples if i == 0 else None,
-                            num_add if i == 0 else 0.0)
-        return H
+    num_samples += num_add in the same launch.  Any number of tokens per call:
+    the kernel folds its tensor-core accumulators into float32 sums every
+    ``fold_tokens`` tokens (0: the library default, 1024), so H stays within
+    the Hessian bar of the exact sum however long the call.
+
+    ``groups`` > 1: block-diagonal Hessians -- x is (tokens, groups * d) and
+    H is (groups * d, d); group g accumulates columns [g*d, (g+1)*d) of x into
+    rows [g*d, (g+1)*d) of H (one Hessian per MoE expert).
+
+    A bounded wait that runs out inside the kernel raises ``status`` (default:
+    the device's error word, read by ``_lib.check_device_errors``) to ETIMEOUT;
+    this call itself never synchronises.  ``wait_ns`` / ``_test_stall`` exist
+    for the tests of that path."""
     require_cuda(H, x2d)
     if x2d.dtype != torch.bfloat16:
         raise NotImplementedError(f"Hessian inputs of dtype {x2d.dtype}: the tensor-core path takes bf16")
-    if H.dtype != torch.float32 or not H.is_contiguous() or H.ndim != 2 or H.shape[0] != H.shape[1]:
-        raise ValueError("H must be a contiguous float32 (d, d) tensor")
-    d = H.shape[0]
-    if x2d.shape[-1] != d:
-        raise ValueError(f"input feature size {x2d.shape[-1]} != Hessian size {d}")
+    groups = int(groups)
+    if H.dtype != torch.float32 or not H.is_contiguous() or H.ndim != 2 or H.shape[0] != groups * H.shape[1]:
+        raise ValueError("H must be a contiguous float32 (groups * d, d) tensor")
+    d = H.shape[1]
+    if x2d.shape[-1] != groups * d:
+        raise ValueError(f"input feature size {x2d.shape[-1]} != Hessian size {groups} x {d}")
     if x2d.stride(-1) != 1:
         x2d = x2d.contiguous()
     n = x2d.shape[0]
-    ld = x2d.stride(0) if n > 1 else d
+    ld = x2d.stride(0) if n > 1 else groups * d
     ns = None
     if num_samples is not None:
         require_cuda(num_samples)
         if num_samples.dtype != torch.float32:
             raise ValueError("num_samples must be a float32 tensor")
         ns = num_samples
-    check(lib().llmc_hessian_accumulate(ptr(x2d), n, d, ld, ptr(H), float(alpha), ptr(ns), float(num_add), None,
-                                        stream_ptr(H.device)), "hessian_accumulate")
+    st = status if status is not None else _lib.error_word(H.device)
+    opts = HessianOpts(int(fold_tokens), int(wait_ns), 1 if _test_stall else 0, 0)
+    check(lib().llmc_hessian_accumulate_grouped(ptr(x2d), n, groups, d, ld, ptr(H), float(alpha), ptr(ns),
+                                                float(num_add), ptr(st), ctypes.byref(opts), stream_ptr(H.device)),
+          "hessian_accumulate")
     return H
 
 
@@ -95,9 +108,8 @@ def accumulate_hessian(
     """``accumulate_hessian`` (S/modifiers/gptq/gptq_quantize.py:63-97).
 
     ``num_samples`` counts the batch dimension (a 2-D input counts as one
-    sample) and is updated in place on the device, as is ``H``.  Inputs are
-    folded in launches of at most ``EXACT_TOKENS_PER_LAUNCH`` tokens, which
-    keeps H within 1e-5 (relative Frobenius) of the exact sum.
+    sample) and is updated in place on the device, as is ``H``; one launch per
+    call, with no host sync.
     """
     inp = inp.to(device=H.device)
     if len(inp.shape) == 2:
@@ -108,9 +120,9 @@ def accumulate_hessian(
     x = inp.reshape((-1, inp.shape[-1]))
     if num_samples.device != H.device or num_samples.dtype != torch.float32:
         num_samples += num_added
-        hessian_update_(H, x, 2.0, max_tokens=EXACT_TOKENS_PER_LAUNCH)
+        hessian_update_(H, x, 2.0)
     else:
-        hessian_update_(H, x, 2.0, num_samples, float(num_added), max_tokens=EXACT_TOKENS_PER_LAUNCH)
+        hessian_update_(H, x, 2.0, num_samples, float(num_added))
     return H, num_samples
 
 
@@ -120,21 +132,17 @@ class BatchedHessian:
     The reference accumulates each Linear's Hessian once per calibration
     sample from its forward hook (S/modifiers/gptq/base.py:255-289 ->
     ``accumulate_hessian``, S/modifiers/gptq/gptq_quantize.py:63-97): 2048
-    tokens per call, where the tensor-core kernel runs at about 55% of its
-    rate for 16384 tokens.  This class keeps the calls' inputs in a device
-    buffer of ``chunk_tokens`` rows and folds a full buffer into H with one
-    launch (an input at least that long goes straight to the kernel), so the
-    hook pays only a device-to-device copy.  ``num_samples`` counts as the
-    reference does: the batch dimension, a 2-D input counting as one.
+    tokens per call, too few to keep every SM pair busy for long.  This class
+    keeps the calls' inputs in a device buffer of ``chunk_tokens`` rows and
+    folds a full buffer into H with one launch (an input at least that long
+    goes straight to the kernel), so the hook pays only a device-to-device
+    copy.  ``num_samples`` counts as the reference does: the batch dimension,
+    a 2-D input counting as one.  The kernel's in-launch folding keeps the
+    accuracy of the per-call drop-in at any chunk size.
 
     Call ``finalize()`` (or ``flush()``) before reading H: up to
     ``chunk_tokens - 1`` tokens may still sit in the buffer.  Calls must come
-    from one stream (the buffer is reused in stream order).  Accuracy follows
-    the tokens per launch (``EXACT_TOKENS_PER_LAUNCH``): 16384-token chunks
-    (the default, 1.8x the rate of 2048-token launches) give H within about
-    6e-5 of the exact sum, almost all of it a uniform scale, to which GPTQ is
-    insensitive (damping is relative to the mean diagonal); chunk_tokens=2048
-    keeps 1e-5.
+    from one stream (the buffer is reused in stream order).
     """
 
     def __init__(self, d: int, device: torch.device | str = "cuda", chunk_tokens: int = 16384,
@@ -158,7 +166,7 @@ class BatchedHessian:
         while pos < n:
             if self._fill == 0 and n - pos >= self.chunk:
                 take = n - pos - (n - pos) % self.chunk  # whole chunks go straight to the kernel
-                hessian_update_(self.H, x[pos:pos + take], 2.0, max_tokens=self.chunk)
+                hessian_update_(self.H, x[pos:pos + take], 2.0)
                 pos += take
                 continue
             take = min(self.chunk - self._fill, n - pos)
@@ -278,7 +286,12 @@ class InverseHessian:
         self.hinv, self.dead, self.status, self.hinv_t, self.perm = hinv, dead, status, hinv_t, perm
 
     def ok(self) -> bool:
-        return int(self.status.item()) != _lib.ENOT_PD
+        """False when the factorisation fell back to the identity (ENOT_PD);
+        raises ``DeviceTimeout`` if a kernel of the solve timed out."""
+        code = int(self.status.item())
+        if code == _lib.ETIMEOUT:
+            _lib.raise_status(code, "gptq solve")
+        return code != _lib.ENOT_PD
 
 
 def inverse_hessian(H: torch.Tensor, percdamp: float = 0.01, actorder=None) -> InverseHessian:
@@ -460,6 +473,8 @@ def quantize_weight(
     else:
         scale, zp, gs = weight_qparams(module, quant_args)
     wq, loss = quantize_with_inverse(module.weight, quant_args, hinv, scale, zp, blocksize, order, gs, g_idx)
+    # one host sync: Hessian-accumulation timeouts since the last check, then the factor's status
+    _lib.check_device_errors(module.weight.device, "hessian_accumulate")
     if not hinv.ok():
         _warn_fallback()
     zp_dtype = getattr(quant_args, "zp_dtype", None) or torch.int8

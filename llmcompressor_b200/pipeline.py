@@ -89,6 +89,17 @@ class LayerHessians:
         gptq.hessian_update_(self.H[key], x2d, alpha)
 
 
+def _fold_timeouts(statuses: list[torch.Tensor], err: torch.Tensor) -> None:
+    """Raise the device error word to ETIMEOUT if any factor's status says a
+    solve kernel timed out (an ENOT_PD fallback is not an error); queued on
+    the current stream, no host sync.  ``_lib.check_device_errors`` reads it."""
+    if not statuses:
+        return
+    s = torch.cat([t.reshape(1) for t in statuses])
+    hit = torch.where(s == _lib.ETIMEOUT, s, torch.zeros_like(s)).amax().reshape(1)
+    torch.maximum(err, hit, out=err)
+
+
 _STREAMS: dict[int, list[torch.cuda.Stream]] = {}
 
 
@@ -122,7 +133,12 @@ def solve_layer(
     The independent pieces run concurrently on side streams: the
     factorisations of the distinct Hessians, and each module's block loop as
     soon as its factor is ready.  The caller's stream waits for all of them
-    before this function returns, so results are ordered on it as usual."""
+    before this function returns, so results are ordered on it as usual.
+
+    Nothing here synchronises the host: a kernel timeout (Hessian
+    accumulation or solve) is left in the device error word, which the
+    caller reads once, when it syncs anyway, with
+    ``_lib.check_device_errors``."""
     rank, ws = world()
     dims = hessians.dims
     # activation ordering WEIGHT / STATIC permutes each Hessian's columns;
@@ -215,6 +231,7 @@ def solve_layer(
         for t in (v.hinv, v.dead, v.status, v.hinv_t, v.perm):
             if t is not None:
                 t.record_stream(main)
+    _fold_timeouts([v.status for v in inv.values()], _lib.error_word(dev))
 
     out: dict[str, LayerResult] = {}
     for s in specs:

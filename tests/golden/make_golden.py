@@ -21,6 +21,14 @@ seeded synthetic inputs and stores inputs and outputs as ``.npz`` files:
 * ``gptq_<case>.npz`` -- ``quantize_weight``
   (``S/modifiers/gptq/gptq_quantize.py:100-296``) on a Hessian built from
   seeded activations.
+* ``oneshot_c1.npz`` -- the reference's ``oneshot`` (sequential pipeline,
+  ``GPTQModifier(scheme="W4A16", actorder=None, ignore=["lm_head"])``,
+  ``S/entrypoints/oneshot.py:285``) on the 2-layer Llama of
+  ``llmcompressor_b200.synthetic`` (hidden 1024, 32 x 512 calibration
+  tokens), then ``compress_module`` of every quantized Linear: the first 128
+  rows of each ``weight_packed`` / ``weight_scale`` (GPTQ rows are
+  independent given the Hessian, so a row sample is a fair sample), the
+  weight shapes, and the final hidden-state error of the quantized model.
 
 bf16 tensors are stored as ``uint16`` bit patterns, fp8 as ``uint8``.
 Only run where a reference checkout exists:
@@ -457,8 +465,61 @@ def gen_act_observers():
         print("actobs", name, arrays["min3"][:4], arrays["max3"][:4], arrays["scale"].reshape(-1)[:2])
 
 
+# --------------------------------------------------------------------------
+# oneshot GPTQ W4A16 end to end (config C1)
+# --------------------------------------------------------------------------
+
+ONESHOT_ROWS = 128
+
+
+def gen_oneshot_c1():
+    import time
+
+    from torch.utils.data import DataLoader
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from llmcompressor_b200 import synthetic
+
+    from llmcompressor import oneshot
+    from llmcompressor.modifiers.gptq import GPTQModifier
+
+    model = synthetic.random_llama("c1")
+    ids = synthetic.calibration_tokens("c1")
+    data = [{"input_ids": ids[i:i + 1], "attention_mask": torch.ones_like(ids[i:i + 1])} for i in range(len(ids))]
+    t0 = time.time()
+    oneshot(model=model, dataset=DataLoader(data, batch_size=None, shuffle=False), processor=object(),
+            recipe=GPTQModifier(targets="Linear", scheme="W4A16", ignore=["lm_head"], actorder=None,
+                                block_size=128, dampening_frac=0.01),
+            pipeline="sequential", num_calibration_samples=len(ids), shuffle_calibration_samples=False)
+    secs = time.time() - t0
+    arrays = {"oneshot_seconds": np.array(secs), "rows": np.array(ONESHOT_ROWS)}
+    # end-to-end effect: final hidden states of the quantized model against the unquantized one
+    fp = synthetic.random_llama("c1")
+    with torch.no_grad():
+        hq = model.model(ids[:4]).last_hidden_state.float()
+        hf = fp.model(ids[:4]).last_hidden_state.float()
+    arrays["hidden_rel_err"] = (torch.linalg.norm((hq - hf).reshape(4, -1), dim=1)
+                                / torch.linalg.norm(hf.reshape(4, -1), dim=1)).numpy()
+    names = []
+    for name, mod in model.named_modules():
+        if not isinstance(mod, torch.nn.Linear) or not hasattr(mod, "weight_scale"):
+            continue
+        compress_module(mod)
+        sd = mod.state_dict()
+        arrays[f"{name}.weight_packed"] = sd["weight_packed"][:ONESHOT_ROWS].numpy()
+        arrays[f"{name}.weight_scale"] = to_np(sd["weight_scale"][:ONESHOT_ROWS])
+        arrays[f"{name}.weight_shape"] = sd["weight_shape"].numpy()
+        names.append(name)
+    arrays["modules"] = np.array(names)
+    np.savez_compressed(os.path.join(HERE, "oneshot_c1.npz"), **arrays)
+    print("oneshot c1", f"{secs:.1f}s", names, arrays["hidden_rel_err"])
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
+    if sys.argv[1:2] == ["oneshot_c1"]:
+        gen_oneshot_c1()
+        sys.exit(0)
     if sys.argv[1:2] == ["act_observers"]:
         gen_act_observers()
         sys.exit(0)
@@ -480,3 +541,4 @@ if __name__ == "__main__":
     gen_gptq()
     gen_gptq_orderings()
     gen_act_observers()
+    gen_oneshot_c1()
