@@ -540,7 +540,7 @@ def run_micro(args) -> None:
     if args.micro == "hessian":
         x = torch.randn(n, d, device=dev, generator=g).to(torch.bfloat16)
         H = torch.zeros(d, d, device=dev)
-        fn = lambda: gptq.hessian_update_(H, x, 2.0 / n)  # noqa: E731
+        fn = lambda: gptq.hessian_update_(H, x, 2.0 / n, fold_tokens=args.fold)  # noqa: E731
         work, unit = n * d * (d + 1) / 1e12, "TFLOP/s"
     elif args.micro in ("gptq", "hinv"):
         w = (0.02 * torch.randn(rows, d, device=dev, generator=g)).to(torch.bfloat16)
@@ -638,6 +638,7 @@ def main():
     ap.add_argument("--micro", choices=["hessian", "hessianhook", "gptq", "hinv", "cast", "castbatch", "actobs"], default=None,
                     help="time one kernel on a small case instead of the model benchmark")
     ap.add_argument("--d", type=int, default=4096)
+    ap.add_argument("--fold", type=int, default=0, help="--micro hessian: tokens per tensor-core partial (0: default)")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--scheme", default="W4A16", choices=list(CAST_SCHEMES), help="format of --micro cast")

@@ -433,6 +433,68 @@ def _warn_fallback():
     )
 
 
+def quantize_modules_shared(
+    modules: list[torch.nn.Module],
+    quant_args,
+    hessian: torch.Tensor,
+    blocksize: int = 128,
+    percdamp: float = 0.01,
+) -> tuple[InverseHessian, list[tuple[torch.Tensor, dict]]]:
+    """``quantize_weight`` for several modules that read the same input (q/k/v,
+    gate/up, the experts of an all-expert MoE layer): the Hessian is factored
+    once and every module runs its block loop against the shared factor.
+    ``quant_args`` is one QuantizationArgs for all modules or a list, one per
+    module (the activation ordering must agree).  No host sync: returns the
+    factor (``ok()`` reads its status) and, per module, (loss as a float32
+    device scalar, q_param_dict as ``quantize_weight`` returns it)."""
+    args_list = list(quant_args) if isinstance(quant_args, (list, tuple)) else [quant_args] * len(modules)
+    orders = []
+    for qa in args_list:
+        strategy = _strategy(qa)
+        order = resolve_actorder(getattr(qa, "actorder", None))
+        if order == "group" and strategy not in ("group", "tensor_group"):
+            from loguru import logger
+
+            logger.warning(
+                "ActivationOrdering.GROUP requires a grouped quantization strategy; "
+                "falling back to actorder=None for this module."
+            )
+            order = None
+        if strategy not in ("tensor", "channel", "group", "tensor_group", "block"):
+            raise ValueError(f"Quantization strategy is not supported for GPTQ: {strategy}")
+        if order == "group" and (strategy == "tensor_group" or _qtype(qa) == "float"):
+            raise NotImplementedError("activation ordering GROUP with float types: scales from float32 statistics "
+                                      "are only built for integer types")
+        orders.append(order)
+    if len({bool(o) for o in orders}) > 1:
+        raise ValueError("modules sharing a Hessian must agree on whether activation ordering is used")
+    hinv = inverse_hessian(hessian, percdamp, orders[0] if orders else None)
+    results = []
+    for module, qa, order in zip(modules, args_list, orders):
+        final_dtype = module.weight.dtype
+        g_idx = None
+        if order == "group":
+            # re-observe the permuted (float32) weight for the groups of the new order (:141-145)
+            wp = permute_columns(module.weight, hinv.perm)
+            scale, zp, gs = weight_qparams(module, qa, weight=wp, stats_dtype=torch.float32)
+            g_idx = torch.empty(module.weight.shape[1], dtype=torch.int32, device=module.weight.device)
+        else:
+            scale, zp, gs = weight_qparams(module, qa)
+        wq, loss = quantize_with_inverse(module.weight, qa, hinv, scale, zp, blocksize, order, gs, g_idx)
+        zp_dtype = getattr(qa, "zp_dtype", None) or torch.int8
+        q_param_dict = {
+            "weight": wq.reshape(module.weight.shape).to(final_dtype),
+            "weight_scale": scale.to(dtype=final_dtype),
+            "weight_zero_point": zp.to(dtype=zp_dtype),
+        }
+        if gs is not None:
+            q_param_dict["weight_global_scale"] = gs.to(dtype=final_dtype)
+        if g_idx is not None:
+            q_param_dict["weight_g_idx"] = g_idx
+        results.append((loss, q_param_dict))
+    return hinv, results
+
+
 def quantize_weight(
     module: torch.nn.Module,
     quant_args,
@@ -447,44 +509,9 @@ def quantize_weight(
         ``weight_global_scale`` (TENSOR_GROUP) and ``weight_g_idx``
         (activation ordering GROUP).
     """
-    strategy = _strategy(quant_args)
-    order = resolve_actorder(getattr(quant_args, "actorder", None))
-    if order == "group" and strategy not in ("group", "tensor_group"):
-        from loguru import logger
-
-        logger.warning(
-            "ActivationOrdering.GROUP requires a grouped quantization strategy; "
-            "falling back to actorder=None for this module."
-        )
-        order = None
-    if strategy not in ("tensor", "channel", "group", "tensor_group", "block"):
-        raise ValueError(f"Quantization strategy is not supported for GPTQ: {strategy}")
-    if order == "group" and (strategy == "tensor_group" or _qtype(quant_args) == "float"):
-        raise NotImplementedError("activation ordering GROUP with float types: scales from float32 statistics "
-                                  "are only built for integer types")
-    final_dtype = module.weight.dtype
-    hinv = inverse_hessian(hessian, percdamp, order)
-    g_idx = None
-    if order == "group":
-        # re-observe the permuted (float32) weight for the groups of the new order (:141-145)
-        wp = permute_columns(module.weight, hinv.perm)
-        scale, zp, gs = weight_qparams(module, quant_args, weight=wp, stats_dtype=torch.float32)
-        g_idx = torch.empty(module.weight.shape[1], dtype=torch.int32, device=module.weight.device)
-    else:
-        scale, zp, gs = weight_qparams(module, quant_args)
-    wq, loss = quantize_with_inverse(module.weight, quant_args, hinv, scale, zp, blocksize, order, gs, g_idx)
+    hinv, [(loss, q_param_dict)] = quantize_modules_shared([module], quant_args, hessian, blocksize, percdamp)
     # one host sync: Hessian-accumulation timeouts since the last check, then the factor's status
     _lib.check_device_errors(module.weight.device, "hessian_accumulate")
     if not hinv.ok():
         _warn_fallback()
-    zp_dtype = getattr(quant_args, "zp_dtype", None) or torch.int8
-    q_param_dict = {
-        "weight": wq.reshape(module.weight.shape).to(final_dtype),
-        "weight_scale": scale.to(dtype=final_dtype),
-        "weight_zero_point": zp.to(dtype=zp_dtype),
-    }
-    if gs is not None:
-        q_param_dict["weight_global_scale"] = gs.to(dtype=final_dtype)
-    if g_idx is not None:
-        q_param_dict["weight_g_idx"] = g_idx
     return float(loss.item()), q_param_dict

@@ -1,0 +1,586 @@
+"""``oneshot`` with ``GPTQModifier`` / ``QuantizationModifier`` on the GPU.
+
+Drop-in for the reference's entry point and modifiers on the
+post-training-quantization path:
+
+* ``oneshot(model, dataset, recipe=GPTQModifier(...))``
+  (S/entrypoints/oneshot.py:285) with the sequential pipeline
+  (S/pipelines/sequential/pipeline.py:55-178): the model is processed one
+  decoder layer at a time; each layer sees the calibration data twice --
+  a calibration pass whose forward hooks accumulate the GPTQ Hessians
+  (S/modifiers/gptq/base.py:255-289), then, after the layer's weights are
+  quantized (``on_sequential_epoch_end``, :239-321), a propagation pass whose
+  outputs, computed with the quantized weights, become the next layer's
+  inputs.
+* ``GPTQModifier``: same arguments and scheme resolution as
+  S/modifiers/gptq/base.py:44-193 (``actorder`` defaults to STATIC for
+  schemes that leave it unset).
+* ``QuantizationModifier``: round-to-nearest weight qparams
+  (S/modifiers/quantization/quantization/base.py:85-137), no calibration
+  data needed for weight-only schemes.
+
+What is structured differently (the results are not):
+
+* Layer inputs live on the GPU between layers (the reference offloads them
+  to the CPU per batch, S/pipelines/cache.py), and calibration samples of
+  equal length are stacked into batches of up to
+  ``calibration_batch_tokens`` tokens per forward call; the Hessian counts
+  samples (the batch dimension), as the reference does.
+* Modules that read the same tensor in a forward pass (q/k/v, gate/up, the
+  experts of an all-expert MoE layer) share one Hessian accumulation and one
+  factorisation (the reference accumulates and factors identical copies).
+* Layers are found as the reference's default sequential targets do: the
+  model's ``_no_split_modules`` classes, in module order.
+
+The arithmetic is the library's CUDA kernels (Hessians, factorisation, block
+loop, observers); the decoder forward passes are the model's own torch code.
+"""
+from __future__ import annotations
+
+import contextlib
+import math
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from . import _lib, gptq, ops
+
+__all__ = ["oneshot", "GPTQModifier", "QuantizationModifier", "OneshotStats"]
+
+
+class _Static:
+    """The modifier-level ``actorder`` default: STATIC where the scheme
+    leaves it unset (S/modifiers/gptq/base.py:142-160)."""
+
+    def __repr__(self):
+        return "Sentinel('static')"
+
+
+_STATIC_DEFAULT = _Static()
+
+
+def _schemes(targets, scheme, config_groups):
+    """QuantizationSchemes of a modifier, in the precedence the reference's
+    ``QuantizationMixin.resolve_quantization_config`` gives them."""
+    from compressed_tensors.quantization import QuantizationScheme
+    from compressed_tensors.quantization.quant_scheme import preset_name_to_scheme
+
+    targets = [targets] if isinstance(targets, str) else list(targets or ["Linear"])
+    out = []
+    if config_groups:
+        for g in config_groups.values():
+            out.append(g if isinstance(g, QuantizationScheme) else QuantizationScheme(**g))
+        return out
+    if scheme is None:
+        raise ValueError("a scheme or config_groups is required")
+    if isinstance(scheme, str):
+        return [preset_name_to_scheme(scheme, targets)]
+    if isinstance(scheme, QuantizationScheme):
+        return [scheme]
+    if isinstance(scheme, dict):
+        if all(isinstance(k, str) and k.isupper() for k in scheme):  # {"W4A16": ["Linear"], ...}
+            for name, tg in scheme.items():
+                out.append(preset_name_to_scheme(name, [tg] if isinstance(tg, str) else list(tg)))
+            return out
+        return [QuantizationScheme(targets=targets, **scheme)]
+    raise ValueError(f"unsupported scheme {scheme!r}")
+
+
+class _Modifier:
+    kind = ""
+
+    def __init__(self, targets="Linear", scheme=None, config_groups=None, ignore=None, **kwargs):
+        self.targets = targets
+        self.scheme = scheme
+        self.config_groups = config_groups
+        self.ignore = list(ignore or [])
+        self.extra = kwargs
+
+    def resolve(self, model: torch.nn.Module) -> dict[str, tuple[torch.nn.Module, object]]:
+        """name -> (module, QuantizationScheme) for every module to quantize."""
+        from compressed_tensors.utils import match_named_modules
+
+        found: dict[str, tuple[torch.nn.Module, object]] = {}
+        for sch in self._resolved_schemes():
+            for name, mod in match_named_modules(model, sch.targets, self.ignore):
+                if name in found or sch.weights is None or isinstance(mod, torch.nn.Embedding):
+                    continue
+                found[name] = (mod, sch)
+        if not found:
+            raise ValueError(f"{type(self).__name__} was unable to find any modules to quantize. Please check "
+                             "quantization `config_groups` and `targets` in recipe")
+        return found
+
+    def _resolved_schemes(self):
+        return _schemes(self.targets, self.scheme, self.config_groups)
+
+
+class GPTQModifier(_Modifier):
+    """``GPTQModifier`` (S/modifiers/gptq/base.py:44-140): ``block_size``,
+    ``dampening_frac``, ``actorder`` (default: STATIC unless the scheme sets
+    one), ``offload_hessians`` (accepted; Hessians stay on the GPU),
+    ``targets`` / ``scheme`` / ``config_groups`` / ``ignore``."""
+
+    kind = "gptq"
+
+    def __init__(self, targets="Linear", scheme=None, config_groups=None, ignore=None, block_size: int = 128,
+                 dampening_frac: float | None = 0.01, actorder=_STATIC_DEFAULT, offload_hessians: bool = False,
+                 **kwargs):
+        super().__init__(targets, scheme, config_groups, ignore, **kwargs)
+        self.block_size = int(block_size)
+        self.dampening_frac = 0.01 if dampening_frac is None else float(dampening_frac)
+        self.actorder = actorder
+        self.offload_hessians = offload_hessians
+
+    def _resolved_schemes(self):
+        from compressed_tensors.quantization import QuantizationStrategy
+        from compressed_tensors.quantization.quant_args import ActivationOrdering
+
+        out = []
+        for sch in super()._resolved_schemes():
+            sch = sch.model_copy(deep=True)
+            w = sch.weights
+            if w is not None and w.strategy in (QuantizationStrategy.GROUP, QuantizationStrategy.TENSOR_GROUP,
+                                                QuantizationStrategy.CHANNEL, QuantizationStrategy.TENSOR,
+                                                QuantizationStrategy.BLOCK):
+                existing = w.actorder
+                if self.actorder is _STATIC_DEFAULT:
+                    w.actorder = ActivationOrdering.STATIC if existing is None else existing
+                elif existing is None or self.actorder == existing:
+                    w.actorder = self.actorder
+                else:
+                    raise ValueError(
+                        "Cannot resolve activation ordering when both `GPTQModifier.actorder` and "
+                        f"`QuantizationScheme.actorder` are provided and differ ({self.actorder}, {existing}). "
+                        "Either unset `GPTQModifier.actorder` or remove `actorder` from config groups.")
+                if w.actorder == ActivationOrdering.GROUP and w.strategy not in (
+                        QuantizationStrategy.GROUP, QuantizationStrategy.TENSOR_GROUP):
+                    from loguru import logger
+
+                    logger.warning(f"ActivationOrdering.GROUP is not compatible with strategy={w.strategy}; "
+                                   "falling back to actorder=None for this scheme.")
+                    w.actorder = None
+            out.append(sch)
+        return out
+
+
+class QuantizationModifier(_Modifier):
+    """``QuantizationModifier`` (S/modifiers/quantization/quantization/base.py):
+    round-to-nearest weight qparams from the memoryless min-max observer.
+    Weight-only schemes (and schemes whose activations are dynamic) need no
+    calibration data; static activation schemes are not taken here."""
+
+    kind = "rtn"
+
+
+@dataclass
+class OneshotStats:
+    """Where the time of the last ``oneshot`` call went (wall seconds, host
+    clock around synchronised phases) and the per-module GPTQ losses."""
+
+    seconds: dict = field(default_factory=dict)
+    losses: dict = field(default_factory=dict)
+    samples: int = 0
+    tokens: int = 0
+
+
+LAST_STATS = OneshotStats()
+
+
+# ------------------------------------------------------------------ data
+def _calibration_batches(dataset, num_samples: int, batch_tokens: int, device) -> list[dict]:
+    """Calibration samples as forward-call batches on ``device``: samples of
+    equal length are stacked up to ``batch_tokens`` tokens per call."""
+    samples: list[tuple[torch.Tensor, torch.Tensor | None]] = []
+
+    def add(ids, mask=None):
+        ids = torch.as_tensor(ids)
+        if ids.ndim == 1:
+            ids = ids.unsqueeze(0)
+        mask = None if mask is None else torch.as_tensor(mask).reshape(ids.shape)
+        for i in range(ids.shape[0]):
+            samples.append((ids[i], None if mask is None else mask[i]))
+
+    if isinstance(dataset, torch.Tensor):
+        add(dataset)
+    else:
+        for item in dataset:
+            if len(samples) >= num_samples:
+                break
+            if isinstance(item, dict):
+                add(item["input_ids"], item.get("attention_mask"))
+            elif isinstance(item, (list, tuple)):
+                add(item[0], item[1] if len(item) > 1 else None)
+            else:
+                add(item)
+    samples = samples[:num_samples]
+    if not samples:
+        raise ValueError("oneshot needs calibration samples")
+    batches, i = [], 0
+    while i < len(samples):
+        L = samples[i][0].shape[-1]
+        per = max(1, batch_tokens // max(1, L))
+        j = i
+        while j < len(samples) and j - i < per and samples[j][0].shape[-1] == L:
+            j += 1
+        ids = torch.stack([s[0] for s in samples[i:j]]).to(device, non_blocking=True)
+        masks = [s[1] for s in samples[i:j]]
+        batch = {"input_ids": ids}
+        if any(m is not None for m in masks):
+            batch["attention_mask"] = torch.stack(
+                [m if m is not None else torch.ones_like(s[0]) for m, s in zip(masks, samples[i:j])]).to(device)
+        batches.append(batch)
+        i = j
+    return batches
+
+
+# ------------------------------------------------------------------ layers
+def sequential_layers(model: torch.nn.Module, targets=None) -> list[torch.nn.Module]:
+    """The decoder layers, in order: modules whose class is named in
+    ``targets`` or, by default, in the model's ``_no_split_modules`` (the
+    reference's ``infer_sequential_targets``)."""
+    names = targets or getattr(model, "_no_split_modules", None) or []
+    names = [names] if isinstance(names, str) else list(names)
+    layers = [m for m in model.modules() if type(m).__name__ in names]
+    if not layers:
+        raise ValueError(f"no sequential target layers ({names}) found in {type(model).__name__}")
+    return layers
+
+
+class _Stop(Exception):
+    pass
+
+
+@torch.no_grad()
+def _capture_layer_inputs(model, first_layer, batches) -> list[tuple[torch.Tensor, dict]]:
+    """Run the model up to the first decoder layer for every batch and keep
+    that layer's inputs (hidden states and keyword arguments)."""
+    got = []
+
+    def pre(mod, args, kwargs):
+        got.append((args[0], dict(kwargs), args[1:]))
+        raise _Stop
+
+    h = first_layer.register_forward_pre_hook(pre, with_kwargs=True)
+    try:
+        for b in batches:
+            try:
+                model(**b, use_cache=False)
+            except _Stop:
+                pass
+    finally:
+        h.remove()
+    return got
+
+
+def _layer_out(out):
+    return out[0] if isinstance(out, (tuple, list)) else out
+
+
+# ------------------------------------------------------------------ modules
+def _init_modules(found: dict) -> None:
+    """Attach the compressed-tensors quantization parameters and scheme to
+    every module (``initialize_module_for_quantization``), with fake-quant
+    in the forward disabled while calibrating (``DisableQuantization``)."""
+    from compressed_tensors.quantization import initialize_module_for_quantization
+    from compressed_tensors.quantization.lifecycle.helpers import disable_quantization
+
+    for _, (mod, sch) in found.items():
+        initialize_module_for_quantization(mod, sch, force_zero_point=False)
+        disable_quantization(mod)
+
+
+def _finish_modules(found: dict) -> None:
+    from compressed_tensors.quantization import QuantizationStatus
+    from compressed_tensors.quantization.lifecycle.helpers import enable_quantization
+
+    for _, (mod, _) in found.items():
+        mod.quantization_status = QuantizationStatus.FROZEN
+        enable_quantization(mod)
+
+
+def _set_params(mod: torch.nn.Module, q: dict) -> None:
+    """``update_offload_parameter(module, attr, val)`` for every result the
+    module has a parameter for (compressed-tensors creates them at
+    initialization: no zero point for symmetric schemes), plus ``weight_g_idx``
+    / ``weight_global_scale``, registered when missing."""
+    for k, v in q.items():
+        p = getattr(mod, k, None)
+        if isinstance(p, torch.nn.Parameter):
+            if p.shape == v.shape:
+                p.data.copy_(v.to(p.dtype))
+            else:
+                p.data = v.to(p.dtype)
+        elif k in ("weight_g_idx", "weight_global_scale"):
+            mod.register_parameter(k, torch.nn.Parameter(v, requires_grad=False))
+
+
+def _rtn(found: dict) -> None:
+    """Round-to-nearest weight qparams for every module (GPU observers)."""
+    for name, (mod, sch) in found.items():
+        qa = sch.weights
+        mn, mx = ops.observe_minmax(mod.weight, qa)
+        gs = None
+        if getattr(qa.strategy, "value", qa.strategy) == "tensor_group":
+            gs = ops.fused_global_scale(gptq._fused_weights(mod))
+        scale, zp = ops.calculate_qparams(mn, mx, qa, gs)
+        q = {"weight_scale": scale.to(mod.weight.dtype) if scale.dtype != torch.float32 or gs is None else scale,
+             "weight_zero_point": zp}
+        if gs is not None:
+            q["weight_global_scale"] = gs
+        _set_params(mod, q)
+
+
+# ------------------------------------------------------------------ GPTQ per layer
+class _LayerCalibration:
+    """Forward hooks on one layer's quantized modules: modules that read the
+    same tensor in a forward pass share one Hessian (``BatchedHessian``)."""
+
+    def __init__(self, modules: dict[str, torch.nn.Module]):
+        self.modules = modules  # name -> module
+        self.group_of: dict[str, int] = {}
+        self.groups: list[list[str]] = []
+        self.hess: list[gptq.BatchedHessian] = []
+        self._seen: dict[tuple, int] = {}
+        self._handles = []
+        self._first = True
+        for name, mod in modules.items():
+            self._handles.append(mod.register_forward_hook(self._hook(name)))
+
+    def _hook(self, name):
+        def hook(mod, args, out):
+            x = args[0]
+            key = id(x)
+            if self._first:
+                # the first batch decides the groups; the inputs are held until
+                # it ends, so no id is reused by another tensor meanwhile
+                g = self._seen.get(key, (None,))[0]
+                if g is None:
+                    g = len(self.groups)
+                    self._seen[key] = (g, x)
+                    self.groups.append([])
+                    self.hess.append(gptq.BatchedHessian(x.shape[-1], x.device))
+                    self.hess[g].add(x)
+                self.groups[g].append(name)
+                self.group_of[name] = g
+            else:
+                g = self.group_of[name]
+                if self.groups[g][0] == name:
+                    self.hess[g].add(x)
+        return hook
+
+    def end_batch(self):
+        self._first = False
+        self._seen.clear()
+
+    def remove(self):
+        for h in self._handles:
+            h.remove()
+        self._handles = []
+
+
+def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, stats: OneshotStats) -> None:
+    """Factor each group's Hessian once and quantize its modules; groups run
+    concurrently on side streams (largest Hessian first), the caller's stream
+    waits for all of them."""
+    from .pipeline import _side_streams
+
+    dev = next(iter(cal.modules.values())).weight.device
+    main = torch.cuda.current_stream(dev)
+    order = sorted(range(len(cal.groups)), key=lambda g: -cal.hess[g].d)
+    streams = _side_streams(dev, max(1, len(order)))
+    done = []
+    results = []
+    for i, g in enumerate(order):
+        st = streams[i % len(streams)]
+        st.wait_stream(main)
+        with torch.cuda.stream(st):
+            bh = cal.hess[g]
+            H, n = bh.finalize()
+            for t in (bh.H, bh._buf):  # allocated on the caller's stream, read on this one
+                t.record_stream(st)
+            H = H / n  # the reference's hessian / num_samples (S/modifiers/gptq/base.py:594)
+            names = cal.groups[g]
+            mods = [cal.modules[nm] for nm in names]
+            qas = [found[nm][1].weights for nm in names]
+            hinv, res = gptq.quantize_modules_shared(mods, qas, H, modifier.block_size, modifier.dampening_frac)
+            for nm, mod, (loss, q) in zip(names, mods, res):
+                _set_params(mod, q)
+                results.append((nm, loss, hinv))
+            ev = torch.cuda.Event()
+            ev.record(st)
+            done.append(ev)
+        cal.hess[g] = None  # release the Hessian buffers with the stream's work
+    for ev in done:
+        main.wait_event(ev)
+    for nm, loss, hinv in results:
+        stats.losses[nm] = (loss, hinv)
+
+
+def _check_losses(stats: OneshotStats) -> None:
+    """One host sync at the end: losses to floats, RTN-fallback warnings,
+    kernel timeouts."""
+    warned = set()
+    for nm, v in list(stats.losses.items()):
+        if isinstance(v, tuple):
+            loss, hinv = v
+            if id(hinv) not in warned:
+                warned.add(id(hinv))
+                if not hinv.ok():
+                    gptq._warn_fallback()
+            stats.losses[nm] = float(loss.item())
+
+
+# ------------------------------------------------------------------ entry point
+def oneshot(
+    model: torch.nn.Module,
+    dataset=None,
+    recipe=None,
+    num_calibration_samples: int = 512,
+    shuffle_calibration_samples: bool = True,
+    pipeline: str | None = "sequential",
+    sequential_targets=None,
+    calibration_batch_tokens: int = 16384,
+    device: torch.device | str | None = None,
+    offload_layers: bool | None = None,
+    **kwargs,
+) -> torch.nn.Module:
+    """``oneshot`` (S/entrypoints/oneshot.py:285) for a ``GPTQModifier`` or
+    ``QuantizationModifier`` recipe on a decoder model.
+
+    ``dataset``: a DataLoader / iterable of ``{"input_ids", "attention_mask"}``
+    samples or an (n, L) tensor of token ids; the first
+    ``num_calibration_samples`` are used in order (a DataLoader's own order;
+    shuffling is the DataLoader's business, as in the reference when one is
+    passed).  ``device``: the GPU to calibrate on (default: the model's, or
+    the current CUDA device).  A model left on the CPU is moved there one
+    layer at a time and each quantized layer is moved back
+    (``offload_layers``, default: True when the model starts on the CPU).
+    Returns the model with quantized weights, compressed-tensors scales and
+    zero points, ready for ``save_compressed`` / ``ModelCompressor``.
+    """
+    mods = recipe if isinstance(recipe, (list, tuple)) else [recipe]
+    mods = [m for m in mods if m is not None]
+    if not mods:
+        raise ValueError("oneshot needs a recipe (GPTQModifier or QuantizationModifier)")
+    for m in mods:
+        if not isinstance(m, _Modifier):
+            raise NotImplementedError(f"recipe entry {type(m).__name__}: only GPTQModifier and "
+                                      "QuantizationModifier run on this path")
+    if pipeline not in (None, "sequential", "independent", "basic", "datafree"):
+        raise ValueError(f"unknown pipeline {pipeline!r}")
+    first_param = next(model.parameters())
+    if device is None:
+        device = first_param.device if first_param.is_cuda else torch.device("cuda", torch.cuda.current_device())
+    device = torch.device(device)
+    if offload_layers is None:
+        offload_layers = not first_param.is_cuda
+    stats = OneshotStats()
+    t_all = time.perf_counter()
+
+    gptq_mods = [m for m in mods if m.kind == "gptq"]
+    rtn_mods = [m for m in mods if m.kind == "rtn"]
+    found_all = {}
+    for m in mods:
+        f = m.resolve(model)
+        for k, v in f.items():
+            found_all.setdefault(k, (v[0], v[1], m))
+    found = {k: (v[0], v[1]) for k, v in found_all.items()}
+    _init_modules(found)
+
+    rtn_found = {k: (v[0], v[1]) for k, v in found_all.items() if v[2].kind == "rtn"}
+    gptq_found = {k: (v[0], v[1]) for k, v in found_all.items() if v[2].kind == "gptq"}
+
+    if rtn_found and not gptq_found:
+        # weight-only RTN: no calibration pass (the qparams do not depend on data)
+        for name, (mod, _) in rtn_found.items():
+            if not mod.weight.is_cuda:
+                mod.to(device)
+        _rtn(rtn_found)
+        _finish_modules(found)
+        torch.cuda.synchronize(device)
+        stats.seconds["total"] = time.perf_counter() - t_all
+        globals()["LAST_STATS"] = stats
+        return model
+
+    if dataset is None:
+        raise ValueError("GPTQ needs calibration data (dataset)")
+    modifier = gptq_mods[0]
+    layers = sequential_layers(model, sequential_targets)
+    layer_ids = {id(l) for l in layers}
+    # everything but the layers goes to the device; the layers follow one at a time
+    if offload_layers:
+        _to_device_except(model, layer_ids, device)
+    else:
+        model.to(device)
+    batches = _calibration_batches(dataset, num_calibration_samples, calibration_batch_tokens, device)
+    stats.samples = sum(b["input_ids"].shape[0] for b in batches)
+    stats.tokens = sum(b["input_ids"].numel() for b in batches)
+
+    t0 = time.perf_counter()
+    if offload_layers:
+        layers[0].to(device)
+    cache = _capture_layer_inputs(model, layers[0], batches)
+    torch.cuda.synchronize(device)
+    stats.seconds["capture"] = time.perf_counter() - t0
+
+    name_of = {id(m): n for n, (m, _) in gptq_found.items()}
+    t_layers = time.perf_counter()
+    with torch.no_grad():
+        for li, layer in enumerate(layers):
+            if offload_layers:
+                layer.to(device)
+            lm = {name_of[id(m)]: m for m in layer.modules() if id(m) in name_of}
+            if lm:
+                cal = _LayerCalibration(lm)
+                for (h, kw, rest) in cache:
+                    layer(h, *rest, **kw)
+                    cal.end_batch()
+                cal.remove()
+                _solve_layer(cal, gptq_found, modifier, stats)
+            rl = {n: v for n, v in rtn_found.items() if any(v[0] is m for m in layer.modules())}
+            if rl:
+                _rtn(rl)
+            if li + 1 < len(layers):
+                # propagate: the quantized layer's outputs are the next layer's inputs
+                for i, (h, kw, rest) in enumerate(cache):
+                    cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
+            if offload_layers:
+                layer.to("cpu")
+    torch.cuda.synchronize(device)
+    stats.seconds["layers"] = time.perf_counter() - t_layers
+    # modules outside the layers (none for the usual targets with lm_head ignored)
+    rest = {n: v for n, v in gptq_found.items() if not any(v[0] is m for l in layers for m in l.modules())}
+    if rest:
+        raise NotImplementedError(f"GPTQ targets outside the sequential layers: {sorted(rest)[:4]}")
+    rtn_rest = {n: v for n, v in rtn_found.items() if not any(v[0] is m for l in layers for m in l.modules())}
+    if rtn_rest:
+        _rtn(rtn_rest)
+    _check_losses(stats)
+    _lib.check_device_errors(device, "oneshot")
+    _finish_modules(found)
+    if offload_layers:
+        model.to("cpu")
+    stats.seconds["total"] = time.perf_counter() - t_all
+    globals()["LAST_STATS"] = stats
+    return model
+
+
+def _to_device_except(model: torch.nn.Module, skip_ids: set, device) -> None:
+    """Move every parameter and buffer to ``device`` except those inside the
+    modules in ``skip_ids`` (the decoder layers, moved one at a time)."""
+
+    def visit(mod):
+        if id(mod) in skip_ids:
+            return
+        for k, p in list(mod._parameters.items()):
+            if p is not None and p.device != device:
+                mod._parameters[k] = torch.nn.Parameter(p.data.to(device), requires_grad=p.requires_grad)
+        for k, b in list(mod._buffers.items()):
+            if b is not None and b.device != device:
+                mod._buffers[k] = b.to(device)
+        for c in mod.children():
+            visit(c)
+
+    visit(model)
