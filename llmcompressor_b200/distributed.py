@@ -108,3 +108,20 @@ def gather_rows(local: torch.Tensor, rows: int, dst: int = 0) -> torch.Tensor | 
     if rank != dst:
         return None
     return torch.cat(bufs, dim=0)[:rows]
+
+
+def all_gather_rows(local: torch.Tensor, out: torch.Tensor, rows: int, align: int = 1) -> torch.Tensor:
+    """Every rank's ``row_range`` slice of a (rows, ...) tensor into ``out``
+    on every rank (one padded ``all_gather_into_tensor``)."""
+    _, ws = world()
+    if ws == 1:
+        out.copy_(local)
+        return out
+    units = -(-rows // align)
+    per = -(-units // ws) * align
+    pad = torch.zeros((per,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    pad[: local.shape[0]] = local
+    full = torch.empty((per * ws,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(full, pad)
+    out.copy_(full[:rows])
+    return out

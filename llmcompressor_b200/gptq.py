@@ -54,6 +54,12 @@ def make_empty_hessian(module: torch.nn.Module, device: torch.device | None = No
     return torch.zeros((num_columns, num_columns), device=device, dtype=GPTQ_PRECISION)
 
 
+# Optional instrumentation: when a list, every Hessian launch appends
+# (start event, end event, useful flops) recorded on its stream, so a caller
+# (the benchmark) can time the kernel inside a larger pipeline.
+TIMING_EVENTS: list | None = None
+
+
 def hessian_update_(H: torch.Tensor, x2d: torch.Tensor, alpha: float = 2.0,
                     num_samples: torch.Tensor | None = None, num_add: float = 0.0,
                     groups: int = 1, fold_tokens: int = 0, wait_ns: int = 0,
@@ -93,9 +99,17 @@ def hessian_update_(H: torch.Tensor, x2d: torch.Tensor, alpha: float = 2.0,
         ns = num_samples
     st = status if status is not None else _lib.error_word(H.device)
     opts = HessianOpts(int(fold_tokens), int(wait_ns), 1 if _test_stall else 0, 0)
+    ev = TIMING_EVENTS
+    if ev is not None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record()
     check(lib().llmc_hessian_accumulate_grouped(ptr(x2d), n, groups, d, ld, ptr(H), float(alpha), ptr(ns),
                                                 float(num_add), ptr(st), ctypes.byref(opts), stream_ptr(H.device)),
           "hessian_accumulate")
+    if ev is not None:
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record()
+        ev.append((e0, e1, float(n) * d * (d + 1) * groups))
     return H
 
 

@@ -432,7 +432,220 @@ def _check_losses(stats: OneshotStats) -> None:
             stats.losses[nm] = float(loss.item())
 
 
+# ------------------------------------------------------------------ multi-GPU solve
+def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, stats: OneshotStats,
+                      rank: int, ws: int) -> None:
+    """The multi-rank form of ``_solve_layer`` (the reference's
+    ``compress_modules`` under DDP, S/modifiers/gptq/base.py:291-321,603-645,
+    restructured): every shared Hessian is summed onto an owner rank chosen by
+    solve cost, the owner factors it and broadcasts the upper factor (each
+    rank forms its transpose locally), every rank quantizes an equal slice of
+    every module's rows, and the quantized rows and scales are all-gathered so
+    that every rank holds the whole quantized layer for the propagation pass.
+    Every rank issues the same collectives in the same order."""
+    import torch.distributed as dist
+
+    from .distributed import all_gather_rows, greedy_owners, row_range, solve_cost
+
+    dev = next(iter(cal.modules.values())).weight.device
+    ng = len(cal.groups)
+    # sample counts: one all-reduce for the layer
+    counts = torch.tensor([float(cal.hess[g].samples) for g in range(ng)], dtype=torch.float64, device=dev)
+    Hs = []
+    for g in range(ng):
+        H, _ = cal.hess[g].finalize()
+        Hs.append(H)
+    dist.all_reduce(counts)
+    keys = [f"g{g}" for g in range(ng)]
+    rows_total = {f"g{g}": sum(cal.modules[n].weight.shape[0] for n in cal.groups[g]) for g in range(ng)}
+    owners = greedy_owners({k: solve_cost(Hs[g].shape[0], rows_total[k]) for g, k in enumerate(keys)}, ws)
+    works = [dist.reduce(Hs[g], dst=owners[keys[g]], async_op=True) for g in range(ng)]
+    for w in works:
+        w.wait()
+    invs = []
+    for g in range(ng):
+        names = cal.groups[g]
+        qa0 = found[names[0]][1].weights
+        order = gptq.resolve_actorder(getattr(qa0, "actorder", None))
+        d = Hs[g].shape[0]
+        if owners[keys[g]] == rank:
+            inv = gptq.inverse_hessian(Hs[g] / counts[g].float(), modifier.dampening_frac, order)
+        else:
+            inv = gptq.InverseHessian(torch.empty(d, d, dtype=torch.float32, device=dev),
+                                      torch.empty(d, dtype=torch.uint8, device=dev),
+                                      torch.empty(1, dtype=torch.int32, device=dev), None,
+                                      torch.empty(d, dtype=torch.int32, device=dev) if order else None)
+        invs.append(inv)
+    works = []
+    for g in range(ng):
+        src = owners[keys[g]]
+        for t in (invs[g].hinv, invs[g].dead, invs[g].status) + ((invs[g].perm,) if invs[g].perm is not None else ()):
+            works.append(dist.broadcast(t, src=src, async_op=True))
+    for w in works:
+        w.wait()
+    for g in range(ng):
+        if invs[g].hinv_t is None:
+            invs[g].hinv_t = invs[g].hinv.t().contiguous()
+        names = cal.groups[g]
+        for nm in names:
+            mod = cal.modules[nm]
+            qa = found[nm][1].weights
+            order = gptq.resolve_actorder(getattr(qa, "actorder", None))
+            rows = mod.weight.shape[0]
+            align = int(qa.block_structure[0]) if getattr(qa.strategy, "value", qa.strategy) == "block" else 1
+            r0, r1 = row_range(rows, rank, ws, align)
+            g_idx = None
+            if order == "group":
+                wp = gptq.permute_columns(mod.weight, invs[g].perm)
+                scale, zp, gs = gptq.weight_qparams(mod, qa, weight=wp, stats_dtype=torch.float32)
+                g_idx = torch.empty(mod.weight.shape[1], dtype=torch.int32, device=dev)
+            else:
+                scale, zp, gs = gptq.weight_qparams(mod, qa)
+            srow = lambda t: t if t is None or t.numel() <= 1 else t[r0 // align:(r1 + align - 1) // align]  # noqa
+            wq_full = torch.empty_like(mod.weight)
+            if r1 > r0:
+                wq, loss = gptq.quantize_with_inverse(mod.weight[r0:r1], qa, invs[g], srow(scale), srow(zp),
+                                                      modifier.block_size, order, gs, g_idx)
+            else:
+                wq = mod.weight[r0:r0]
+                loss = torch.zeros(1, dtype=torch.float32, device=dev)
+            all_gather_rows(wq, wq_full, rows, align)
+            dist.all_reduce(loss)
+            q = {"weight": wq_full, "weight_scale": scale.to(mod.weight.dtype), "weight_zero_point": zp}
+            if gs is not None:
+                q["weight_global_scale"] = gs.to(mod.weight.dtype)
+            if g_idx is not None:
+                q["weight_g_idx"] = g_idx
+            _set_params(mod, q)
+            stats.losses[nm] = (loss, invs[g])
+        cal.hess[g] = None
+
+
 # ------------------------------------------------------------------ entry point
+class SequentialRunner:
+    """The layer-by-layer GPTQ pipeline behind ``oneshot`` with its steps
+    exposed: ``capture()`` runs the model up to the first layer for every
+    calibration batch, ``run_layer(i)`` calibrates, quantizes and propagates
+    decoder layer i, ``finish()`` reads the losses and errors back and marks
+    the modules frozen.  ``bench.py`` times ``run_layer`` steps."""
+
+    def __init__(self, model, modifiers, batches, device, sequential_targets=None, offload_layers=False):
+        self.model = model
+        self.device = device
+        self.offload = offload_layers
+        self.stats = OneshotStats()
+        from .distributed import world
+
+        self.rank, self.ws = world()
+        found_all = {}
+        for m in modifiers:
+            for k, v in m.resolve(model).items():
+                found_all.setdefault(k, (v[0], v[1], m))
+        self.found = {k: (v[0], v[1]) for k, v in found_all.items()}
+        self.gptq_found = {k: (v[0], v[1]) for k, v in found_all.items() if v[2].kind == "gptq"}
+        self.rtn_found = {k: (v[0], v[1]) for k, v in found_all.items() if v[2].kind == "rtn"}
+        gm = [m for m in modifiers if m.kind == "gptq"]
+        self.modifier = gm[0] if gm else None
+        _init_modules(self.found)
+        self.layers = sequential_layers(model, sequential_targets) if self.gptq_found else []
+        self.batches = batches
+        self.cache = None
+        self._host: dict[int, torch.Tensor] = {}
+        self._name_of = {id(m): n for n, (m, _) in self.gptq_found.items()}
+
+    def capture(self) -> None:
+        self.cache = _capture_layer_inputs(self.model, self.layers[0], self.batches)
+        self.stats.samples = sum(b["input_ids"].shape[0] for b in self.batches)
+        self.stats.tokens = sum(b["input_ids"].numel() for b in self.batches)
+
+    @torch.no_grad()
+    def run_layer(self, li: int, phases: list | None = None, propagate: bool | None = None) -> None:
+        """Calibrate, quantize and (unless it is the last layer) propagate
+        layer ``li``.  ``phases``: if a list, CUDA events marking the ends of
+        onload / calibration / solve / propagation / offload are appended."""
+        def mark(name):
+            if phases is not None:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                phases.append((name, e))
+
+        layer = self.layers[li]
+        mark("start")
+        if self.offload:
+            self._onload(layer)
+        mark("onload")
+        lm = {self._name_of[id(m)]: m for m in layer.modules() if id(m) in self._name_of}
+        if lm:
+            cal = _LayerCalibration(lm)
+            for (h, kw, rest) in self.cache:
+                layer(h, *rest, **kw)
+                cal.end_batch()
+            cal.remove()
+            mark("calibrate")
+            if self.ws > 1:
+                _solve_layer_dist(cal, self.gptq_found, self.modifier, self.stats, self.rank, self.ws)
+            else:
+                _solve_layer(cal, self.gptq_found, self.modifier, self.stats)
+            mark("solve")
+        mods = set(id(m) for m in layer.modules())
+        rl = {n: v for n, v in self.rtn_found.items() if id(v[0]) in mods}
+        if rl:
+            _rtn(rl)
+        if propagate if propagate is not None else li + 1 < len(self.layers):
+            # propagate: the quantized layer's outputs are the next layer's inputs
+            for i, (h, kw, rest) in enumerate(self.cache):
+                self.cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
+        mark("propagate")
+        if self.offload:
+            self._offload(layer)
+        mark("offload")
+
+    def _onload(self, layer: torch.nn.Module) -> None:
+        """Layer parameters to the device (from pinned host memory when the
+        host copies are pinned: asynchronous on the current stream)."""
+        for mod in layer.modules():
+            for k, p in list(mod._parameters.items()):
+                if p is not None and not p.is_cuda:
+                    host = p.data
+                    p.data = torch.empty_like(host, device=self.device)
+                    p.data.copy_(host, non_blocking=host.is_pinned())
+                    self._host[id(p)] = host
+            for k, b in list(mod._buffers.items()):
+                if b is not None and not b.is_cuda:
+                    mod._buffers[k] = b.to(self.device)
+
+    def _offload(self, layer: torch.nn.Module) -> None:
+        """Layer parameters back to the host (into their pinned host copies
+        when they have one, else new host tensors)."""
+        for mod in layer.modules():
+            for k, p in list(mod._parameters.items()):
+                if p is None or not p.is_cuda:
+                    continue
+                host = self._host.pop(id(p), None)
+                if host is not None and host.shape == p.shape and host.dtype == p.dtype:
+                    host.copy_(p.data, non_blocking=host.is_pinned())
+                    p.data = host
+                else:
+                    p.data = p.data.to("cpu")
+
+    def finish(self) -> OneshotStats:
+        in_layers = set(id(m) for l in self.layers for m in l.modules())
+        rest = {n: v for n, v in self.gptq_found.items() if id(v[0]) not in in_layers}
+        if rest:
+            raise NotImplementedError(f"GPTQ targets outside the sequential layers: {sorted(rest)[:4]}")
+        rtn_rest = {n: v for n, v in self.rtn_found.items() if id(v[0]) not in in_layers}
+        if rtn_rest:
+            for _, (mod, _) in rtn_rest.items():
+                if not mod.weight.is_cuda:
+                    mod.to(self.device)
+            _rtn(rtn_rest)
+        _check_losses(self.stats)
+        _lib.check_device_errors(self.device, "oneshot")
+        _finish_modules(self.found)
+        self.cache = None
+        return self.stats
+
+
 def oneshot(
     model: torch.nn.Module,
     dataset=None,
@@ -453,12 +666,14 @@ def oneshot(
     samples or an (n, L) tensor of token ids; the first
     ``num_calibration_samples`` are used in order (a DataLoader's own order;
     shuffling is the DataLoader's business, as in the reference when one is
-    passed).  ``device``: the GPU to calibrate on (default: the model's, or
-    the current CUDA device).  A model left on the CPU is moved there one
-    layer at a time and each quantized layer is moved back
-    (``offload_layers``, default: True when the model starts on the CPU).
-    Returns the model with quantized weights, compressed-tensors scales and
-    zero points, ready for ``save_compressed`` / ``ModelCompressor``.
+    passed).  Under ``torch.distributed`` every rank passes the same dataset
+    and calibrates its own contiguous share of the samples, as the
+    reference's DDP oneshot does with its per-rank data.  ``device``: the GPU
+    to calibrate on (default: the model's, or the current CUDA device).  A
+    model left on the CPU is moved there one layer at a time and each
+    quantized layer is moved back (``offload_layers``, default: True when the
+    model starts on the CPU).  Returns the model with quantized weights and
+    compressed-tensors scales and zero points, ready for ``save_compressed``.
     """
     mods = recipe if isinstance(recipe, (list, tuple)) else [recipe]
     mods = [m for m in mods if m is not None]
@@ -476,90 +691,51 @@ def oneshot(
     device = torch.device(device)
     if offload_layers is None:
         offload_layers = not first_param.is_cuda
-    stats = OneshotStats()
     t_all = time.perf_counter()
-
-    gptq_mods = [m for m in mods if m.kind == "gptq"]
-    rtn_mods = [m for m in mods if m.kind == "rtn"]
-    found_all = {}
-    for m in mods:
-        f = m.resolve(model)
-        for k, v in f.items():
-            found_all.setdefault(k, (v[0], v[1], m))
-    found = {k: (v[0], v[1]) for k, v in found_all.items()}
-    _init_modules(found)
-
-    rtn_found = {k: (v[0], v[1]) for k, v in found_all.items() if v[2].kind == "rtn"}
-    gptq_found = {k: (v[0], v[1]) for k, v in found_all.items() if v[2].kind == "gptq"}
-
-    if rtn_found and not gptq_found:
+    needs_data = any(m.kind == "gptq" for m in mods)
+    if not needs_data:
         # weight-only RTN: no calibration pass (the qparams do not depend on data)
-        for name, (mod, _) in rtn_found.items():
+        runner = SequentialRunner(model, mods, [], device)
+        for _, (mod, _) in runner.rtn_found.items():
             if not mod.weight.is_cuda:
                 mod.to(device)
-        _rtn(rtn_found)
-        _finish_modules(found)
-        torch.cuda.synchronize(device)
+        _rtn(runner.rtn_found)
+        stats = runner.finish()
         stats.seconds["total"] = time.perf_counter() - t_all
         globals()["LAST_STATS"] = stats
         return model
-
     if dataset is None:
         raise ValueError("GPTQ needs calibration data (dataset)")
-    modifier = gptq_mods[0]
+    from .distributed import row_range, world
+
+    rank, ws = world()
     layers = sequential_layers(model, sequential_targets)
-    layer_ids = {id(l) for l in layers}
-    # everything but the layers goes to the device; the layers follow one at a time
     if offload_layers:
-        _to_device_except(model, layer_ids, device)
+        _to_device_except(model, {id(l) for l in layers}, device)
     else:
         model.to(device)
-    batches = _calibration_batches(dataset, num_calibration_samples, calibration_batch_tokens, device)
-    stats.samples = sum(b["input_ids"].shape[0] for b in batches)
-    stats.tokens = sum(b["input_ids"].numel() for b in batches)
-
+    batches_all = _calibration_batches(dataset, num_calibration_samples, calibration_batch_tokens, "cpu")
+    if ws > 1:
+        # contiguous share of the samples per rank
+        samples = [(b["input_ids"][i], None if "attention_mask" not in b else b["attention_mask"][i])
+                   for b in batches_all for i in range(b["input_ids"].shape[0])]
+        s0, s1 = row_range(len(samples), rank, ws)
+        mine = [{"input_ids": s[0]} if s[1] is None else {"input_ids": s[0], "attention_mask": s[1]}
+                for s in samples[s0:s1]]
+        batches = _calibration_batches(mine, len(mine), calibration_batch_tokens, device)
+    else:
+        batches = [{k: v.to(device) for k, v in b.items()} for b in batches_all]
+    runner = SequentialRunner(model, mods, batches, device, sequential_targets, offload_layers)
     t0 = time.perf_counter()
-    if offload_layers:
-        layers[0].to(device)
-    cache = _capture_layer_inputs(model, layers[0], batches)
+    runner.capture()
     torch.cuda.synchronize(device)
-    stats.seconds["capture"] = time.perf_counter() - t0
-
-    name_of = {id(m): n for n, (m, _) in gptq_found.items()}
-    t_layers = time.perf_counter()
-    with torch.no_grad():
-        for li, layer in enumerate(layers):
-            if offload_layers:
-                layer.to(device)
-            lm = {name_of[id(m)]: m for m in layer.modules() if id(m) in name_of}
-            if lm:
-                cal = _LayerCalibration(lm)
-                for (h, kw, rest) in cache:
-                    layer(h, *rest, **kw)
-                    cal.end_batch()
-                cal.remove()
-                _solve_layer(cal, gptq_found, modifier, stats)
-            rl = {n: v for n, v in rtn_found.items() if any(v[0] is m for m in layer.modules())}
-            if rl:
-                _rtn(rl)
-            if li + 1 < len(layers):
-                # propagate: the quantized layer's outputs are the next layer's inputs
-                for i, (h, kw, rest) in enumerate(cache):
-                    cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
-            if offload_layers:
-                layer.to("cpu")
+    runner.stats.seconds["capture"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    for li in range(len(runner.layers)):
+        runner.run_layer(li)
     torch.cuda.synchronize(device)
-    stats.seconds["layers"] = time.perf_counter() - t_layers
-    # modules outside the layers (none for the usual targets with lm_head ignored)
-    rest = {n: v for n, v in gptq_found.items() if not any(v[0] is m for l in layers for m in l.modules())}
-    if rest:
-        raise NotImplementedError(f"GPTQ targets outside the sequential layers: {sorted(rest)[:4]}")
-    rtn_rest = {n: v for n, v in rtn_found.items() if not any(v[0] is m for l in layers for m in l.modules())}
-    if rtn_rest:
-        _rtn(rtn_rest)
-    _check_losses(stats)
-    _lib.check_device_errors(device, "oneshot")
-    _finish_modules(found)
+    runner.stats.seconds["layers"] = time.perf_counter() - t0
+    stats = runner.finish()
     if offload_layers:
         model.to("cpu")
     stats.seconds["total"] = time.perf_counter() - t_all
