@@ -77,6 +77,11 @@ const char* llmc_status_string(int status);
  * none).  No counterpart in the reference (its errors are Python
  * exceptions carrying torch's message). */
 const char* llmc_last_cuda_error(void);
+/* Status raised on the current device by kernels whose entry points take no
+ * status word (the streaming casts): LLMC_ETIMEOUT if a bounded wait ran out
+ * since the last clear, else LLMC_OK.  Synchronises the device (it reads a
+ * device variable); clear != 0 resets it.  No counterpart in the reference. */
+int llmc_device_status(int clear, int* status);
 
 /* ---------------------------------------------------------------- observers
  * Memoryless min-max statistics of a bf16 weight (rows x cols):
@@ -326,6 +331,8 @@ typedef struct {
   int32_t scale_is_f32;
   const float* global_scale;
   int32_t* g_idx_out;
+  float* row_loss_out;  /* optional (rows floats): each row's share of the loss, so callers that run several
+                           modules' rows in one call (modules sharing a Hessian) can report each module's loss */
 } LlmcGptqColumns;
 int llmc_gptq_actorder_perm(const float* H, int64_t d, int32_t* perm, void* stream);
 int llmc_gptq_permute_hessian(const float* H, int64_t d, const int32_t* perm, float* Hp, void* stream);

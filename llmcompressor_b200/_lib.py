@@ -83,6 +83,7 @@ _SIGS = {
     "llmc_kernel_launches": [],
     "llmc_status_string": [_I32],
     "llmc_last_cuda_error": [],
+    "llmc_device_status": [_I32, ctypes.POINTER(ctypes.c_int)],
     "llmc_observe_minmax": [_P, _I64, _I64, _QA, _P, _P, _P],
     "llmc_observe_mse_workspace_size": [_I64, _I64, _QA, _P],
     "llmc_modelfree_quantize_batch": [ctypes.POINTER(CastJob), _I32, _QA, _I32, _P],
@@ -179,6 +180,12 @@ def check_device_errors(device: torch.device | int | str | None = None, what: st
     if code != OK:
         w.zero_()
         raise_status(code, what or "device kernel")
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        v = ctypes.c_int(0)
+        check(lib().llmc_device_status(1, ctypes.byref(v)), "llmc_device_status")
+    if v.value != OK:
+        raise_status(v.value, what or "device kernel")
 
 
 def raise_status(code: int, what: str) -> None:

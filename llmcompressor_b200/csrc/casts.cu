@@ -13,6 +13,9 @@
 // Both run in three modes: FUSED (observe + qparams + quantize + pack),
 // STATS (min/max only) and GIVEN (quantize + pack with stored qparams).
 #include "llmc_common.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
 
 #include <cstdio>
 
@@ -20,6 +23,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
 
 namespace llmc {
 
@@ -591,11 +595,11 @@ __device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, floa
         }
       }
     } else if (FMT == LLMC_FMT_FP8) {
+      // no clamp to [-448, 448]: the saturating E4M3 conversion does it (and,
+      // like torch.clamp, keeps NaN a NaN, where a bf16x2 min/max would not)
 #pragma unroll
-      for (int j = 0; j < NW / 2; ++j) {
-        uint32_t a = hmin2(hmax2(Q[2 * j], QMIN2), QMAX2), b = hmin2(hmax2(Q[2 * j + 1], QMIN2), QMAX2);
-        o[j] = e4m3x2(bf_lo(a), bf_hi(a)) | (e4m3x2(bf_lo(b), bf_hi(b)) << 16);
-      }
+      for (int j = 0; j < NW / 2; ++j)
+        o[j] = e4m3x2(bf_lo(Q[2 * j]), bf_hi(Q[2 * j])) | (e4m3x2(bf_lo(Q[2 * j + 1]), bf_hi(Q[2 * j + 1])) << 16);
     } else {  // FP4 from a bf16 quotient (MXFP4)
 #pragma unroll
       for (int j = 0; j < NW / 4; ++j) {
@@ -1175,6 +1179,219 @@ __global__ void __launch_bounds__(256, 2) k_tile_batch(const __grid_constant__ C
 }
 
 // ------------------------------------------------------------------------
+// k_block_tma: 128 x 128 BLOCK groups (FP8_BLOCK and other block schemes of
+// that size) streamed through shared memory by the tensor-memory accelerator.
+// Persistent CTAs, three per SM; each keeps a ring of two 32 KB stages, one
+// whole block per stage, filled by one 2-D bulk tensor copy (out-of-range
+// rows and columns arrive as zeros, which is the reference's zero padding of
+// partial blocks).  The 256 threads read the block from shared memory twice
+// (consecutive 16-byte chunks across a warp: conflict-free): once for the
+// block's min/max, once to quantize and write the codes straight to global
+// memory.  Nothing of a block is held in registers, so three CTAs (24 warps)
+// fit an SM with six blocks in flight.  Jobs
+// (tensors) of a batch each have their own tensor map.  Every wait is
+// bounded; a timeout raises the library's device status word and the CTA
+// stops (llmc_device_status reads it).
+// ------------------------------------------------------------------------
+constexpr int TB_STAGES = 2;
+constexpr int TB_BYTES = 128 * 128 * 2;
+constexpr int TB_SMEM = TB_STAGES * TB_BYTES + 1024 + 64;
+constexpr int kTmaJobsMax = kBatchMax;  // maps in the kernel parameters: 6 KB (parameter space up to 32 KB)
+__device__ int g_async_status;  // LLMC_ETIMEOUT after a bounded wait ran out (llmc_device_status)
+
+struct TmaMaps {
+  CUtensorMap map[kTmaJobsMax];
+};
+
+template <int FMT, int BITS, int MODE>
+__global__ void __launch_bounds__(256, 3) k_block_tma(const __grid_constant__ CastBatch b,
+                                                      const __grid_constant__ TmaMaps m) {
+  using namespace sm100;
+  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+  extern __shared__ uint8_t tb_raw[];
+  uint8_t* ring = (uint8_t*)(((uintptr_t)tb_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(ring + TB_STAGES * TB_BYTES);
+  __shared__ float sh[32];
+  __shared__ int abort_flag;
+  const int t = threadIdx.x;
+  if (t == 0) {
+    for (int s = 0; s < TB_STAGES; ++s) mbar_init(smem_u32(&full[s]), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  int jl = 0;  // job cursor of the loads (units only increase)
+  auto issue = [&](int64_t u, int s) {
+    while (jl + 1 < b.njobs && b.job[jl + 1].first <= u) ++jl;
+    const CastParams p = job_params(b, jl);
+    const Rect R = group_rect(p, u - b.job[jl].first);
+    const uint32_t bar = smem_u32(&full[s]);
+    mbar_arrive_expect_tx(bar, TB_BYTES);
+    tma_load_2d(smem_u32(ring + s * TB_BYTES), &m.map[jl], (int32_t)R.c0, (int32_t)R.r0, bar);
+  };
+  const int64_t stride = gridDim.x;
+  if (t == 0) {
+    for (int s = 0; s < TB_STAGES; ++s) {
+      const int64_t u = blockIdx.x + s * stride;
+      if (u < b.units) issue(u, s);
+    }
+  }
+  int jp = 0;
+  int s = 0;
+  uint32_t phase = 0;
+  const float qmin = b.base.a.qmin(), qmax = b.base.a.qmax();
+  // this thread's chunks: c = j * 256 + t -> row j * 16 + t / 16, columns (t % 16) * 8 .. + 7
+  const int crow = t >> 4, ccol = (t & 15) * 8;
+  for (int64_t u = blockIdx.x; u < b.units; u += stride) {
+    if (t == 0 && !mbar_wait(smem_u32(&full[s]), phase, (volatile int*)&abort_flag)) {
+      atomicMax(&g_async_status, (int)LLMC_ETIMEOUT);
+    }
+    __syncthreads();  // the block has landed (or the wait gave up)
+    if (abort_flag) break;
+    const uint4* stage = (const uint4*)(ring + s * TB_BYTES) + t;
+    while (jp + 1 < b.njobs && b.job[jp + 1].first <= u) ++jp;
+    const CastParams p = job_params(b, jp);
+    const int64_t gi = u - b.job[jp].first;
+    const Rect R = group_rect(p, gi);
+    ElemQ e;
+    float s_store = 0.f, zp_store = 0.f;
+    if (MODE != MODE_GIVEN) {
+      uint32_t M = 0xFF80FF80u, mn2 = 0x7F807F80u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint4 v = stage[j * 256];
+        M = hmax2(hmax2(M, v.x), hmax2(v.y, hmax2(v.z, v.w)));
+        mn2 = hmin2(hmin2(mn2, v.x), hmin2(v.y, hmin2(v.z, v.w)));
+      }
+      float mx = fmaxf(bf_lo(M), bf_hi(M)), mn = fminf(bf_lo(mn2), bf_hi(mn2));
+      mn = block_reduce(mn, false, sh);
+      mx = block_reduce(mx, true, sh);
+      if (MODE == MODE_STATS) {
+        if (t == 0) { p.min_out[gi] = f_to_bf16(mn); p.max_out[gi] = f_to_bf16(mx); }
+      } else {
+        e = make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
+        if (t == 0) store_scale<FMT>(p, gi, s_store, zp_store);
+      }
+    } else {
+      e = make_elemq_given<FMT>(p, gi);
+    }
+    if (MODE != MODE_STATS) {
+      const GQ g = to_gq(e);
+      const int64_t h = R.r1 - R.r0, wd = R.c1 - R.c0;
+      const bool full_block = h == 128 && wd == 128;
+      uint8_t* out0 = (uint8_t*)p.out;
+      const int64_t el0 = (R.r0 + crow) * p.cols + R.c0 + ccol;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (!full_block && (j * 16 + crow >= h || ccol >= wd)) continue;
+        const uint4 v = stage[j * 256];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[2];
+        if (MODE == MODE_GIVEN && g.f32q) quant_group<FMT, BITS, true, true, 4>(w, g, qmin, qmax, o);
+        else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, 4>(w, g, qmin, qmax, o);
+        const int64_t el = el0 + (int64_t)j * 16 * p.cols;
+        if (OUT4) *(uint32_t*)(out0 + el / 2) = o[0];
+        else *(uint2*)(out0 + el) = make_uint2(o[0], o[1]);
+      }
+    }
+    __syncthreads();  // every thread is done with the stage: refill it
+    if (t == 0) {
+      fence_proxy_async_smem();
+      const int64_t nu = u + TB_STAGES * stride;
+      if (nu < b.units) issue(nu, s);
+    }
+    if (++s == TB_STAGES) { s = 0; phase ^= 1; }
+  }
+  if (abort_flag && t == 0) {
+    // let the copies issued before the stop land before the CTA exits
+    volatile int dummy = 0;
+    for (int k = 0; k < TB_STAGES; ++k) {
+      mbar_wait(smem_u32(&full[s]), phase, &dummy, 100000000ull);
+      if (++s == TB_STAGES) { s = 0; phase ^= 1; }
+    }
+  }
+}
+
+static int n_groups(const CastParams& p);
+
+static PFN_cuTensorMapEncodeTiled_v12000 tb_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  });
+  return fn;
+}
+
+// Whether the TMA block kernel takes these jobs: 128 x 128 blocks, 16-byte
+// aligned rows and bases, outputs aligned for their vector stores.
+static bool tma_block_ok(const CastParams& p) {
+  const QArgs& a = p.a;
+  const bool out4 = p.fmt == LLMC_FMT_NVFP4 || p.fmt == LLMC_FMT_MXFP4 || (p.fmt == LLMC_FMT_PACK_INT32 && a.bits == 4);
+  return a.strategy == LLMC_STRAT_BLOCK && a.bh == 128 && a.bw == 128 && p.cols % 16 == 0 &&
+         (uintptr_t)p.w % 16 == 0 && (p.mode == MODE_STATS || (uintptr_t)p.out % (out4 ? 4 : 8) == 0) &&
+         p.rows < (1ll << 31) && p.cols < (1ll << 31) && tb_encoder() != nullptr;
+}
+
+template <int FMT, int BITS, int MODE>
+static bool launch_block_tma(CastBatch& b, cudaStream_t st) {
+  if (b.njobs > kTmaJobsMax) return false;
+  TmaMaps m;
+  memset(&m, 0, sizeof(m));
+  int64_t units = 0;
+  for (int i = 0; i < b.njobs; ++i) {
+    CastJob& j = b.job[i];
+    j.first = units;
+    CastParams p = b.base;
+    p.rows = j.rows; p.cols = j.cols;
+    units += n_groups(p);
+    cuuint64_t dims[2] = {(cuuint64_t)j.cols, (cuuint64_t)j.rows};
+    cuuint64_t strides[1] = {(cuuint64_t)j.cols * 2};
+    cuuint32_t box[2] = {128, 128};
+    cuuint32_t estr[2] = {1, 1};
+    if (tb_encoder()(&m.map[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(j.w), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  b.units = units;
+  if (units == 0) return true;
+  static std::mutex mu;
+  static uint64_t done = 0;
+  {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (dev < 64 && !((done >> dev) & 1ull)) {
+      if (cudaFuncSetAttribute(k_block_tma<FMT, BITS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, TB_SMEM) !=
+          cudaSuccess)
+        return false;
+      done |= 1ull << dev;
+    }
+  }
+  const unsigned grid = (unsigned)std::min<int64_t>(units, 148 * 3);
+  k_block_tma<FMT, BITS, MODE><<<grid, 256, TB_SMEM, st>>>(b, m);
+  llmc::note_launch();
+  return cudaGetLastError() == cudaSuccess;
+}
+
+template <int FMT, int BITS, int MODE>
+static bool launch_block_tma_one(const CastParams& p, cudaStream_t st) {
+  CastBatch b;
+  memset(&b, 0, sizeof(b));
+  b.base = p;
+  b.njobs = 1;
+  CastJob& j = b.job[0];
+  j.w = p.w; j.rows = p.rows; j.cols = p.cols; j.gs = p.gs;
+  j.out = p.out; j.scale_out = p.scale_out; j.zp_out = p.zp_out;
+  return launch_block_tma<FMT, BITS, MODE>(b, st);
+}
+
+// ------------------------------------------------------------------------
 // small kernels
 // ------------------------------------------------------------------------
 __global__ void k_absmax(const uint16_t* w, int64_t n, float* out) {
@@ -1404,6 +1621,13 @@ static bool launch_fast(const CastParams& p, cudaStream_t st) {
       if (a.bw % 16) return false;
       pieces = std::min<int64_t>(a.bh, p.rows) * (std::min<int64_t>(a.bw, p.cols) / 16);
     }
+    if constexpr (FMT != LLMC_FMT_NVFP4 && FMT != LLMC_FMT_MXFP4) {
+      if (tma_block_ok(p)) {
+        if (p.mode == MODE_STATS) return launch_block_tma_one<LLMC_FMT_INT8, 8, MODE_STATS>(p, st);
+        if (p.mode == MODE_FUSED) return launch_block_tma_one<FMT, BITS, MODE_FUSED>(p, st);
+        return launch_block_tma_one<FMT, BITS, MODE_GIVEN>(p, st);
+      }
+    }
     if (p.mode == MODE_STATS) return launch_tile<LLMC_FMT_INT8, 8, MODE_STATS>(p, pieces, st);
     if ((uintptr_t)p.out % 16) return false;
     if (p.mode == MODE_FUSED) return launch_tile<FMT, BITS, MODE_FUSED>(p, pieces, st);
@@ -1495,6 +1719,17 @@ static bool launch_batch_fmt(CastBatch& b, cudaStream_t st) {
     return false;
   } else {
     if (a.strategy != LLMC_STRAT_CHANNEL && a.strategy != LLMC_STRAT_BLOCK) return false;
+    if (a.strategy == LLMC_STRAT_BLOCK && b.njobs <= kTmaJobsMax) {
+      bool all = true;
+      for (int i = 0; i < b.njobs && all; ++i) {
+        CastParams p = b.base;  // the job's parameters, built on the host
+        const CastJob& jb = b.job[i];
+        p.w = jb.w; p.rows = jb.rows; p.cols = jb.cols; p.gs = jb.gs;
+        p.out = jb.out; p.scale_out = jb.scale_out; p.zp_out = jb.zp_out;
+        all = tma_block_ok(p);
+      }
+      if (all) return launch_block_tma<FMT, BITS, MODE_FUSED>(b, st);
+    }
     const unsigned g = (unsigned)std::min<int64_t>(units, 148 * 2);
     const unsigned g128 = (unsigned)std::min<int64_t>(units, 148 * 16);
     if (pieces <= 256) k_tile_batch<FMT, BITS, 1><<<g, 256, 0, st>>>(b);
@@ -1567,6 +1802,20 @@ extern "C" {
 int llmc_version(void) { return 100; }
 
 const char* llmc_last_cuda_error(void) { return llmc::g_last_error; }
+
+int llmc_device_status(int clear, int* status) {
+  if (!status) return LLMC_EINVAL_ARG;
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, llmc::g_async_status, sizeof(int));
+  if (e != cudaSuccess) return llmc::cuda_fail("llmc_device_status: cudaMemcpyFromSymbol", e);
+  if (clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(llmc::g_async_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return llmc::cuda_fail("llmc_device_status: cudaMemcpyToSymbol", e);
+  }
+  *status = v;
+  return LLMC_OK;
+}
 
 int64_t llmc_kernel_launches(void) { return (int64_t)g_launches.load(std::memory_order_relaxed); }
 

@@ -1215,6 +1215,9 @@ int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const 
   else k_finish<<<grid_for(rows * cols), 256, 0, st>>>(W, (uint16_t*)wq_bf16, rows * cols);
   llmc::note_launch();
   k_sum<<<1, 1024, 0, st>>>(L, rows, loss_out); llmc::note_launch();
+  if (x.row_loss_out &&
+      cudaMemcpyAsync(x.row_loss_out, L, sizeof(float) * rows, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+    return LLMC_ECUDA;
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 

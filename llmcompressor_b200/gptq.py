@@ -223,6 +223,7 @@ class GptqColumns(ctypes.Structure):
         ("scale_is_f32", ctypes.c_int32),
         ("global_scale", ctypes.c_void_p),
         ("g_idx_out", ctypes.c_void_p),
+        ("row_loss_out", ctypes.c_void_p),
     ]
 
 
@@ -397,14 +398,16 @@ def weight_qparams(module: torch.nn.Module, quant_args, weight: torch.Tensor | N
 def quantize_with_inverse(weight: torch.Tensor, quant_args, hinv: InverseHessian, scale: torch.Tensor,
                           zero_point: torch.Tensor | None, blocksize: int = 128, actorder=None,
                           global_scale: torch.Tensor | None = None,
-                          g_idx_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+                          g_idx_out: torch.Tensor | None = None,
+                          row_loss_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """GPTQ block loop for one bf16 weight with a prepared inverse factor.
     Returns (fake-quantized bf16 weight, loss as a float32 device scalar).
 
     ``actorder`` must match the ordering ``hinv`` was built with; with GROUP
     ordering ``scale`` holds the groups of the permuted weight (float32) and
     ``g_idx_out`` (int32, cols) receives each column's group.  ``global_scale``:
-    TENSOR_GROUP; ``scale`` is then float32."""
+    TENSOR_GROUP; ``scale`` is then float32.  ``row_loss_out`` (float32,
+    rows): each row's share of the loss."""
     require_cuda(weight, scale)
     if weight.dtype != torch.bfloat16:
         raise NotImplementedError(f"weights of dtype {weight.dtype}: the GPTQ kernels take bf16 weights")
@@ -425,7 +428,11 @@ def quantize_with_inverse(weight: torch.Tensor, quant_args, hinv: InverseHessian
     scale_f32 = scale.dtype == torch.float32
     sc = scale.contiguous() if scale_f32 else scale.to(torch.bfloat16).contiguous()
     gsc = global_scale.to(torch.float32).contiguous() if global_scale is not None else None
-    cx = GptqColumns(ptr(hinv.perm), _ORDER_CODE[order], int(scale_f32), ptr(gsc), ptr(g_idx_out))
+    if row_loss_out is not None and (row_loss_out.dtype != torch.float32 or row_loss_out.numel() != rows
+                                     or not row_loss_out.is_contiguous()):
+        raise ValueError("row_loss_out must be a contiguous float32 tensor of one value per row")
+    cx = GptqColumns(ptr(hinv.perm), _ORDER_CODE[order], int(scale_f32), ptr(gsc), ptr(g_idx_out),
+                     ptr(row_loss_out))
     ws = torch.empty(_ws_bytes(lib().llmc_gptq_quantize_workspace_size, rows, cols), dtype=torch.uint8, device=dev)
     out = torch.empty_like(w)
     loss = torch.empty(1, dtype=torch.float32, device=dev)
@@ -483,6 +490,8 @@ def quantize_modules_shared(
     if len({bool(o) for o in orders}) > 1:
         raise ValueError("modules sharing a Hessian must agree on whether activation ordering is used")
     hinv = inverse_hessian(hessian, percdamp, orders[0] if orders else None)
+    if len(modules) > 1 and _stackable(modules, args_list, orders):
+        return hinv, _quantize_stacked(modules, args_list[0], orders[0], hinv, blocksize)
     results = []
     for module, qa, order in zip(modules, args_list, orders):
         final_dtype = module.weight.dtype
@@ -507,6 +516,44 @@ def quantize_modules_shared(
             q_param_dict["weight_g_idx"] = g_idx
         results.append((loss, q_param_dict))
     return hinv, results
+
+
+def _stackable(modules, args_list, orders) -> bool:
+    """Modules whose rows can go through one block-loop call: the same
+    per-row-scaled scheme (GROUP or CHANNEL, bf16 weights of one width) and
+    the same ordering -- GPTQ rows are independent given the factor, so
+    stacking them changes nothing but the number of launches."""
+    qa0 = args_list[0]
+    if _strategy(qa0) not in ("group", "channel") or orders[0] == "group":
+        return False
+    cols = modules[0].weight.shape[1]
+    for m, qa in zip(modules, args_list):
+        if m.weight.dtype != torch.bfloat16 or m.weight.shape[1] != cols or qa != qa0:
+            return False
+        if getattr(m, "weight_observer", None) is not None and "mse" in type(m.weight_observer).__name__.lower():
+            return False
+    return True
+
+
+def _quantize_stacked(modules, qa, order, hinv, blocksize) -> list[tuple[torch.Tensor, dict]]:
+    """One block-loop call over the stacked rows of several modules; each
+    module gets its rows back, its own scales and its own loss (the sum of
+    its rows' losses)."""
+    qp = [weight_qparams(m, qa) for m in modules]
+    w = torch.cat([m.weight.detach() for m in modules])
+    scale = torch.cat([q[0] for q in qp])
+    zp = torch.cat([q[1] for q in qp]) if qp[0][1] is not None else None
+    row_loss = torch.empty(w.shape[0], dtype=torch.float32, device=w.device)
+    wq, _ = quantize_with_inverse(w, qa, hinv, scale, zp, blocksize, order, None, None, row_loss)
+    zp_dtype = getattr(qa, "zp_dtype", None) or torch.int8
+    out, r0 = [], 0
+    for m, (sc, z, _) in zip(modules, qp):
+        r1 = r0 + m.weight.shape[0]
+        q = {"weight": wq[r0:r1].to(m.weight.dtype), "weight_scale": sc.to(dtype=m.weight.dtype),
+             "weight_zero_point": z.to(dtype=zp_dtype)}
+        out.append((row_loss[r0:r1].sum().reshape(1), q))
+        r0 = r1
+    return out
 
 
 def quantize_weight(

@@ -334,43 +334,58 @@ def _rtn(found: dict) -> None:
 
 # ------------------------------------------------------------------ GPTQ per layer
 class _LayerCalibration:
-    """Forward hooks on one layer's quantized modules: modules that read the
-    same tensor in a forward pass share one Hessian (``BatchedHessian``)."""
+    """Forward pre-hooks on one layer's quantized modules: modules that read
+    the same tensor in a forward pass share one Hessian (``BatchedHessian``).
+
+    The calibration pass only needs the modules' inputs; its layer output is
+    discarded (the propagation pass recomputes it with the quantized
+    weights).  So after the first batch, which runs whole and fixes the order
+    in which the modules are called, the pass stops at the input of the last
+    module called (for a Llama layer: before the down projection's GEMM)."""
 
     def __init__(self, modules: dict[str, torch.nn.Module]):
         self.modules = modules  # name -> module
         self.group_of: dict[str, int] = {}
         self.groups: list[list[str]] = []
         self.hess: list[gptq.BatchedHessian] = []
-        self._seen: dict[tuple, int] = {}
+        self.order: list[str] = []
+        self._seen: dict[int, tuple] = {}
         self._handles = []
         self._first = True
         for name, mod in modules.items():
-            self._handles.append(mod.register_forward_hook(self._hook(name)))
+            self._handles.append(mod.register_forward_pre_hook(self._hook(name)))
 
     def _hook(self, name):
-        def hook(mod, args, out):
+        def hook(mod, args):
             x = args[0]
-            key = id(x)
             if self._first:
                 # the first batch decides the groups; the inputs are held until
                 # it ends, so no id is reused by another tensor meanwhile
-                g = self._seen.get(key, (None,))[0]
+                g = self._seen.get(id(x), (None,))[0]
                 if g is None:
                     g = len(self.groups)
-                    self._seen[key] = (g, x)
+                    self._seen[id(x)] = (g, x)
                     self.groups.append([])
                     self.hess.append(gptq.BatchedHessian(x.shape[-1], x.device))
                     self.hess[g].add(x)
                 self.groups[g].append(name)
                 self.group_of[name] = g
-            else:
-                g = self.group_of[name]
-                if self.groups[g][0] == name:
-                    self.hess[g].add(x)
+                self.order.append(name)
+                return None
+            g = self.group_of[name]
+            if self.groups[g][0] == name:
+                self.hess[g].add(x)
+            if name == self.order[-1]:
+                raise _Stop
+            return None
         return hook
 
-    def end_batch(self):
+    def run(self, layer, h, rest, kw) -> None:
+        """One calibration batch through the layer."""
+        try:
+            layer(h, *rest, **kw)
+        except _Stop:
+            pass
         self._first = False
         self._seen.clear()
 
@@ -440,85 +455,126 @@ def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifie
     restructured): every shared Hessian is summed onto an owner rank chosen by
     solve cost, the owner factors it and broadcasts the upper factor (each
     rank forms its transpose locally), every rank quantizes an equal slice of
-    every module's rows, and the quantized rows and scales are all-gathered so
+    the group's (stacked) rows, and the quantized rows are all-gathered so
     that every rank holds the whole quantized layer for the propagation pass.
-    Every rank issues the same collectives in the same order."""
+
+    Groups go smallest Hessian first, each on its own stream: the owners'
+    factorisations run concurrently, and the collectives are issued group by
+    group (broadcast, then the row gathers) so that the small groups' row
+    solves and gathers proceed while the largest factorisation is still
+    running.  Every rank issues the same collectives in the same order."""
     import torch.distributed as dist
 
-    from .distributed import all_gather_rows, greedy_owners, row_range, solve_cost
+    from .distributed import greedy_owners, solve_cost
+    from .pipeline import _side_streams
 
     dev = next(iter(cal.modules.values())).weight.device
+    main = torch.cuda.current_stream(dev)
     ng = len(cal.groups)
-    # sample counts: one all-reduce for the layer
     counts = torch.tensor([float(cal.hess[g].samples) for g in range(ng)], dtype=torch.float64, device=dev)
-    Hs = []
-    for g in range(ng):
-        H, _ = cal.hess[g].finalize()
-        Hs.append(H)
+    Hs = [cal.hess[g].finalize()[0] for g in range(ng)]
     dist.all_reduce(counts)
     keys = [f"g{g}" for g in range(ng)]
     rows_total = {f"g{g}": sum(cal.modules[n].weight.shape[0] for n in cal.groups[g]) for g in range(ng)}
     owners = greedy_owners({k: solve_cost(Hs[g].shape[0], rows_total[k]) for g, k in enumerate(keys)}, ws)
-    works = [dist.reduce(Hs[g], dst=owners[keys[g]], async_op=True) for g in range(ng)]
-    for w in works:
-        w.wait()
-    invs = []
-    for g in range(ng):
+    order = sorted(range(ng), key=lambda g: (Hs[g].shape[0], g))  # smallest Hessian first
+    streams = _side_streams(dev, ng)
+    red = {g: dist.reduce(Hs[g], dst=owners[keys[g]], async_op=True) for g in order}
+    invs = {}
+    for i, g in enumerate(order):
+        st = streams[ng - 1 - i]  # the largest Hessian (the critical path) gets the high-priority stream
+        st.wait_stream(main)
         names = cal.groups[g]
         qa0 = found[names[0]][1].weights
-        order = gptq.resolve_actorder(getattr(qa0, "actorder", None))
+        act = gptq.resolve_actorder(getattr(qa0, "actorder", None))
         d = Hs[g].shape[0]
-        if owners[keys[g]] == rank:
-            inv = gptq.inverse_hessian(Hs[g] / counts[g].float(), modifier.dampening_frac, order)
-        else:
-            inv = gptq.InverseHessian(torch.empty(d, d, dtype=torch.float32, device=dev),
-                                      torch.empty(d, dtype=torch.uint8, device=dev),
-                                      torch.empty(1, dtype=torch.int32, device=dev), None,
-                                      torch.empty(d, dtype=torch.int32, device=dev) if order else None)
-        invs.append(inv)
-    works = []
-    for g in range(ng):
-        src = owners[keys[g]]
-        for t in (invs[g].hinv, invs[g].dead, invs[g].status) + ((invs[g].perm,) if invs[g].perm is not None else ()):
-            works.append(dist.broadcast(t, src=src, async_op=True))
-    for w in works:
-        w.wait()
-    for g in range(ng):
-        if invs[g].hinv_t is None:
-            invs[g].hinv_t = invs[g].hinv.t().contiguous()
-        names = cal.groups[g]
-        for nm in names:
-            mod = cal.modules[nm]
-            qa = found[nm][1].weights
-            order = gptq.resolve_actorder(getattr(qa, "actorder", None))
-            rows = mod.weight.shape[0]
-            align = int(qa.block_structure[0]) if getattr(qa.strategy, "value", qa.strategy) == "block" else 1
-            r0, r1 = row_range(rows, rank, ws, align)
-            g_idx = None
-            if order == "group":
-                wp = gptq.permute_columns(mod.weight, invs[g].perm)
-                scale, zp, gs = gptq.weight_qparams(mod, qa, weight=wp, stats_dtype=torch.float32)
-                g_idx = torch.empty(mod.weight.shape[1], dtype=torch.int32, device=dev)
+        with torch.cuda.stream(st):
+            red[g].wait()
+            if owners[keys[g]] == rank:
+                inv = gptq.inverse_hessian(Hs[g] / counts[g].float(), modifier.dampening_frac, act)
             else:
-                scale, zp, gs = gptq.weight_qparams(mod, qa)
-            srow = lambda t: t if t is None or t.numel() <= 1 else t[r0 // align:(r1 + align - 1) // align]  # noqa
-            wq_full = torch.empty_like(mod.weight)
-            if r1 > r0:
-                wq, loss = gptq.quantize_with_inverse(mod.weight[r0:r1], qa, invs[g], srow(scale), srow(zp),
-                                                      modifier.block_size, order, gs, g_idx)
-            else:
-                wq = mod.weight[r0:r0]
-                loss = torch.zeros(1, dtype=torch.float32, device=dev)
-            all_gather_rows(wq, wq_full, rows, align)
-            dist.all_reduce(loss)
-            q = {"weight": wq_full, "weight_scale": scale.to(mod.weight.dtype), "weight_zero_point": zp}
-            if gs is not None:
-                q["weight_global_scale"] = gs.to(mod.weight.dtype)
-            if g_idx is not None:
-                q["weight_g_idx"] = g_idx
-            _set_params(mod, q)
-            stats.losses[nm] = (loss, invs[g])
+                inv = gptq.InverseHessian(torch.empty(d, d, dtype=torch.float32, device=dev),
+                                          torch.empty(d, dtype=torch.uint8, device=dev),
+                                          torch.empty(1, dtype=torch.int32, device=dev), None,
+                                          torch.empty(d, dtype=torch.int32, device=dev) if act else None)
+            ts = (inv.hinv, inv.dead, inv.status) + ((inv.perm,) if inv.perm is not None else ())
+            for w in [dist.broadcast(t, src=owners[keys[g]], async_op=True) for t in ts]:
+                w.wait()
+            if inv.hinv_t is None:
+                inv.hinv_t = inv.hinv.t().contiguous()
+            invs[g] = inv
+            _solve_group_rows(cal, g, found, modifier, stats, inv, rank, ws, dev)
         cal.hess[g] = None
+    for st in streams[:ng]:
+        main.wait_stream(st)
+
+
+def _solve_group_rows(cal, g, found, modifier, stats, inv, rank, ws, dev) -> None:
+    """Quantize this rank's share of group ``g``'s rows against the shared
+    factor and all-gather the quantized rows (on the current stream)."""
+    names = cal.groups[g]
+    mods = [cal.modules[nm] for nm in names]
+    qas = [found[nm][1].weights for nm in names]
+    orders = [gptq.resolve_actorder(getattr(qa, "actorder", None)) for qa in qas]
+    if len(mods) > 1 and gptq._stackable(mods, qas, orders):
+        # one row split over the stacked rows of the group's modules
+        qp = [gptq.weight_qparams(m, qas[0]) for m in mods]
+        w = torch.cat([m.weight.detach() for m in mods])
+        scale = torch.cat([q[0] for q in qp])
+        zp = torch.cat([q[1] for q in qp])
+        wq_full, row_loss = _solve_rows_dist(w, qas[0], inv, scale, zp, None, None, orders[0], 1,
+                                             modifier.block_size, rank, ws, dev)
+        r0 = 0
+        for nm, mod, (sc, z, _) in zip(names, mods, qp):
+            r1 = r0 + mod.weight.shape[0]
+            _set_params(mod, {"weight": wq_full[r0:r1], "weight_scale": sc.to(mod.weight.dtype),
+                              "weight_zero_point": z})
+            stats.losses[nm] = (row_loss[r0:r1].sum().reshape(1), inv)
+            r0 = r1
+        return
+    for nm, mod, qa, order in zip(names, mods, qas, orders):
+        align = int(qa.block_structure[0]) if getattr(qa.strategy, "value", qa.strategy) == "block" else 1
+        g_idx = None
+        if order == "group":
+            wp = gptq.permute_columns(mod.weight, inv.perm)
+            scale, zp, gs = gptq.weight_qparams(mod, qa, weight=wp, stats_dtype=torch.float32)
+            g_idx = torch.empty(mod.weight.shape[1], dtype=torch.int32, device=dev)
+        else:
+            scale, zp, gs = gptq.weight_qparams(mod, qa)
+        wq_full, row_loss = _solve_rows_dist(mod.weight.detach(), qa, inv, scale, zp, gs, g_idx, order, align,
+                                             modifier.block_size, rank, ws, dev)
+        q = {"weight": wq_full, "weight_scale": scale.to(mod.weight.dtype), "weight_zero_point": zp}
+        if gs is not None:
+            q["weight_global_scale"] = gs.to(mod.weight.dtype)
+        if g_idx is not None:
+            q["weight_g_idx"] = g_idx
+        _set_params(mod, q)
+        stats.losses[nm] = (row_loss.sum().reshape(1), inv)
+
+
+def _solve_rows_dist(w, qa, inv, scale, zp, gs, g_idx, order, align, blocksize, rank, ws, dev):
+    """This rank's slice of the rows of ``w`` through the block loop, then
+    every rank's rows and per-row losses all-gathered."""
+    from .distributed import all_gather_rows, row_range
+
+    rows = w.shape[0]
+    r0, r1 = row_range(rows, rank, ws, align)
+
+    def srow(t):
+        return t if t is None or t.numel() <= 1 else t[r0 // align:(r1 + align - 1) // align]
+
+    wq_full = torch.empty_like(w)
+    row_loss_full = torch.empty(rows, dtype=torch.float32, device=dev)
+    if r1 > r0:
+        rl = torch.empty(r1 - r0, dtype=torch.float32, device=dev)
+        wq, _ = gptq.quantize_with_inverse(w[r0:r1], qa, inv, srow(scale), srow(zp), blocksize, order, gs, g_idx,
+                                           rl)
+    else:
+        wq = w[r0:r0]
+        rl = torch.empty(0, dtype=torch.float32, device=dev)
+    all_gather_rows(wq, wq_full, rows, align)
+    all_gather_rows(rl, row_loss_full, rows, align)
+    return wq_full, row_loss_full
 
 
 # ------------------------------------------------------------------ entry point
@@ -578,8 +634,7 @@ class SequentialRunner:
         if lm:
             cal = _LayerCalibration(lm)
             for (h, kw, rest) in self.cache:
-                layer(h, *rest, **kw)
-                cal.end_batch()
+                cal.run(layer, h, rest, kw)
             cal.remove()
             mark("calibrate")
             if self.ws > 1:
