@@ -165,7 +165,7 @@ class BatchedHessian:
         self.device = torch.device(device)
         self.H = H if H is not None else torch.zeros(self.d, self.d, dtype=GPTQ_PRECISION, device=self.device)
         self.chunk = int(chunk_tokens)
-        self._buf = torch.empty(self.chunk, self.d, dtype=torch.bfloat16, device=self.device)
+        self._buf = None  # allocated when a call shorter than the chunk arrives
         self._fill = 0
         self.samples = 0
 
@@ -184,6 +184,8 @@ class BatchedHessian:
                 pos += take
                 continue
             take = min(self.chunk - self._fill, n - pos)
+            if self._buf is None:
+                self._buf = torch.empty(self.chunk, self.d, dtype=torch.bfloat16, device=self.device)
             self._buf[self._fill:self._fill + take].copy_(x[pos:pos + take])
             self._fill += take
             pos += take

@@ -44,7 +44,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from . import _lib, gptq, ops
+from . import _lib, gptq, moe, ops
 
 __all__ = ["oneshot", "GPTQModifier", "QuantizationModifier", "OneshotStats"]
 
@@ -404,7 +404,7 @@ def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, st
     dev = next(iter(cal.modules.values())).weight.device
     main = torch.cuda.current_stream(dev)
     order = sorted(range(len(cal.groups)), key=lambda g: -cal.hess[g].d)
-    streams = _side_streams(dev, max(1, len(order)))
+    streams = _side_streams(dev, max(1, min(MAX_SIDE_STREAMS, len(order))))
     done = []
     results = []
     for i, g in enumerate(order):
@@ -414,7 +414,8 @@ def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, st
             bh = cal.hess[g]
             H, n = bh.finalize()
             for t in (bh.H, bh._buf):  # allocated on the caller's stream, read on this one
-                t.record_stream(st)
+                if t is not None:
+                    t.record_stream(st)
             H = H / n  # the reference's hessian / num_samples (S/modifiers/gptq/base.py:594)
             names = cal.groups[g]
             mods = [cal.modules[nm] for nm in names]
@@ -431,6 +432,9 @@ def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, st
         main.wait_event(ev)
     for nm, loss, hinv in results:
         stats.losses[nm] = (loss, hinv)
+
+
+MAX_SIDE_STREAMS = 8  # concurrent solve streams (an MoE layer has one Hessian group per expert)
 
 
 def _check_losses(stats: OneshotStats) -> None:
@@ -478,11 +482,12 @@ def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifie
     rows_total = {f"g{g}": sum(cal.modules[n].weight.shape[0] for n in cal.groups[g]) for g in range(ng)}
     owners = greedy_owners({k: solve_cost(Hs[g].shape[0], rows_total[k]) for g, k in enumerate(keys)}, ws)
     order = sorted(range(ng), key=lambda g: (Hs[g].shape[0], g))  # smallest Hessian first
-    streams = _side_streams(dev, ng)
+    nst = max(1, min(MAX_SIDE_STREAMS, ng))
+    streams = _side_streams(dev, nst)
     red = {g: dist.reduce(Hs[g], dst=owners[keys[g]], async_op=True) for g in order}
     invs = {}
     for i, g in enumerate(order):
-        st = streams[ng - 1 - i]  # the largest Hessian (the critical path) gets the high-priority stream
+        st = streams[(ng - 1 - i) % nst]  # the largest Hessian (the critical path) gets the high-priority stream
         st.wait_stream(main)
         names = cal.groups[g]
         qa0 = found[names[0]][1].weights
@@ -505,7 +510,7 @@ def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifie
             invs[g] = inv
             _solve_group_rows(cal, g, found, modifier, stats, inv, rank, ws, dev)
         cal.hess[g] = None
-    for st in streams[:ng]:
+    for st in streams[:nst]:
         main.wait_stream(st)
 
 
@@ -585,11 +590,19 @@ class SequentialRunner:
     decoder layer i, ``finish()`` reads the losses and errors back and marks
     the modules frozen.  ``bench.py`` times ``run_layer`` steps."""
 
-    def __init__(self, model, modifiers, batches, device, sequential_targets=None, offload_layers=False):
+    def __init__(self, model, modifiers, batches, device, sequential_targets=None, offload_layers=False,
+                 moe_calibrate_all_experts: bool = True):
         self.model = model
         self.device = device
         self.offload = offload_layers
+        self.all_experts = moe_calibrate_all_experts
         self.stats = OneshotStats()
+        if moe.linearize_experts(model):
+            # fused experts become per-expert Linear modules (the reference's
+            # post-load linearize_moe) before the modules are matched
+            from loguru import logger
+
+            logger.info("MoE experts linearized into per-expert Linear modules for calibration")
         from .distributed import world
 
         self.rank, self.ws = world()
@@ -633,8 +646,9 @@ class SequentialRunner:
         lm = {self._name_of[id(m)]: m for m in layer.modules() if id(m) in self._name_of}
         if lm:
             cal = _LayerCalibration(lm)
-            for (h, kw, rest) in self.cache:
-                cal.run(layer, h, rest, kw)
+            with moe.calibrate_all_experts(self.all_experts):
+                for (h, kw, rest) in self.cache:
+                    cal.run(layer, h, rest, kw)
             cal.remove()
             mark("calibrate")
             if self.ws > 1:
@@ -712,6 +726,7 @@ def oneshot(
     calibration_batch_tokens: int = 16384,
     device: torch.device | str | None = None,
     offload_layers: bool | None = None,
+    moe_calibrate_all_experts: bool = True,
     **kwargs,
 ) -> torch.nn.Module:
     """``oneshot`` (S/entrypoints/oneshot.py:285) for a ``GPTQModifier`` or
@@ -729,6 +744,9 @@ def oneshot(
     quantized layer is moved back (``offload_layers``, default: True when the
     model starts on the CPU).  Returns the model with quantized weights and
     compressed-tensors scales and zero points, ready for ``save_compressed``.
+    Mixture-of-experts models have their fused experts split into per-expert
+    Linear modules first; with ``moe_calibrate_all_experts`` (the default, as
+    in the reference) every expert sees every token in the calibration pass.
     """
     mods = recipe if isinstance(recipe, (list, tuple)) else [recipe]
     mods = [m for m in mods if m is not None]
@@ -780,7 +798,8 @@ def oneshot(
         batches = _calibration_batches(mine, len(mine), calibration_batch_tokens, device)
     else:
         batches = [{k: v.to(device) for k, v in b.items()} for b in batches_all]
-    runner = SequentialRunner(model, mods, batches, device, sequential_targets, offload_layers)
+    runner = SequentialRunner(model, mods, batches, device, sequential_targets, offload_layers,
+                              moe_calibrate_all_experts)
     t0 = time.perf_counter()
     runner.capture()
     torch.cuda.synchronize(device)

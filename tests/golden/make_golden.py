@@ -29,6 +29,11 @@ seeded synthetic inputs and stores inputs and outputs as ``.npz`` files:
   rows of each ``weight_packed`` / ``weight_scale`` (GPTQ rows are
   independent given the Hessian, so a row sample is a fair sample), the
   weight shapes, and the final hidden-state error of the quantized model.
+* ``oneshot_c3tiny.npz`` -- the same for a 2-layer Qwen3-MoE at reduced width
+  (``llmcompressor_b200.synthetic`` "c3tiny": 8 experts top-2) with the
+  reference's all-expert calibration (``moe_calibrate_all_experts``, after its
+  post-load ``linearize_moe``), the router ignored (``re:.*mlp.gate$``); all
+  rows of every module.
 
 bf16 tensors are stored as ``uint16`` bit patterns, fp8 as ``uint8``.
 Only run where a reference checkout exists:
@@ -515,8 +520,54 @@ def gen_oneshot_c1():
     print("oneshot c1", f"{secs:.1f}s", names, arrays["hidden_rel_err"])
 
 
+def gen_oneshot_c3tiny():
+    import time
+
+    from torch.utils.data import DataLoader
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from llmcompressor_b200 import synthetic
+
+    from llmcompressor import oneshot
+    from llmcompressor.modifiers.gptq import GPTQModifier
+
+    model = synthetic.random_qwen3_moe("c3tiny")
+    ids = synthetic.calibration_tokens("c3tiny")
+    data = [{"input_ids": ids[i:i + 1], "attention_mask": torch.ones_like(ids[i:i + 1])} for i in range(len(ids))]
+    t0 = time.time()
+    oneshot(model=model, dataset=DataLoader(data, batch_size=None, shuffle=False), processor=object(),
+            recipe=GPTQModifier(targets="Linear", scheme="W4A16", ignore=["lm_head", "re:.*mlp.gate$"],
+                                actorder=None, block_size=128, dampening_frac=0.01),
+            pipeline="sequential", num_calibration_samples=len(ids), shuffle_calibration_samples=False,
+            moe_calibrate_all_experts=True)
+    secs = time.time() - t0
+    arrays = {"oneshot_seconds": np.array(secs)}
+    fp = synthetic.random_qwen3_moe("c3tiny")
+    with torch.no_grad():
+        hq = model.model(ids[:4]).last_hidden_state.float()
+        hf = fp.model(ids[:4]).last_hidden_state.float()
+    arrays["hidden_rel_err"] = (torch.linalg.norm((hq - hf).reshape(4, -1), dim=1)
+                                / torch.linalg.norm(hf.reshape(4, -1), dim=1)).numpy()
+    names = []
+    for name, mod in model.named_modules():
+        if not isinstance(mod, torch.nn.Linear) or not hasattr(mod, "weight_scale"):
+            continue
+        compress_module(mod)
+        sd = mod.state_dict()
+        arrays[f"{name}.weight_packed"] = sd["weight_packed"].numpy()
+        arrays[f"{name}.weight_scale"] = to_np(sd["weight_scale"])
+        arrays[f"{name}.weight_shape"] = sd["weight_shape"].numpy()
+        names.append(name)
+    arrays["modules"] = np.array(names)
+    np.savez_compressed(os.path.join(HERE, "oneshot_c3tiny.npz"), **arrays)
+    print("oneshot c3tiny", f"{secs:.1f}s", len(names), arrays["hidden_rel_err"])
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
+    if sys.argv[1:2] == ["oneshot_c3tiny"]:
+        gen_oneshot_c3tiny()
+        sys.exit(0)
     if sys.argv[1:2] == ["oneshot_c1"]:
         gen_oneshot_c1()
         sys.exit(0)
@@ -542,3 +593,4 @@ if __name__ == "__main__":
     gen_gptq_orderings()
     gen_act_observers()
     gen_oneshot_c1()
+    gen_oneshot_c3tiny()
