@@ -233,6 +233,8 @@ def run_ours(args, rank, world, device):
     }
     if args.e2e:
         out["e2e"] = run_e2e(args, rank, world, device)
+    if args.c3 and world == 1:
+        out["c3"] = run_c3(args, rank, world, device)
     return out
 
 
@@ -266,6 +268,62 @@ def run_e2e(args, rank, world, device):
     del model, runner
     torch.cuda.empty_cache()
     return {"ms": ms, "h2d_per_step": layer_bytes, "d2h_per_step": layer_bytes + 4 * 7, "layers": L}
+
+
+C3 = dict(layers=48, samples=256, seq=2048)
+
+
+def run_c3(args, rank, world, device):
+    """Config C3: oneshot GPTQ W4A16 with all-expert calibration on the
+    Qwen3-30B-A3B shape (128 experts top-8; every expert sees every token in
+    the calibration pass), 256 x 2048 tokens.  The model is built with the
+    layers the steps run (all 48 have the same shape); value = capture +
+    48 x mean timed layer step."""
+    from llmcompressor_b200 import _lib
+    from llmcompressor_b200 import oneshot as O
+    from llmcompressor_b200 import synthetic
+    from llmcompressor_b200.distributed import row_range
+
+    n_layers = min(C3["layers"], args.c3_warmup + args.c3_steps + 1)
+    model = synthetic.random_qwen3_moe("qwen3_30b_a3b", device=device, init_device=device,
+                                       num_hidden_layers=n_layers)
+    ids = synthetic.calibration_tokens("qwen3_30b_a3b", n=C3["samples"], seq_len=C3["seq"])
+    s0, s1 = row_range(ids.shape[0], rank, world)
+    batches = O._calibration_batches(ids[s0:s1], s1 - s0, CHUNK, device)
+    mod = O.GPTQModifier(targets="Linear", scheme="W4A16", ignore=["lm_head", "re:.*mlp.gate$"], actorder=None)
+    runner = O.SequentialRunner(model, [mod], batches, device)
+    _barrier(world)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    runner.capture()
+    c1.record()
+    for i in range(args.c3_warmup):
+        runner.run_layer(i, propagate=True)
+    _barrier(world)
+    launches0 = _lib.kernel_launches()
+    phases = []
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(args.c3_warmup, args.c3_warmup + args.c3_steps):
+        runner.run_layer(i, phases=phases, propagate=True)
+    t1.record()
+    _barrier(world)
+    ms = _max_over_ranks(t0.elapsed_time(t1), world, device)
+    cap_ms = _max_over_ranks(c0.elapsed_time(c1), world, device)
+    split, prev = {}, None
+    for name, ev in phases:
+        if name != "start" and prev is not None:
+            split[name] = split.get(name, 0.0) + prev.elapsed_time(ev)
+        prev = ev
+    runner.finish()
+    launches = _lib.kernel_launches() - launches0
+    del model, runner
+    torch.cuda.empty_cache()
+    return {"value": (cap_ms + ms * C3["layers"] / args.c3_steps) * 1e-3, "unit": "s",
+            "ms_per_step": ms / args.c3_steps, "steps": args.c3_steps, "warmup": args.c3_warmup,
+            "phases_ms_per_step": {k: v / args.c3_steps for k, v in split.items()}, "gpu_launches": launches,
+            "workload": "C3: oneshot GPTQ W4A16 g128, all-expert calibration, Qwen3-30B-A3B shape "
+                        "(48 layers, 128 experts top-8), 256x2048 tokens; value = capture + 48 x mean layer step"}
 
 
 CAST_SCHEMES = ("W4A16", "NVFP4A16", "MXFP4A16", "FP8_BLOCK", "FP8_DYNAMIC")
@@ -613,6 +671,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
+    ap.add_argument("--no-c3", dest="c3", action="store_false", help="skip the MoE (Qwen3-30B-A3B shape) leg")
+    ap.add_argument("--c3-steps", type=int, default=2)
+    ap.add_argument("--c3-warmup", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
 
@@ -713,6 +774,8 @@ def main():
                        "h2d_bytes_per_step": int(e["h2d_per_step"]), "d2h_bytes_per_step": int(e["d2h_per_step"]),
                        "note": "layer weights from pinned host memory in, quantized layer back out, loss read "
                                "on the host, every step"}
+    if "c3" in res:
+        line["c3"] = res["c3"]
     if args.cpu_baseline and world == 1:
         cb = cpu_sample(3, 1)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}

@@ -13,12 +13,13 @@ them) and every expert's down projection its own.
 ``linearize_experts`` does the split here; the module names
 (``experts.{e}.gate_proj`` / ``up_proj`` / ``down_proj``) are the reference's,
 so checkpoints and ignore patterns carry over.  The combine differs in form,
-not in result: in all-expert mode each expert's output over all tokens is
-weighted by its dense routing column (zero for tokens not routed to it) and
-added in expert order, which adds the same bf16 products in the same order
-as the reference's gather / ``index_add_`` without a host sync per expert;
-outside that mode (the propagation pass) each expert runs on its routed
-tokens only, grouped with one host sync per call.
+not in result: in all-expert mode (the whole oneshot, calibration and
+propagation passes, as in the reference) each expert's output over all
+tokens is weighted by its dense routing column (zero for tokens not routed
+to it) and added in expert order, which adds the same bf16 products in the
+same order as the reference's gather / ``index_add_`` without a host sync per
+expert; outside that mode each expert runs on its routed tokens only,
+grouped with one host sync per call.
 """
 from __future__ import annotations
 

@@ -662,8 +662,11 @@ class SequentialRunner:
             _rtn(rl)
         if propagate if propagate is not None else li + 1 < len(self.layers):
             # propagate: the quantized layer's outputs are the next layer's inputs
-            for i, (h, kw, rest) in enumerate(self.cache):
-                self.cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
+            # (MoE layers in all-expert mode, as the reference keeps it for the
+            # whole oneshot)
+            with moe.calibrate_all_experts(self.all_experts):
+                for i, (h, kw, rest) in enumerate(self.cache):
+                    self.cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
         mark("propagate")
         if self.offload:
             self._offload(layer)
