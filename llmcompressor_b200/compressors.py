@@ -42,14 +42,41 @@ class PackedQuantizationCompressor:
         zp = sd.get("weight_zero_point", None)
         args = scheme.weights
         g_idx = sd.get("weight_g_idx")
-        if g_idx is not None and g_idx.device.type != "meta" and not bool((g_idx == -1).all()):
-            raise NotImplementedError("activation-ordered g_idx is not implemented on this path")
-        sd["weight_packed"] = ops.quantize_pack(weight, args, scale, zp, fmt=_lib.FMT_PACK_INT32)
+        if g_idx is not None and g_idx.device.type != "meta" and getattr(args, "group_size", None):
+            sd["weight_packed"] = _pack_with_g_idx(weight, args, scale, zp, g_idx)
+        else:
+            sd["weight_packed"] = ops.quantize_pack(weight, args, scale, zp, fmt=_lib.FMT_PACK_INT32)
         sd["weight_shape"] = torch.tensor(weight.shape)
         strategy = getattr(args.strategy, "value", args.strategy)
         if not args.symmetric and strategy in ("group", "channel"):
             sd["weight_zero_point"] = ops.pack_zero_point(zp, args.num_bits)
         return _remove_symmetric_zp(sd, scheme)
+
+
+def _pack_with_g_idx(weight, args, scale, zp, g_idx):
+    """Packed codes when column j belongs to group ``g_idx[j]`` (activation
+    ordering GROUP; -1 means the column's own group j // group_size, the
+    placeholder compressed-tensors initialises g_idx with): the group scales
+    are expanded to one scale per column on the device (no host sync) and the
+    columns quantized as groups of one -- the same per-element arithmetic as
+    ``quantize`` with ``g_idx``."""
+    rows, cols = weight.shape
+    own = torch.arange(cols, device=weight.device) // int(args.group_size)
+    gi = torch.where(g_idx.to(torch.int64) < 0, own, g_idx.to(torch.int64))
+    idx = gi.unsqueeze(0).expand(rows, cols)
+    scale_cols = scale.gather(1, idx).contiguous()
+    zp_cols = zp.gather(1, idx).contiguous() if (zp is not None and not args.symmetric) else None
+    args1 = args.model_copy(update={"group_size": 1, "actorder": None})
+    # one code per byte (a packed word may not straddle parameter groups), then
+    # pack_to_int32's layout: code j of a word at bits j * num_bits, offset 2^(num_bits-1)
+    codes = ops.quantize_pack(weight, args1, scale_cols, zp_cols, fmt=_lib.FMT_INT8)
+    bits = int(args.num_bits)
+    per = 32 // bits
+    if cols % per:
+        codes = torch.nn.functional.pad(codes, (0, per - cols % per))
+    u = (codes.to(torch.int32) + (1 << (bits - 1))) & ((1 << bits) - 1)
+    shifts = torch.arange(per, device=weight.device, dtype=torch.int32) * bits
+    return (u.reshape(rows, -1, per) << shifts).sum(dim=-1, dtype=torch.int32)
 
 
 class NaiveQuantizationCompressor:
@@ -106,12 +133,12 @@ class MXFP4PackedCompressor(NVFP4PackedCompressor):
 
     @classmethod
     def _compress_scale(cls, scale: torch.Tensor, args) -> torch.Tensor:
-        # compress_mx_scale (CT/compressors/mx_utils.py:18-30): the scale is a power
-        # of two, so 127 + floor(log2(scale)) is its biased exponent field; the
-        # bit extraction runs in the kernel that produced it (ops.modelfree_quantize)
-        # or here on an already power-of-two float scale.
-        bits = scale.to(torch.float32).contiguous().view(torch.int32)
-        return ((bits >> 23) & 0xFF).to(torch.uint8)
+        # compress_mx_scale (CT/compressors/mx_utils.py:18-30) step for step, in
+        # the scale's own dtype (the log2 rounds there) -- the same value for
+        # every input, powers of two or not, subnormals and zeros included.
+        # The model-free kernels write E8M0 directly; this is the save path's
+        # small per-group tensor.
+        return (127 + torch.floor(torch.log2(scale)).to(torch.int32)).to(args.scale_dtype or torch.uint8)
 
 
 COMPRESSORS = {
@@ -151,11 +178,27 @@ def compress_module(module: torch.nn.Module, format: str | None = None) -> None:
         module.register_parameter(k, torch.nn.Parameter(v, requires_grad=False))
 
 
+_ORIGINAL: dict = {}
+
+
 def register_with_compressed_tensors() -> None:
     """Route compressed-tensors' ``compress`` classmethods for every format
-    covered here to these kernels (the save-path plug-in point)."""
+    covered here to these kernels (the save-path plug-in point).
+    ``unregister_from_compressed_tensors`` restores the originals."""
     from compressed_tensors.compressors import BaseCompressor
 
     for fmt, cls in COMPRESSORS.items():
         ct_cls = BaseCompressor.get_value_from_registry(fmt)
+        if fmt not in _ORIGINAL:
+            _ORIGINAL[fmt] = (ct_cls, ct_cls.__dict__.get("compress"))
         ct_cls.compress = classmethod(lambda _c, state_dict, scheme, _impl=cls: _impl.compress(state_dict, scheme))
+
+
+def unregister_from_compressed_tensors() -> None:
+    for fmt, (ct_cls, orig) in list(_ORIGINAL.items()):
+        if orig is None:
+            if "compress" in ct_cls.__dict__:
+                delattr(ct_cls, "compress")
+        else:
+            ct_cls.compress = orig
+        del _ORIGINAL[fmt]

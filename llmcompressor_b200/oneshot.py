@@ -772,11 +772,7 @@ def oneshot(
     if not needs_data:
         # weight-only RTN: no calibration pass (the qparams do not depend on data)
         runner = SequentialRunner(model, mods, [], device)
-        for _, (mod, _) in runner.rtn_found.items():
-            if not mod.weight.is_cuda:
-                mod.to(device)
-        _rtn(runner.rtn_found)
-        stats = runner.finish()
+        stats = runner.finish()  # every module is outside the (absent) GPTQ layers: round-to-nearest there
         stats.seconds["total"] = time.perf_counter() - t_all
         globals()["LAST_STATS"] = stats
         return model
