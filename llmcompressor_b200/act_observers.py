@@ -234,3 +234,68 @@ OBSERVERS = {
     "static_minmax": StaticMinMaxObserver,
     "minmax": MinMaxObserver,
 }
+
+
+# ------------------------------------------------------------------ reference registry seam
+_REGISTERED: dict = {}
+
+
+def register_with_llmcompressor() -> list[str]:
+    """Make the reference's observer registry (``Observer.register`` /
+    ``load_from_registry``, S/observers/base.py:29,
+    S/modifiers/quantization/calibration.py:80-83) build observers whose
+    activation statistics come from the GPU kernels.
+
+    Each registry name (``memoryless_minmax``, ``static_minmax``, ``minmax``)
+    is pointed at a subclass of the reference's own observer class, so
+    ``initialize_observer`` attaches it as before (an ``nn.Module`` with the
+    fusion handler, ``get_qparams``, ``sync_activation_stats`` ...); only its
+    ``forward`` on a CUDA activation is replaced by the kernel update above
+    (bit-identical statistics).  Weight observations and CPU tensors keep the
+    reference's path.  Returns the names routed; ``unregister_from_llmcompressor``
+    restores the registry.  Needs the reference package importable."""
+    from compressed_tensors.registry.registry import _REGISTRY, standardize_lookup_name
+    from llmcompressor.observers.base import Observer as RefObserver
+
+    table = _REGISTRY[RefObserver]
+    modes = {"memoryless_minmax": _MEMORYLESS, "static_minmax": _STATIC, "minmax": _AVERAGE}
+    for name, mode in modes.items():
+        key = standardize_lookup_name(name)  # the registry's own key form
+        ref_cls = _REGISTERED.get(name, (table.get(key), key))[0]
+        if ref_cls is None:
+            continue
+        _REGISTERED.setdefault(name, (ref_cls, key))
+        table[key] = _gpu_subclass(ref_cls, mode)
+    return sorted(n for n in modes if n in _REGISTERED)
+
+
+def unregister_from_llmcompressor() -> None:
+    from compressed_tensors.registry.registry import _REGISTRY
+    from llmcompressor.observers.base import Observer as RefObserver
+
+    table = _REGISTRY[RefObserver]
+    for name, (ref_cls, key) in list(_REGISTERED.items()):
+        table[key] = ref_cls
+        del _REGISTERED[name]
+
+
+def _gpu_subclass(ref_cls, mode: int):
+    class GpuActivationObserver(ref_cls):
+        @torch.no_grad()
+        def forward(self, observed: torch.Tensor):
+            if self.is_weight_obs or not observed.is_cuda or observed.dtype not in (torch.bfloat16, torch.float32):
+                return super().forward(observed)
+            if observed.numel() == 0:
+                return self
+            c = float((self.args.observer_kwargs or {}).get("averaging_constant", 0.01))
+            m = _MEMORYLESS if (mode == _AVERAGE and c == 1.0) else mode
+            prev = self.has_statistics
+            mn, mx = observe_activation_(observed, self.args, self.base_name, m, c,
+                                         self.min_vals if prev else None, self.max_vals if prev else None)
+            self.min_vals, self.max_vals = mn, mx
+            self.fusion_handler.get_fused_statistics()
+            return self
+
+    GpuActivationObserver.__name__ = f"Gpu{ref_cls.__name__}"
+    GpuActivationObserver.__qualname__ = GpuActivationObserver.__name__
+    return GpuActivationObserver

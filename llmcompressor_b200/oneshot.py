@@ -332,6 +332,30 @@ def _rtn(found: dict) -> None:
         _set_params(mod, q)
 
 
+def _rtn_dist(found: dict, rank: int, ws: int) -> None:
+    """Round-to-nearest qparams under DDP
+    (``QuantizationModifier.on_sequential_epoch_end`` and
+    ``_broadcast_qparam_onloads``, S/modifiers/quantization/quantization/base.py:85-137):
+    modules are split across ranks by weight size (greedy bin packing), each
+    rank observes its own, and every module's qparams are broadcast from its
+    owner.  Every rank issues the same broadcasts in the same order."""
+    import torch.distributed as dist
+
+    from .distributed import greedy_owners
+
+    owners = greedy_owners({n: float(m.weight.numel()) for n, (m, _) in found.items()}, ws)
+    _rtn({n: v for n, v in found.items() if owners[n] == rank})
+    works = []
+    for n in sorted(found):
+        mod = found[n][0]
+        for attr in ("weight_scale", "weight_zero_point", "weight_global_scale"):
+            t = getattr(mod, attr, None)
+            if isinstance(t, torch.Tensor):
+                works.append(dist.broadcast(t.data, src=owners[n], async_op=True))
+    for w in works:
+        w.wait()
+
+
 # ------------------------------------------------------------------ GPTQ per layer
 class _LayerCalibration:
     """Forward pre-hooks on one layer's quantized modules: modules that read
@@ -710,7 +734,10 @@ class SequentialRunner:
             for _, (mod, _) in rtn_rest.items():
                 if not mod.weight.is_cuda:
                     mod.to(self.device)
-            _rtn(rtn_rest)
+            if self.ws > 1:
+                _rtn_dist(rtn_rest, self.rank, self.ws)
+            else:
+                _rtn(rtn_rest)
         _check_losses(self.stats)
         _lib.check_device_errors(self.device, "oneshot")
         _finish_modules(self.found)

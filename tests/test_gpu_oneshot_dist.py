@@ -5,7 +5,9 @@ rows are split and the quantized rows all-gathered.  Checks: both ranks end
 with identical weights; against the reference's own oneshot run
 (``tests/golden/oneshot_c1.npz``), layer 0's q/k/v codes are >= 99% identical
 and the quantized model's final hidden-state error is within 5% of the
-reference's.  Needs two GPUs; skipped otherwise."""
+reference's.  Round-to-nearest (``QuantizationModifier``) under DDP splits
+the modules across the ranks and broadcasts their qparams: both ranks must
+hold exactly the single-GPU qparams.  Needs two GPUs; skipped otherwise."""
 import datetime
 import os
 import socket
@@ -67,6 +69,63 @@ def _worker(rank, world, port, q):
         q.put((rank, f"error: {type(e).__name__}: {e}", None))
     finally:
         dist.destroy_process_group()
+
+
+def _rtn_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from llmcompressor_b200 import oneshot as O
+        from llmcompressor_b200 import synthetic
+
+        model = synthetic.random_llama("c1").to(dev)
+        O.oneshot(model, recipe=O.QuantizationModifier(targets="Linear", scheme="W4A16_ASYM", ignore=["lm_head"]))
+        torch.cuda.synchronize()
+        out = {n: (m.weight_scale.detach().cpu(), m.weight_zero_point.detach().cpu())
+               for n, m in model.named_modules() if hasattr(m, "weight_scale")}
+        q.put((rank, "ok", out))
+    except Exception as e:
+        q.put((rank, f"error: {type(e).__name__}: {e}", None))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(target, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        r, status, out = q.get(timeout=600)
+        got[r] = (status, out)
+    for p in procs:
+        p.join(timeout=120)
+    return got
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_rtn_matches_one_gpu():
+    from llmcompressor_b200 import oneshot as O
+    from llmcompressor_b200 import synthetic
+
+    got = _spawn(_rtn_worker)
+    assert all(v[0] == "ok" for v in got.values()), {r: v[0] for r, v in got.items()}
+    model = synthetic.random_llama("c1").cuda()
+    O.oneshot(model, recipe=O.QuantizationModifier(targets="Linear", scheme="W4A16_ASYM", ignore=["lm_head"]))
+    ref = {n: (m.weight_scale.detach().cpu(), m.weight_zero_point.detach().cpu())
+           for n, m in model.named_modules() if hasattr(m, "weight_scale")}
+    for r in (0, 1):
+        out = got[r][1]
+        assert set(out) == set(ref)
+        for n in ref:
+            assert torch.equal(out[n][0], ref[n][0]) and torch.equal(out[n][1], ref[n][1]), (r, n)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
