@@ -213,7 +213,7 @@ def run_ours(args, rank, world, device):
     stats = runner.finish()
     casts = None
     mfree = None
-    if rank == 0:
+    if rank == 0 and args.casts:
         from llmcompressor_b200 import oneshot as O
 
         lw = [{n: m.weight.data for n, m in l.named_modules() if isinstance(m, torch.nn.Linear)}
@@ -221,7 +221,7 @@ def run_ours(args, rank, world, device):
         casts = measure_casts(lw)
     del model, runner
     torch.cuda.empty_cache()
-    if rank == 0:
+    if rank == 0 and args.casts:
         mfree = modelfree_layers(device)
     out = {
         "ms": ms, "capture_ms": capture_ms, "layers": L, "launches": launches, "clocks": clk,
@@ -672,6 +672,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-c3", dest="c3", action="store_false", help="skip the MoE (Qwen3-30B-A3B shape) leg")
+    ap.add_argument("--no-casts", dest="casts", action="store_false", help="skip the cast and model-free legs")
     ap.add_argument("--c3-steps", type=int, default=2)
     ap.add_argument("--c3-warmup", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
