@@ -145,7 +145,7 @@ def build_runner(args, rank, world, device, on_host: bool = False):
                 p.data = p.data.cpu().pin_memory()
     mod = O.GPTQModifier(targets="Linear", scheme="W4A16", ignore=["lm_head"], actorder=None, block_size=128,
                          dampening_frac=0.01)
-    runner = O.SequentialRunner(model, [mod], batches, device, offload_layers=on_host)
+    runner = O.SequentialRunner(model, [mod], batches, device, offload_layers=on_host, fused_forward=args.fused)
     return model, runner
 
 
@@ -291,7 +291,7 @@ def run_c3(args, rank, world, device):
     s0, s1 = row_range(ids.shape[0], rank, world)
     batches = O._calibration_batches(ids[s0:s1], s1 - s0, CHUNK, device)
     mod = O.GPTQModifier(targets="Linear", scheme="W4A16", ignore=["lm_head", "re:.*mlp.gate$"], actorder=None)
-    runner = O.SequentialRunner(model, [mod], batches, device)
+    runner = O.SequentialRunner(model, [mod], batches, device, fused_forward=args.fused)
     _barrier(world)
     c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     c0.record()
@@ -676,6 +676,8 @@ def main():
     ap.add_argument("--c3-steps", type=int, default=2)
     ap.add_argument("--c3-warmup", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--eager-forward", dest="fused", action="store_false",
+                    help="run the decoder layers' HF forwards as they are (no fused elementwise kernels)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

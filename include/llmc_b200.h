@@ -352,6 +352,33 @@ int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const 
 int llmc_gemm_f32_nt(int64_t m, int64_t n, int64_t k, const float* A, int64_t lda, const float* B, int64_t ldb,
                      float* C, int64_t ldc, int mode, void* stream);
 
+/* ---------------------------------------------------------------- calibration forward
+ * Fused elementwise parts of a Llama-family decoder layer, used by the
+ * sequential calibration pipeline's forward passes (the reference runs the
+ * HF modules eagerly: S/pipelines/sequential/pipeline.py:70-118 calling
+ * transformers' LlamaDecoderLayer.forward).  bf16 in and out, 16-byte
+ * aligned pointers and strides in elements that are multiples of 8, else
+ * LLMC_EINVAL_SHAPE.
+ *
+ * RMSNorm of `rows` rows of `cols` values (LlamaRMSNorm.forward): float32
+ * mean of squares, rsqrt(mean + eps), bf16(x*r), bf16(weight * that).  With
+ * `residual` non-NULL the normalised value is h = bf16(residual + x), also
+ * written to residual_out (the decoder layer's post-attention
+ * `residual + hidden_states` fused with post_attention_layernorm). */
+int llmc_rmsnorm_bf16(const void* x, const void* residual, int64_t rows, int64_t cols, const void* weight, float eps,
+                      void* out, void* residual_out, void* stream);
+/* Rotary embedding (apply_rotary_pos_emb: x*cos + rotate_half(x)*sin, each
+ * product and the sum rounded to bf16) of x (batch, heads, seq, head_dim)
+ * with element strides sb, sh, ss (unit stride inside a head) into out laid
+ * out (batch, seq, heads, head_dim) contiguous.  cos / sin: (batch or 1, seq,
+ * head_dim), rows contiguous, batch stride cos_batch_stride (0: shared). */
+int llmc_rotary_bf16(const void* x, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t sb,
+                     int64_t sh, int64_t ss, const void* cos, const void* sin, int64_t cos_batch_stride, void* out,
+                     void* stream);
+/* out = bf16(bf16(silu(gate)) * up) over n contiguous values (LlamaMLP's
+ * act_fn(gate_proj(x)) * up_proj(x) with act_fn = SiLU). */
+int llmc_silu_mul_bf16(const void* gate, const void* up, int64_t n, void* out, void* stream);
+
 /* ---------------------------------------------------------------- no-allocation variant
  * llmc_gptq_quantize for callers that cannot allocate device memory -- code
  * running during CUDA stream capture (where cudaMalloc is not allowed),

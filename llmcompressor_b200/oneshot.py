@@ -45,6 +45,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib, gptq, moe, ops
+from .layer_forward import fused_layer_ops
 
 __all__ = ["oneshot", "GPTQModifier", "QuantizationModifier", "OneshotStats"]
 
@@ -615,8 +616,9 @@ class SequentialRunner:
     the modules frozen.  ``bench.py`` times ``run_layer`` steps."""
 
     def __init__(self, model, modifiers, batches, device, sequential_targets=None, offload_layers=False,
-                 moe_calibrate_all_experts: bool = True):
+                 moe_calibrate_all_experts: bool = True, fused_forward: bool = True):
         self.model = model
+        self.fused = fused_forward
         self.device = device
         self.offload = offload_layers
         self.all_experts = moe_calibrate_all_experts
@@ -670,7 +672,7 @@ class SequentialRunner:
         lm = {self._name_of[id(m)]: m for m in layer.modules() if id(m) in self._name_of}
         if lm:
             cal = _LayerCalibration(lm)
-            with moe.calibrate_all_experts(self.all_experts):
+            with moe.calibrate_all_experts(self.all_experts), fused_layer_ops(layer, enabled=self.fused):
                 for (h, kw, rest) in self.cache:
                     cal.run(layer, h, rest, kw)
             cal.remove()
@@ -688,7 +690,7 @@ class SequentialRunner:
             # propagate: the quantized layer's outputs are the next layer's inputs
             # (MoE layers in all-expert mode, as the reference keeps it for the
             # whole oneshot)
-            with moe.calibrate_all_experts(self.all_experts):
+            with moe.calibrate_all_experts(self.all_experts), fused_layer_ops(layer, enabled=self.fused):
                 for i, (h, kw, rest) in enumerate(self.cache):
                     self.cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
         mark("propagate")
@@ -757,6 +759,7 @@ def oneshot(
     device: torch.device | str | None = None,
     offload_layers: bool | None = None,
     moe_calibrate_all_experts: bool = True,
+    fused_forward: bool = True,
     **kwargs,
 ) -> torch.nn.Module:
     """``oneshot`` (S/entrypoints/oneshot.py:285) for a ``GPTQModifier`` or
@@ -777,6 +780,10 @@ def oneshot(
     Mixture-of-experts models have their fused experts split into per-expert
     Linear modules first; with ``moe_calibrate_all_experts`` (the default, as
     in the reference) every expert sees every token in the calibration pass.
+    ``fused_forward``: run the decoder layers' elementwise ops (RMSNorm,
+    rotary, SiLU * up, residual add) as fused kernels in the calibration and
+    propagation passes (``layer_forward.fused_layer_ops``); False runs the HF
+    forwards as they are.
     """
     mods = recipe if isinstance(recipe, (list, tuple)) else [recipe]
     mods = [m for m in mods if m is not None]
@@ -825,7 +832,7 @@ def oneshot(
     else:
         batches = [{k: v.to(device) for k, v in b.items()} for b in batches_all]
     runner = SequentialRunner(model, mods, batches, device, sequential_targets, offload_layers,
-                              moe_calibrate_all_experts)
+                              moe_calibrate_all_experts, fused_forward)
     t0 = time.perf_counter()
     runner.capture()
     torch.cuda.synchronize(device)
