@@ -373,8 +373,8 @@ def measure_casts(layers, reps: int = 3) -> dict:
 
 
 def modelfree_layers(device, reps: int = 10) -> dict:
-    """Device-resident model-free passes at BASELINE configs[3] / configs[4]
-    shapes, one layer (or expert sample) each, timed with CUDA events:
+    """Device-resident model-free passes at the C4 / C5 benchmark shapes, one
+    layer (or expert sample) each, timed with CUDA events:
 
     * C4: one Llama-3-70B-shaped layer (q/k/v/o 8192-wide, gate/up/down 28672),
       ~N(0, 0.02) with 0.1% of values x50, NVFP4A16 with fused q/k/v and

@@ -1,6 +1,6 @@
 """GPU parity of the GPTQ solve (damping, inverse factor, block loop) through the C ABI.
 
-Bar (BASELINE north star): GPTQ integer codes >= 99% identical to the
+Bar: GPTQ integer codes >= 99% identical to the
 reference's, loss and per-layer output error ||(W-Q)X||^2/||WX||^2 within 1%
 relative of the reference's."""
 import numpy as np
