@@ -343,6 +343,27 @@ int llmc_gptq_quantize_ex(const void* w_bf16, int64_t rows, int64_t cols, const 
                           const LlmcGptqColumns* cx, int64_t blocksize, void* wq_bf16, float* loss,
                           void* workspace, int* status, void* stream);
 
+/* GPTQ for E weights of one shape, each with its own Hessian (the down
+ * projections of an MoE layer's experts, S/modifiers/gptq/base.py:591-597 once
+ * per expert): for every expert e, llmc_gptq_prepare_hessian and
+ * llmc_gptq_hinv on H[e] and the block loop (llmc_gptq_quantize) on W[e]
+ * with its scales, in column order.  The experts are issued across
+ * `nstreams` (1..16) library-owned streams joined to `stream`, so their
+ * small, latency-bound kernels overlap; one host call for all experts.
+ *   H       (E, d, d) float32, the averaged Hessians (clobbered);
+ *   w_bf16  (E, rows, d); scale_bf16 / zp: each expert's qparams laid out as
+ *           llmc_calculate_qparams gives them (CHANNEL, GROUP, TENSOR or
+ *           BLOCK; TENSOR_GROUP -> LLMC_ENOSUPPORT), experts back to back;
+ *           zp NULL for symmetric / float types;
+ *   wq_bf16 (E, rows, d) out; loss (E) float32 out; status (E) int32 out
+ *           (zeroed here; LLMC_ENOT_PD: that expert fell back to
+ *           round-to-nearest; LLMC_ETIMEOUT: a bounded wait ran out);
+ *   workspace: llmc_gptq_solve_batch_workspace_size bytes, 256-byte aligned. */
+int llmc_gptq_solve_batch_workspace_size(int64_t E, int64_t rows, int64_t d, int nstreams, int64_t* bytes);
+int llmc_gptq_solve_batch(float* H, int64_t E, int64_t d, float percdamp, const void* w_bf16, int64_t rows,
+                          const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp, int64_t blocksize,
+                          void* wq_bf16, float* loss, int* status, void* workspace, int nstreams, void* stream);
+
 /* Float32-accurate GEMM on the tensor cores (3xTF32 split):
  *   C (m x n, ldc) = A*B^T (mode 0), C - A*B^T (mode 1) or -A*B^T (mode 2),
  * A row-major m x k, B row-major n x k -- the shape of the GPTQ trailing update
@@ -378,6 +399,28 @@ int llmc_rotary_bf16(const void* x, int64_t batch, int64_t heads, int64_t seq, i
 /* out = bf16(bf16(silu(gate)) * up) over n contiguous values (LlamaMLP's
  * act_fn(gate_proj(x)) * up_proj(x) with act_fn = SiLU). */
 int llmc_silu_mul_bf16(const void* gate, const void* up, int64_t n, void* out, void* stream);
+/* Mixture-of-experts layers in all-expert mode (every expert on every token,
+ * the reference's moe_calibrate_all_experts; S/modeling/moe/linear_experts.py:244-277)
+ * with the experts' projections stacked: gate / up are (rows, cols) with
+ * cols = experts * group, expert e owning columns [e*group, (e+1)*group).
+ * out = bf16(bf16(silu(gate)) * up) (may be NULL) and out_scaled =
+ * bf16(out * weights[row, e]) (may be NULL; weights float32, row stride
+ * weights_ld: the dense routing weights, zero where the token is not routed
+ * to expert e, which gives an exact zero).  llmc_scale_groups_bf16 applies
+ * the same scaling to a given x. */
+int llmc_silu_mul_scaled_bf16(const void* gate, const void* up, int64_t rows, int64_t cols, int64_t group,
+                              const float* weights, int64_t weights_ld, void* out, void* out_scaled, void* stream);
+int llmc_scale_groups_bf16(const void* x, int64_t rows, int64_t cols, int64_t group, const float* weights,
+                           int64_t weights_ld, void* out, void* stream);
+/* Routed MoE combine (transformers' Qwen3MoeExperts.forward: each expert's
+ * output times the token's routing weight, rounded to bf16 and index_add_-ed
+ * into a zero bf16 tensor, experts in increasing index):
+ * out[t] = sum_k bf16(y[pos[t*top_k + k]] * weights[t*top_k + k]) with a bf16
+ * rounding after every add, k in the given order.  y: (y_rows, hidden) bf16
+ * expert outputs; pos: int32 rows of y (an index outside [0, y_rows)
+ * contributes nothing); weights float32; top_k <= 64. */
+int llmc_moe_combine_bf16(const void* y, int64_t y_rows, const int* pos, const float* weights, int64_t tokens,
+                          int64_t top_k, int64_t hidden, void* out, void* stream);
 
 /* ---------------------------------------------------------------- no-allocation variant
  * llmc_gptq_quantize for callers that cannot allocate device memory -- code

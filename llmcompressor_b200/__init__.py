@@ -7,6 +7,6 @@ The host side mirrors the reference's Python interfaces (``accumulate_hessian``,
 CUDA device the entry points raise.
 """
 from . import _lib, ops, gptq  # noqa: F401
-from . import noalloc  # noqa: F401
+from . import act_observers, layer_forward, noalloc  # noqa: F401  (each registers its entry points)
 
 __version__ = "0.1.0"

@@ -1018,10 +1018,28 @@ struct Lookahead {
 
 extern "C" {
 
+namespace llmc {
+namespace gq {
+// The factorisation; `lookahead` puts the wide trailing updates on a side
+// stream (worth it for large d; the batched solve of many small Hessians
+// runs without it, on its own streams).
+static int hinv_impl(const float* A, int64_t d, float* Hinv, float* HinvT, void* workspace, int* status,
+                     cudaStream_t st, bool lookahead);
+}  // namespace gq
+}  // namespace llmc
+
 int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* workspace, int* status,
                    void* stream) {
   if (!A || !Hinv || !workspace || !status || d <= 0) return LLMC_EINVAL_ARG;
-  cudaStream_t st = (cudaStream_t)stream;
+  return llmc::gq::hinv_impl(A, d, Hinv, HinvT, workspace, status, (cudaStream_t)stream, true);
+}
+
+}  // extern "C"
+
+namespace llmc {
+namespace gq {
+static int hinv_impl(const float* A, int64_t d, float* Hinv, float* HinvT, void* workspace, int* status,
+                     cudaStream_t st, bool lookahead) {
   const int64_t nb = (d + PB - 1) / PB;
   float* B = (float*)workspace;
   float* X = B + d * d;
@@ -1039,7 +1057,8 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* w
   // panel k (both write the block column after it); the panel buffers
   // alternate so that (b) still reads its own panel.
   Lookahead la;
-  if (la.open(st)) return LLMC_ECUDA;
+  la.main = st;
+  if (lookahead && la.open(st)) return LLMC_ECUDA;
   int k = 0;
   for (int64_t kb0 = 0; kb0 < d; kb0 += PB, ++k) {
     const int kb = (int)std::min<int64_t>(PB, d - kb0);
@@ -1105,6 +1124,10 @@ int llmc_gptq_hinv(const float* A, int64_t d, float* Hinv, float* HinvT, void* w
   if (HinvT) { k_xt_to_ut<<<rg, 256, 0, st>>>(Xt, HinvT, d); llmc::note_launch(); }
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
+}  // namespace gq
+}  // namespace llmc
+
+extern "C" {
 
 int llmc_gptq_quantize_workspace_size(int64_t rows, int64_t cols, int64_t* bytes) {
   if (!bytes || rows < 0 || cols < 0) return LLMC_EINVAL_ARG;
@@ -1251,6 +1274,140 @@ int llmc_permute_columns_bf16(const void* src, int64_t rows, int64_t cols, const
                                                                             (uint16_t*)dst);
   llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+// ---------------------------------------------------------------- batched solve
+// Many Hessians of one size with one weight each (the down projections of an
+// MoE layer's experts): every expert's prepare / factor / block loop is the
+// single-Hessian sequence, issued from C across a pool of streams so that
+// the small, latency-bound kernels of different experts overlap and the
+// host pays one call instead of one per expert.
+
+namespace {
+constexpr int kBatchStreamsMax = 16;
+
+int64_t align256(int64_t b) { return (b + 255) & ~(int64_t)255; }
+
+// Streams of the current device for the batched solve, made once.
+int batch_streams(cudaStream_t* out, int n) {
+  static std::mutex mu;
+  static cudaStream_t pool[64][kBatchStreamsMax] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LLMC_ECUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!pool[dev][0]) {
+    for (int k = 0; k < kBatchStreamsMax; ++k)
+      if (cudaStreamCreateWithFlags(&pool[dev][k], cudaStreamNonBlocking) != cudaSuccess) {
+        for (int m = 0; m < k; ++m) cudaStreamDestroy(pool[dev][m]);
+        for (int m = 0; m < kBatchStreamsMax; ++m) pool[dev][m] = nullptr;
+        return LLMC_ECUDA;
+      }
+  }
+  for (int k = 0; k < n; ++k) out[k] = pool[dev][k];
+  return LLMC_OK;
+}
+
+struct BatchLayout {
+  int64_t hinv_ws, hinv, quant_ws, slot, dead;
+};
+
+int batch_layout(int64_t E, int64_t rows, int64_t d, int nstreams, BatchLayout* L, int64_t* total) {
+  int64_t hws = 0, qws = 0;
+  if (llmc_gptq_hinv_workspace_size(d, &hws) || llmc_gptq_quantize_workspace_size(rows, d, &qws))
+    return LLMC_EINVAL_ARG;
+  L->hinv_ws = align256(hws);
+  L->hinv = align256(d * d * (int64_t)sizeof(float));
+  L->quant_ws = align256(qws);
+  L->slot = L->hinv_ws + 2 * L->hinv + L->quant_ws;
+  L->dead = align256(E * d);
+  *total = L->dead + (int64_t)std::min<int64_t>(nstreams, E) * L->slot;
+  return LLMC_OK;
+}
+
+int clamp_streams(int n) { return std::max(1, std::min(n, kBatchStreamsMax)); }
+}  // namespace
+
+int llmc_gptq_solve_batch_workspace_size(int64_t E, int64_t rows, int64_t d, int nstreams, int64_t* bytes) {
+  if (!bytes || E <= 0 || rows < 0 || d <= 0) return LLMC_EINVAL_ARG;
+  BatchLayout L;
+  return batch_layout(E, rows, d, clamp_streams(nstreams), &L, bytes);
+}
+
+int llmc_gptq_solve_batch(float* H, int64_t E, int64_t d, float percdamp, const void* w_bf16, int64_t rows,
+                          const LlmcQuantArgs* args, const void* scale_bf16, const int8_t* zp, int64_t blocksize,
+                          void* wq_bf16, float* loss, int* status, void* workspace, int nstreams, void* stream) {
+  if (!H || !args || !w_bf16 || !scale_bf16 || !wq_bf16 || !loss || !status || !workspace || E <= 0 || d <= 0 ||
+      rows <= 0 || blocksize < 1)
+    return LLMC_EINVAL_ARG;
+  if ((uintptr_t)workspace % 256) return LLMC_EINVAL_ARG;
+  const QArgs q = to_qargs(*args);
+  int64_t per_scale = 0;  // scale (and zero-point) values of one expert
+  switch (q.strategy) {
+    case LLMC_STRAT_TENSOR: per_scale = 1; break;
+    case LLMC_STRAT_CHANNEL: per_scale = rows; break;
+    case LLMC_STRAT_GROUP:
+      if (q.group <= 0 || d % q.group) return LLMC_EINVAL_SHAPE;
+      per_scale = rows * (d / q.group);
+      break;
+    case LLMC_STRAT_BLOCK:
+      if (q.bh <= 0 || q.bw <= 0) return LLMC_EINVAL_ARG;
+      per_scale = ((rows + q.bh - 1) / q.bh) * ((d + q.bw - 1) / q.bw);
+      break;
+    default: return LLMC_ENOSUPPORT;  // TENSOR_GROUP needs a global scale per expert
+  }
+  const int ns = (int)std::min<int64_t>(clamp_streams(nstreams), E);
+  BatchLayout L;
+  int64_t total = 0;
+  if (batch_layout(E, rows, d, ns, &L, &total)) return LLMC_EINVAL_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaStream_t sts[kBatchStreamsMax];
+  if (batch_streams(sts, ns)) return cuda_fail("gptq_solve_batch: streams", cudaErrorUnknown);
+  if (cudaMemsetAsync(status, 0, sizeof(int) * E, st) != cudaSuccess) return LLMC_ECUDA;
+  cudaEvent_t ev_start = nullptr, ev_done[kBatchStreamsMax] = {};
+  auto cleanup = [&]() {
+    if (ev_start) cudaEventDestroy(ev_start);
+    for (int k = 0; k < ns; ++k)
+      if (ev_done[k]) cudaEventDestroy(ev_done[k]);
+  };
+  if (cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventRecord(ev_start, st) != cudaSuccess) {
+    cleanup();
+    return LLMC_ECUDA;
+  }
+  for (int k = 0; k < ns; ++k)
+    if (cudaStreamWaitEvent(sts[k], ev_start, 0) != cudaSuccess) {
+      cleanup();
+      return LLMC_ECUDA;
+    }
+  char* ws = (char*)workspace;
+  uint8_t* dead = (uint8_t*)ws;
+  int rc = LLMC_OK;
+  for (int64_t e = 0; e < E && rc == LLMC_OK; ++e) {
+    const int k = (int)(e % ns);
+    char* slot = ws + L.dead + (int64_t)k * L.slot;
+    void* hws = slot;
+    float* hinv = (float*)(slot + L.hinv_ws);
+    float* hinv_t = (float*)(slot + L.hinv_ws + L.hinv);
+    void* qws = slot + L.hinv_ws + 2 * L.hinv;
+    float* He = H + e * d * d;
+    uint8_t* de = dead + e * d;
+    rc = llmc_gptq_prepare_hessian(He, d, percdamp, de, sts[k]);
+    if (rc == LLMC_OK) rc = hinv_impl(He, d, hinv, hinv_t, hws, status + e, sts[k], false);
+    if (rc == LLMC_OK)
+      rc = llmc_gptq_quantize_ex((const uint16_t*)w_bf16 + e * rows * d, rows, d, hinv, hinv_t, de, args,
+                                 (const uint16_t*)scale_bf16 + e * per_scale, zp ? zp + e * per_scale : nullptr,
+                                 nullptr, blocksize, (uint16_t*)wq_bf16 + e * rows * d, loss + e, qws, status + e,
+                                 sts[k]);
+  }
+  // join every stream back to the caller's, also after an error (what was
+  // enqueued stays ordered before the caller's later work)
+  for (int k = 0; k < ns; ++k) {
+    if (cudaEventCreateWithFlags(&ev_done[k], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventRecord(ev_done[k], sts[k]) != cudaSuccess || cudaStreamWaitEvent(st, ev_done[k], 0) != cudaSuccess)
+      rc = rc == LLMC_OK ? LLMC_ECUDA : rc;
+  }
+  cleanup();
+  return rc;
 }
 
 }  // extern "C"

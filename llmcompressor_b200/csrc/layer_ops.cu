@@ -19,6 +19,8 @@
 // 16-byte vector accesses.
 #include "llmc_common.cuh"
 
+#include <algorithm>
+
 namespace llmc {
 namespace layer {
 
@@ -143,6 +145,93 @@ __global__ void __launch_bounds__(256) k_silu_mul(const uint4* __restrict__ g, c
   out[i] = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// MoE all-expert combine input: gate / up (rows, E*I) from the stacked
+// expert projections; act = bf16(bf16(silu(g)) * u) and / or
+// scaled = bf16(act * w[row, e]) with e = column / I and w the float32 dense
+// routing weights (rows, E); a zero weight (token not routed to expert e)
+// gives an exact zero, as the routed combine leaves that token out.
+// Grid: x over a row's 16-byte chunks, y (strided) over rows -- no 64-bit
+// divisions per thread.
+__global__ void __launch_bounds__(256) k_silu_mul_scaled(const uint4* __restrict__ g, const uint4* __restrict__ u,
+                                                         int64_t rows, int cols8, int group8,
+                                                         const float* __restrict__ w, int64_t w_ld,
+                                                         uint4* __restrict__ out, uint4* __restrict__ outs) {
+  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c8 >= cols8) return;
+  const int e = c8 / group8;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int64_t i = row * cols8 + c8;
+    const float s = w ? w[row * w_ld + e] : 1.0f;
+    const uint4 a = g[i], b = u[i];
+    const uint32_t A[4] = {a.x, a.y, a.z, a.w}, B[4] = {b.x, b.y, b.z, b.w};
+    uint32_t o[4], os[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float x0 = lo_f(A[k]), x1 = hi_f(A[k]);
+      const float s0 = rbf(x0 / (1.0f + expf(-x0))), s1 = rbf(x1 / (1.0f + expf(-x1)));
+      const float y0 = rbf(s0 * lo_f(B[k])), y1 = rbf(s1 * hi_f(B[k]));
+      o[k] = pack_bf2(y0, y1);
+      os[k] = s == 0.0f ? 0u : pack_bf2(y0 * s, y1 * s);
+    }
+    if (out) out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    if (outs) outs[i] = make_uint4(os[0], os[1], os[2], os[3]);
+  }
+}
+
+// scaled = bf16(x * w[row, column / group]) (zero weight: exact zero).
+__global__ void __launch_bounds__(256) k_scale_groups(const uint4* __restrict__ x, int64_t rows, int cols8,
+                                                      int group8, const float* __restrict__ w, int64_t w_ld,
+                                                      uint4* __restrict__ out) {
+  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c8 >= cols8) return;
+  const int e = c8 / group8;
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const int64_t i = row * cols8 + c8;
+    const float s = w[row * w_ld + e];
+    if (s == 0.0f) {
+      out[i] = make_uint4(0u, 0u, 0u, 0u);
+      continue;
+    }
+    const uint4 a = x[i];
+    const uint32_t A[4] = {a.x, a.y, a.z, a.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = pack_bf2(lo_f(A[k]) * s, hi_f(A[k]) * s);
+    out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// Routed MoE combine: out[t] = sum over k of bf16(y[pos[t, k]] * w[t, k]),
+// added in k order (the token's experts in increasing index) with a bf16
+// rounding after every add, starting from zero -- the per-expert
+// ``index_add_`` of weighted bf16 expert outputs into a zero tensor.
+// One thread per 8 hidden values of a token.
+__global__ void __launch_bounds__(256) k_moe_combine(const uint4* __restrict__ y, int64_t y_rows,
+                                                     const int* __restrict__ pos, const float* __restrict__ w,
+                                                     int64_t tokens, int K, int h8, uint4* __restrict__ out) {
+  const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c8 >= h8) return;
+  for (int64_t t = blockIdx.y; t < tokens; t += gridDim.y) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    for (int k = 0; k < K; ++k) {
+      const float s = w[t * K + k];
+      const int64_t r = pos[t * K + k];
+      if (r < 0 || r >= y_rows) continue;  // not a row of y: contributes nothing
+      const uint4 v = y[r * h8 + c8];
+      const uint32_t V[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = rbf(acc[2 * j] + rbf(lo_f(V[j]) * s));
+        acc[2 * j + 1] = rbf(acc[2 * j + 1] + rbf(hi_f(V[j]) * s));
+      }
+    }
+    out[t * h8 + c8] = make_uint4(pack_bf2(acc[0], acc[1]), pack_bf2(acc[2], acc[3]), pack_bf2(acc[4], acc[5]),
+                                  pack_bf2(acc[6], acc[7]));
+  }
+}
+
 }  // namespace layer
 }  // namespace llmc
 
@@ -208,6 +297,54 @@ int llmc_silu_mul_bf16(const void* gate, const void* up, int64_t n, void* out, v
   const int64_t n8 = n / 8;
   k_silu_mul<<<(unsigned)((n8 + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint4*)gate, (const uint4*)up,
                                                                             n8, (uint4*)out);
+  llmc::note_launch();
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_silu_mul_scaled_bf16(const void* gate, const void* up, int64_t rows, int64_t cols, int64_t group,
+                              const float* weights, int64_t weights_ld, void* out, void* out_scaled, void* stream) {
+  if (rows < 0 || cols < 0 || group <= 0 || weights_ld < 0) return LLMC_EINVAL_ARG;
+  if (rows == 0 || cols == 0) return LLMC_OK;
+  if (!gate || !up || (!out && !out_scaled) || (out_scaled && !weights)) return LLMC_EINVAL_ARG;
+  if (cols % 8 || group % 8 || cols % group || !al16(gate) || !al16(up) || (out && !al16(out)) ||
+      (out_scaled && !al16(out_scaled)) || (weights && weights_ld < cols / group))
+    return LLMC_EINVAL_SHAPE;
+  if (cols / 8 >= (1ll << 31)) return LLMC_EINVAL_SHAPE;
+  const int cols8 = (int)(cols / 8);
+  const dim3 grid((unsigned)((cols8 + 255) / 256), (unsigned)std::min<int64_t>(rows, 65535));
+  k_silu_mul_scaled<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint4*)gate, (const uint4*)up, rows, cols8,
+                                                            (int)(group / 8), out_scaled ? weights : nullptr,
+                                                            weights_ld, (uint4*)out, (uint4*)out_scaled);
+  llmc::note_launch();
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_scale_groups_bf16(const void* x, int64_t rows, int64_t cols, int64_t group, const float* weights,
+                           int64_t weights_ld, void* out, void* stream) {
+  if (rows < 0 || cols < 0 || group <= 0 || weights_ld < 0) return LLMC_EINVAL_ARG;
+  if (rows == 0 || cols == 0) return LLMC_OK;
+  if (!x || !weights || !out) return LLMC_EINVAL_ARG;
+  if (cols % 8 || group % 8 || cols % group || !al16(x) || !al16(out) || weights_ld < cols / group)
+    return LLMC_EINVAL_SHAPE;
+  if (cols / 8 >= (1ll << 31)) return LLMC_EINVAL_SHAPE;
+  const int cols8 = (int)(cols / 8);
+  const dim3 grid((unsigned)((cols8 + 255) / 256), (unsigned)std::min<int64_t>(rows, 65535));
+  k_scale_groups<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint4*)x, rows, cols8, (int)(group / 8), weights,
+                                                         weights_ld, (uint4*)out);
+  llmc::note_launch();
+  return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+}
+
+int llmc_moe_combine_bf16(const void* y, int64_t y_rows, const int* pos, const float* weights, int64_t tokens,
+                          int64_t top_k, int64_t hidden, void* out, void* stream) {
+  if (tokens < 0 || top_k <= 0 || hidden <= 0 || y_rows < 0) return LLMC_EINVAL_ARG;
+  if (tokens == 0) return LLMC_OK;
+  if (!y || !pos || !weights || !out) return LLMC_EINVAL_ARG;
+  if (hidden % 8 || !al16(y) || !al16(out) || top_k > 64 || hidden / 8 >= (1ll << 31)) return LLMC_EINVAL_SHAPE;
+  const int h8 = (int)(hidden / 8);
+  const dim3 grid((unsigned)((h8 + 255) / 256), (unsigned)std::min<int64_t>(tokens, 65535));
+  k_moe_combine<<<grid, 256, 0, (cudaStream_t)stream>>>((const uint4*)y, y_rows, pos, weights, tokens, (int)top_k,
+                                                        h8, (uint4*)out);
   llmc::note_launch();
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }

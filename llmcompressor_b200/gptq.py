@@ -200,7 +200,8 @@ class BatchedHessian:
     def finalize(self) -> tuple[torch.Tensor, torch.Tensor]:
         """Flush and return (H, num_samples) as ``accumulate_hessian`` leaves them."""
         self.flush()
-        return self.H, torch.tensor(float(self.samples), dtype=torch.float32, device=self.device)
+        # a fill kernel, not a host-to-device copy (which would wait for the stream)
+        return self.H, torch.full((), float(self.samples), dtype=torch.float32, device=self.device)
 
 
 _I64P = ctypes.POINTER(ctypes.c_int64)
@@ -541,21 +542,130 @@ def _quantize_stacked(modules, qa, order, hinv, blocksize) -> list[tuple[torch.T
     """One block-loop call over the stacked rows of several modules; each
     module gets its rows back, its own scales and its own loss (the sum of
     its rows' losses)."""
-    qp = [weight_qparams(m, qa) for m in modules]
+    from . import ops
+
     w = torch.cat([m.weight.detach() for m in modules])
-    scale = torch.cat([q[0] for q in qp])
-    zp = torch.cat([q[1] for q in qp]) if qp[0][1] is not None else None
+    # GROUP / CHANNEL statistics are per row: one pass over the stacked rows
+    # gives each module's own min-max qparams
+    mn, mx = ops.observe_minmax(w, qa)
+    scale, zp = ops.calculate_qparams(mn, mx, qa)
+    for m in modules:
+        obs = getattr(m, "weight_observer", None)
+        if obs is not None and hasattr(obs, "delete_statistics"):
+            try:
+                obs.delete_statistics()
+            except Exception:  # an observer without statistics: nothing to release
+                pass
     row_loss = torch.empty(w.shape[0], dtype=torch.float32, device=w.device)
     wq, _ = quantize_with_inverse(w, qa, hinv, scale, zp, blocksize, order, None, None, row_loss)
     zp_dtype = getattr(qa, "zp_dtype", None) or torch.int8
     out, r0 = [], 0
-    for m, (sc, z, _) in zip(modules, qp):
+    for m in modules:
         r1 = r0 + m.weight.shape[0]
-        q = {"weight": wq[r0:r1].to(m.weight.dtype), "weight_scale": sc.to(dtype=m.weight.dtype),
-             "weight_zero_point": z.to(dtype=zp_dtype)}
+        q = {"weight": wq[r0:r1].to(m.weight.dtype), "weight_scale": scale[r0:r1].to(dtype=m.weight.dtype),
+             "weight_zero_point": zp[r0:r1].to(dtype=zp_dtype)}
         out.append((row_loss[r0:r1].sum().reshape(1), q))
         r0 = r1
     return out
+
+
+_lib.extend_signatures({
+    "llmc_gptq_solve_batch_workspace_size": [_I64, _I64, _I64, ctypes.c_int, _P],
+    "llmc_gptq_solve_batch": [_P, _I64, _I64, ctypes.c_float, _P, _I64, _P, _P, _P, _I64, _P, _P, _P, _P,
+                              ctypes.c_int, _P],
+})
+SOLVE_BATCH_STREAMS = 16
+
+
+class BatchStatus:
+    """The status word of one expert of a batched solve (``ok()`` as
+    ``InverseHessian.ok``)."""
+
+    def __init__(self, status: torch.Tensor, e: int):
+        self.status, self.e = status, e
+
+    def ok(self) -> bool:
+        code = int(self.status[self.e].item())
+        if code == _lib.ETIMEOUT:
+            _lib.raise_status(code, "gptq solve")
+        return code != _lib.ENOT_PD
+
+
+def batchable(modules, args_list, orders) -> bool:
+    """Modules whose Hessians can go through one batched solve: one weight
+    shape, bf16, the same per-row-scaled scheme (GROUP or CHANNEL, min-max
+    observers) and column order."""
+    if not modules or any(o is not None for o in orders):
+        return False
+    shape = modules[0].weight.shape
+    return _stackable(modules, args_list, orders) and all(m.weight.shape == shape for m in modules)
+
+
+def solve_batched(modules: list[torch.nn.Module], qa, H: torch.Tensor, blocksize: int = 128,
+                  percdamp: float = 0.01):
+    """The batched solve of E modules of one shape with E distinct Hessians
+    H (E*d, d) float32 (averaged; clobbered), in one call
+    (``llmc_gptq_solve_batch``).  The qparams come from one min-max pass over
+    the stacked weights (per-row statistics: the same values as per module).
+    Returns the stacked results: (weights (E, rows, d) bf16, scales
+    (E*rows, ...), zero points (E*rows, ...), losses (E) float32, status (E)
+    int32)."""
+    from . import ops
+
+    E = len(modules)
+    rows, d = modules[0].weight.shape
+    if H.dtype != torch.float32 or not H.is_contiguous() or tuple(H.shape) != (E * d, d):
+        raise ValueError("H must be a contiguous float32 (E * d, d) tensor")
+    dev = H.device
+    w = torch.stack([m.weight.detach() for m in modules])  # (E, rows, d)
+    mn, mx = ops.observe_minmax(w.view(E * rows, d), qa)
+    scale, zp = ops.calculate_qparams(mn, mx, qa)
+    for m in modules:
+        obs = getattr(m, "weight_observer", None)
+        if obs is not None and hasattr(obs, "delete_statistics"):
+            try:
+                obs.delete_statistics()
+            except Exception:  # an observer without statistics: nothing to release
+                pass
+    zpk = zp.to(torch.int8).contiguous() if (not qa.symmetric and _qtype(qa) == "int") else None
+    sc = scale.to(torch.bfloat16).contiguous()
+    out = torch.empty_like(w)
+    loss = torch.empty(E, dtype=torch.float32, device=dev)
+    status = torch.empty(E, dtype=torch.int32, device=dev)
+    nb = ctypes.c_int64(0)
+    check(lib().llmc_gptq_solve_batch_workspace_size(E, rows, d, SOLVE_BATCH_STREAMS, ctypes.byref(nb)),
+          "gptq_solve_batch_workspace_size")
+    ws = torch.empty(nb.value + 256, dtype=torch.uint8, device=dev)
+    wsp = (ws.data_ptr() + 255) // 256 * 256
+    qs = _lib.qargs_struct(qa)
+    check(lib().llmc_gptq_solve_batch(ptr(H), E, d, float(percdamp), ptr(w), rows, ctypes.byref(qs), ptr(sc),
+                                      ptr(zpk), int(blocksize), ptr(out), ptr(loss), ptr(status), wsp,
+                                      SOLVE_BATCH_STREAMS, stream_ptr(dev)), "gptq_solve_batch")
+    return out, scale, zp, loss, status
+
+
+def batched_param_dicts(modules, qa, out, scale, zp, loss) -> list[tuple[torch.Tensor, dict]]:
+    """Per module (loss as a float32 device scalar, q_param_dict) from the
+    stacked results of ``solve_batched``."""
+    rows = modules[0].weight.shape[0]
+    zp_dtype = getattr(qa, "zp_dtype", None) or torch.int8
+    res = []
+    for e, m in enumerate(modules):
+        r0, r1 = e * rows, (e + 1) * rows
+        res.append((loss[e:e + 1], {"weight": out[e].to(m.weight.dtype),
+                                    "weight_scale": scale[r0:r1].to(dtype=m.weight.dtype),
+                                    "weight_zero_point": zp[r0:r1].to(dtype=zp_dtype)}))
+    return res
+
+
+def quantize_batched(modules: list[torch.nn.Module], qa, H: torch.Tensor, blocksize: int = 128,
+                     percdamp: float = 0.01) -> tuple[torch.Tensor, list[tuple[torch.Tensor, dict]]]:
+    """``quantize_weight`` for E modules of one shape with E distinct
+    Hessians (``solve_batched``).  Returns (status (E) int32, per module
+    (loss as a float32 device scalar, q_param_dict));
+    ``BatchStatus(status, e).ok()`` reads expert e."""
+    out, scale, zp, loss, status = solve_batched(modules, qa, H, blocksize, percdamp)
+    return status, batched_param_dicts(modules, qa, out, scale, zp, loss)
 
 
 def quantize_weight(

@@ -42,6 +42,9 @@ _lib.extend_signatures({
     "llmc_rmsnorm_bf16": [_P, _P, _I64, _I64, _P, _F, _P, _P, _P],
     "llmc_rotary_bf16": [_P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P],
     "llmc_silu_mul_bf16": [_P, _P, _I64, _P, _P],
+    "llmc_silu_mul_scaled_bf16": [_P, _P, _I64, _I64, _I64, _P, _I64, _P, _P, _P],
+    "llmc_scale_groups_bf16": [_P, _I64, _I64, _I64, _P, _I64, _P, _P],
+    "llmc_moe_combine_bf16": [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _P],
 })
 
 # HF classes whose forwards the fused ones restate (the same source text in
@@ -112,6 +115,43 @@ def silu_mul(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(g)
     _lib.check(_lib.lib().llmc_silu_mul_bf16(g.data_ptr(), u.data_ptr(), g.numel(), out.data_ptr(),
                                              _lib.stream_ptr(g.device)), "silu_mul")
+    return out
+
+
+def silu_mul_scaled(g: torch.Tensor, u: torch.Tensor, group: int, weights: torch.Tensor | None,
+                    act: bool = True, scaled: bool = True):
+    """For stacked expert projections g, u (rows, E * group): ``act`` =
+    bf16(silu(g)) * u and ``scaled`` = bf16(act * weights[row, e]) (float32
+    dense routing weights (rows, E), zero where not routed -> exact zero).
+    Returns (act or None, scaled or None)."""
+    rows, cols = g.shape
+    a = torch.empty_like(g) if act else None
+    sc = torch.empty_like(g) if scaled else None
+    _lib.check(_lib.lib().llmc_silu_mul_scaled_bf16(
+        g.data_ptr(), u.data_ptr(), rows, cols, group, _lib.ptr(weights) if scaled else None,
+        weights.stride(0) if scaled else 0, _lib.ptr(a), _lib.ptr(sc), _lib.stream_ptr(g.device)), "silu_mul_scaled")
+    return a, sc
+
+
+def scale_groups(x: torch.Tensor, group: int, weights: torch.Tensor) -> torch.Tensor:
+    """bf16(x * weights[row, column // group]) (zero weight -> exact zero)."""
+    rows, cols = x.shape
+    out = torch.empty_like(x)
+    _lib.check(_lib.lib().llmc_scale_groups_bf16(x.data_ptr(), rows, cols, group, weights.data_ptr(),
+                                                 weights.stride(0), out.data_ptr(), _lib.stream_ptr(x.device)),
+               "scale_groups")
+    return out
+
+
+def moe_combine(y: torch.Tensor, pos: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+    """out[t] = sum over k of bf16(y[pos[t, k]] * weights[t, k]), added in k
+    order with a bf16 rounding per add (the per-expert ``index_add_``)."""
+    T, K = pos.shape
+    out = torch.empty(T, y.shape[1], dtype=y.dtype, device=y.device)
+    pos = pos.to(torch.int32).contiguous()
+    weights = weights.to(torch.float32).contiguous()
+    _lib.check(_lib.lib().llmc_moe_combine_bf16(y.data_ptr(), y.shape[0], pos.data_ptr(), weights.data_ptr(), T, K,
+                                                y.shape[1], out.data_ptr(), _lib.stream_ptr(y.device)), "moe_combine")
     return out
 
 

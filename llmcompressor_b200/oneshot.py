@@ -368,17 +368,63 @@ class _LayerCalibration:
     in which the modules are called, the pass stops at the input of the last
     module called (for a Llama layer: before the down projection's GEMM)."""
 
-    def __init__(self, modules: dict[str, torch.nn.Module]):
+    def __init__(self, modules: dict[str, torch.nn.Module], layer: torch.nn.Module | None = None,
+                 all_experts: bool = False):
         self.modules = modules  # name -> module
         self.group_of: dict[str, int] = {}
         self.groups: list[list[str]] = []
-        self.hess: list[gptq.BatchedHessian] = []
+        self.hess: list = []
         self.order: list[str] = []
         self._seen: dict[int, tuple] = {}
         self._handles = []
+        self._sinks: list[moe.LinearExperts] = []
         self._first = True
+        sunk: set[str] = set()
+        if layer is not None and all_experts:
+            name_of = {id(m): n for n, m in modules.items()}
+            for le in layer.modules():
+                if not isinstance(le, moe.LinearExperts):
+                    continue
+                names = [name_of.get(id(lin)) for ex in le for lin in (ex.gate_proj, ex.up_proj, ex.down_proj)]
+                if all(names) and le.stacked_ready():
+                    self._add_sink(le, names)
+                    sunk.update(names)
         for name, mod in modules.items():
-            self._handles.append(mod.register_forward_pre_hook(self._hook(name)))
+            if name not in sunk:
+                self._handles.append(mod.register_forward_pre_hook(self._hook(name)))
+
+    def _add_sink(self, le: "moe.LinearExperts", names: list[str]) -> None:
+        """Experts in stacked all-expert form: every expert's gate/up share
+        one Hessian of the block input; the experts' down inputs arrive
+        concatenated and one grouped launch accumulates all their Hessians."""
+        E = le.num_experts
+        ex0 = le[0]
+        inter, hidden = ex0.gate_proj.out_features, ex0.gate_proj.in_features
+        dev = ex0.gate_proj.weight.device
+        gu = [names[3 * e + k] for e in range(E) for k in (0, 1)]
+        g_gu = len(self.groups)
+        self.groups.append(gu)
+        self.hess.append(gptq.BatchedHessian(hidden, dev))
+        for n in gu:
+            self.group_of[n] = g_gu
+        down = _GroupedHessian(E, inter, dev)
+        for e in range(E):
+            n = names[3 * e + 2]
+            self.group_of[n] = len(self.groups)
+            self.groups.append([n])
+            self.hess.append(down.view(e))
+        key = f"experts@{id(le)}"
+
+        def sink(mod, x, act):
+            self.hess[g_gu].add(x)
+            down.add(act)
+            if self._first:
+                self.order.append(key)
+            elif self.order[-1] == key:
+                raise _Stop
+
+        le.calib_sink = sink
+        self._sinks.append(le)
 
     def _hook(self, name):
         def hook(mod, args):
@@ -418,6 +464,42 @@ class _LayerCalibration:
         for h in self._handles:
             h.remove()
         self._handles = []
+        for le in self._sinks:
+            le.calib_sink = None
+        self._sinks = []
+
+
+class _GroupedHessian:
+    """Block-diagonal Hessians of E experts' down projections, H (E*d, d),
+    from their concatenated inputs (tokens, E*d): one grouped launch per
+    batch.  ``view(e)`` is expert e's Hessian with ``BatchedHessian``'s
+    interface (``finalize``, ``samples``, ``d``, ``H``)."""
+
+    def __init__(self, E: int, d: int, device):
+        self.E, self.d = int(E), int(d)
+        self.H = torch.zeros(self.E * self.d, self.d, dtype=gptq.GPTQ_PRECISION, device=device)
+        self.samples = 0
+
+    def add(self, inp: torch.Tensor) -> None:
+        self.samples += inp.shape[0] if inp.ndim > 2 else 1
+        gptq.hessian_update_(self.H, inp.reshape(-1, self.E * self.d), 2.0, groups=self.E)
+
+    def view(self, e: int) -> "_GroupView":
+        return _GroupView(self, e)
+
+
+class _GroupView:
+    def __init__(self, parent: _GroupedHessian, e: int):
+        self.parent, self.d = parent, parent.d
+        self.H = parent.H[e * parent.d:(e + 1) * parent.d]
+        self._buf = None
+
+    @property
+    def samples(self) -> int:
+        return self.parent.samples
+
+    def finalize(self) -> tuple[torch.Tensor, torch.Tensor]:
+        return self.H, torch.full((), float(self.parent.samples), dtype=torch.float32, device=self.H.device)
 
 
 def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, stats: OneshotStats) -> None:
@@ -428,11 +510,29 @@ def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, st
 
     dev = next(iter(cal.modules.values())).weight.device
     main = torch.cuda.current_stream(dev)
-    order = sorted(range(len(cal.groups)), key=lambda g: -cal.hess[g].d)
-    streams = _side_streams(dev, max(1, min(MAX_SIDE_STREAMS, len(order))))
+    jobs, singles = _expert_batches(cal, found)
+    order = sorted(singles, key=lambda g: -cal.hess[g].d)
+    streams = _side_streams(dev, max(1, min(MAX_SIDE_STREAMS, len(order) + len(jobs))))
     done = []
     results = []
-    for i, g in enumerate(order):
+    for j, (gs, names, mods, qa) in enumerate(jobs):
+        # experts' down projections: one batched solve over their Hessians
+        st = streams[j % len(streams)]
+        st.wait_stream(main)
+        with torch.cuda.stream(st):
+            Hp, n = cal.hess[gs[0]].parent.H, cal.hess[gs[0]].finalize()[1]
+            Hp.record_stream(st)
+            Hb = Hp / n  # the reference's hessian / num_samples, per expert (as the single-group path divides)
+            status, res = gptq.quantize_batched(mods, qa, Hb, modifier.block_size, modifier.dampening_frac)
+            for e, (nm, mod, (loss, q)) in enumerate(zip(names, mods, res)):
+                _set_params(mod, q)
+                results.append((nm, loss, gptq.BatchStatus(status, e)))
+            ev = torch.cuda.Event()
+            ev.record(st)
+            done.append(ev)
+        for g in gs:
+            cal.hess[g] = None
+    for i, g in enumerate(order, start=len(jobs)):
         st = streams[i % len(streams)]
         st.wait_stream(main)
         with torch.cuda.stream(st):
@@ -460,6 +560,32 @@ def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, st
 
 
 MAX_SIDE_STREAMS = 8  # concurrent solve streams (an MoE layer has one Hessian group per expert)
+
+
+def _expert_batches(cal: _LayerCalibration, found: dict):
+    """Split the layer's Hessian groups into batched solves (the groups of
+    one grouped expert Hessian whose modules ``gptq.batchable`` takes: one
+    module per expert, one shape and scheme) and the rest.  Returns
+    ([(groups, names, modules, quant_args)], [other groups])."""
+    by_parent: dict[int, list[int]] = {}
+    singles = []
+    for g in range(len(cal.groups)):
+        h = cal.hess[g]
+        if isinstance(h, _GroupView) and len(cal.groups[g]) == 1:
+            by_parent.setdefault(id(h.parent), []).append(g)
+        else:
+            singles.append(g)
+    jobs = []
+    for gs in by_parent.values():
+        names = [cal.groups[g][0] for g in gs]
+        mods = [cal.modules[n] for n in names]
+        qas = [found[n][1].weights for n in names]
+        orders = [gptq.resolve_actorder(getattr(qa, "actorder", None)) for qa in qas]
+        if len(gs) == cal.hess[gs[0]].parent.E and gptq.batchable(mods, qas, orders):
+            jobs.append((gs, names, mods, qas[0]))
+        else:
+            singles.extend(gs)
+    return jobs, singles
 
 
 def _check_losses(stats: OneshotStats) -> None:
@@ -499,8 +625,18 @@ def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifie
 
     dev = next(iter(cal.modules.values())).weight.device
     main = torch.cuda.current_stream(dev)
+    jobs, singles = _expert_batches(cal, found)
+    for job in jobs:  # experts first: owned by ranks, solved in batches
+        _solve_experts_dist(cal, job, modifier, stats, rank, ws, dev)
+    # the remaining groups, renumbered
+    cal.groups = [cal.groups[g] for g in sorted(singles)]
+    cal.hess = [cal.hess[g] for g in sorted(singles)]
     ng = len(cal.groups)
-    counts = torch.tensor([float(cal.hess[g].samples) for g in range(ng)], dtype=torch.float64, device=dev)
+    if ng == 0:
+        return
+    # pinned staging: a pageable host-to-device copy would wait for the stream
+    counts = torch.tensor([float(cal.hess[g].samples) for g in range(ng)], dtype=torch.float64).pin_memory()
+    counts = counts.to(dev, non_blocking=True)
     Hs = [cal.hess[g].finalize()[0] for g in range(ng)]
     dist.all_reduce(counts)
     keys = [f"g{g}" for g in range(ng)]
@@ -537,6 +673,67 @@ def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifie
         cal.hess[g] = None
     for st in streams[:nst]:
         main.wait_stream(st)
+
+
+def _solve_experts_dist(cal, job, modifier, stats, rank: int, ws: int, dev) -> None:
+    """One batched expert solve across ranks (experts assigned to ranks, as
+    the reference assigns modules to owners): the experts' Hessians are
+    summed and scattered by owner in one reduce-scatter, every rank solves
+    its own experts in one batched call, and the quantized weights, qparams,
+    losses and statuses are all-gathered so that every rank holds the whole
+    quantized layer."""
+    import torch.distributed as dist
+
+    from .distributed import row_range
+
+    gs, names, mods, qa = job
+    E = len(gs)
+    parent = cal.hess[gs[0]].parent
+    d = parent.d
+    rows = mods[0].weight.shape[0]
+    per = -(-E // ws)  # experts per rank, the last ranks padded
+    cnt = torch.full((1,), float(parent.samples), dtype=torch.float32, device=dev)
+    dist.all_reduce(cnt)
+    Hfull = parent.H if per * ws == E else torch.cat(
+        [parent.H, torch.zeros((per * ws - E) * d, d, dtype=parent.H.dtype, device=dev)])
+    Hmine = torch.empty(per * d, d, dtype=parent.H.dtype, device=dev)
+    dist.reduce_scatter_tensor(Hmine, Hfull)
+    for g in gs:
+        cal.hess[g] = None
+    del Hfull
+    e0, e1 = row_range(E, rank, ws)  # rank r owns experts [r*per, min(E, (r+1)*per))
+    k = e1 - e0
+    # qparams dtypes and per-row shape, the same on every rank (a rank may own no expert)
+    from . import ops
+
+    mn1, mx1 = ops.observe_minmax(mods[0].weight.detach()[:1], qa)
+    s1, z1 = ops.calculate_qparams(mn1, mx1, qa)
+    parts = [torch.zeros((per, rows, d), dtype=torch.bfloat16, device=dev),
+             torch.zeros((per * rows,) + tuple(s1.shape[1:]), dtype=s1.dtype, device=dev),
+             torch.zeros((per * rows,) + tuple(z1.shape[1:]), dtype=z1.dtype, device=dev),
+             torch.zeros((per,), dtype=torch.float32, device=dev),
+             torch.zeros((per,), dtype=torch.int32, device=dev)]
+    if k > 0:
+        Hb = (Hmine[: k * d] / cnt).contiguous()
+        for dst, src in zip(parts, gptq.solve_batched(mods[e0:e1], qa, Hb, modifier.block_size,
+                                                      modifier.dampening_frac)):
+            dst[: src.shape[0]] = src
+    del Hmine
+    gathered = []
+    for t in parts:
+        full = torch.empty((t.shape[0] * ws,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev)
+        dist.all_gather_into_tensor(full, t)
+        gathered.append(full)
+    out_all, scale_all, zp_all, loss_all, status_all = gathered
+    # rank r's experts sit at [r*per, r*per + its count): back to expert order
+    idx = torch.cat([torch.arange(r * per, r * per + (row_range(E, r, ws)[1] - row_range(E, r, ws)[0]),
+                                  device=dev) for r in range(ws)])
+    ridx = (idx[:, None] * rows + torch.arange(rows, device=dev)[None, :]).reshape(-1)
+    res = gptq.batched_param_dicts(mods, qa, out_all[idx], scale_all[ridx], zp_all[ridx], loss_all[idx])
+    status_e = status_all[idx]
+    for e, (nm, mod, (loss, q)) in enumerate(zip(names, mods, res)):
+        _set_params(mod, q)
+        stats.losses[nm] = (loss, gptq.BatchStatus(status_e, e))
 
 
 def _solve_group_rows(cal, g, found, modifier, stats, inv, rank, ws, dev) -> None:
@@ -616,9 +813,13 @@ class SequentialRunner:
     the modules frozen.  ``bench.py`` times ``run_layer`` steps."""
 
     def __init__(self, model, modifiers, batches, device, sequential_targets=None, offload_layers=False,
-                 moe_calibrate_all_experts: bool = True, fused_forward: bool = True):
+                 moe_calibrate_all_experts: bool = True, fused_forward: bool = True,
+                 moe_routed_propagation: bool = True):
         self.model = model
         self.fused = fused_forward
+        # the propagation pass needs only the routed experts' outputs, which
+        # all-expert mode computes too (and then discards for unrouted tokens)
+        self.routed_propagation = moe_routed_propagation
         self.device = device
         self.offload = offload_layers
         self.all_experts = moe_calibrate_all_experts
@@ -671,7 +872,7 @@ class SequentialRunner:
         mark("onload")
         lm = {self._name_of[id(m)]: m for m in layer.modules() if id(m) in self._name_of}
         if lm:
-            cal = _LayerCalibration(lm)
+            cal = _LayerCalibration(lm, layer, self.all_experts)
             with moe.calibrate_all_experts(self.all_experts), fused_layer_ops(layer, enabled=self.fused):
                 for (h, kw, rest) in self.cache:
                     cal.run(layer, h, rest, kw)
@@ -687,10 +888,12 @@ class SequentialRunner:
         if rl:
             _rtn(rl)
         if propagate if propagate is not None else li + 1 < len(self.layers):
-            # propagate: the quantized layer's outputs are the next layer's inputs
-            # (MoE layers in all-expert mode, as the reference keeps it for the
-            # whole oneshot)
-            with moe.calibrate_all_experts(self.all_experts), fused_layer_ops(layer, enabled=self.fused):
+            # propagate: the quantized layer's outputs are the next layer's inputs.
+            # The reference keeps MoE layers in all-expert mode here too, whose
+            # output keeps only the routed tokens' expert outputs: the routed
+            # forward gives the same sum without the unrouted experts' work.
+            all_ex = self.all_experts and not self.routed_propagation
+            with moe.calibrate_all_experts(all_ex), fused_layer_ops(layer, enabled=self.fused):
                 for i, (h, kw, rest) in enumerate(self.cache):
                     self.cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
         mark("propagate")

@@ -7,7 +7,10 @@ with identical weights; against the reference's own oneshot run
 and the quantized model's final hidden-state error is within 5% of the
 reference's.  Round-to-nearest (``QuantizationModifier``) under DDP splits
 the modules across the ranks and broadcasts their qparams: both ranks must
-hold exactly the single-GPU qparams.  Needs two GPUs; skipped otherwise."""
+hold exactly the single-GPU qparams.  The 2-layer Qwen3-MoE (all-expert
+calibration, experts' down projections owned by ranks and solved in
+batches): both ranks end with identical weights and the final hidden-state
+error within 5% of the reference's.  Needs two GPUs; skipped otherwise."""
 import datetime
 import os
 import socket
@@ -94,6 +97,47 @@ def _rtn_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
+def _moe_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from llmcompressor_b200 import moe
+        from llmcompressor_b200 import oneshot as O
+        from llmcompressor_b200 import synthetic
+
+        model = synthetic.random_qwen3_moe("c3tiny")
+        moe.linearize_experts(model)
+        model = model.to(dev)
+        ids = synthetic.calibration_tokens("c3tiny")
+        before = moe.STACKED_CALLS
+        O.oneshot(model, ids, recipe=O.GPTQModifier(targets="Linear", scheme="W4A16",
+                                                     ignore=["lm_head", "re:.*mlp.gate$"], actorder=None),
+                  num_calibration_samples=len(ids))
+        torch.cuda.synchronize()
+        sums = torch.stack([m.weight.detach().double().sum() for n, m in sorted(model.named_modules())
+                            if hasattr(m, "weight_scale")])
+        lo, hi = sums.clone(), sums.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        out = {"same": bool(torch.equal(lo, hi)), "stacked": moe.STACKED_CALLS - before}
+        if rank == 0:
+            fp = synthetic.random_qwen3_moe("c3tiny").to(dev)
+            with torch.no_grad():
+                hq = model.model(ids[:4].to(dev)).last_hidden_state.float()
+                hf = fp.model(ids[:4].to(dev)).last_hidden_state.float()
+            out["hidden_rel_err"] = (torch.linalg.norm((hq - hf).reshape(4, -1), dim=1)
+                                     / torch.linalg.norm(hf.reshape(4, -1), dim=1)).cpu().numpy()
+        q.put((rank, "ok", out))
+    except Exception as e:
+        q.put((rank, f"error: {type(e).__name__}: {e}", None))
+    finally:
+        dist.destroy_process_group()
+
+
 def _spawn(target, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -156,3 +200,16 @@ def test_two_rank_oneshot_c1():
         assert agree >= 0.99, (n, agree)
     theirs = ref["hidden_rel_err"]
     assert np.all(np.abs(out["hidden_rel_err"] - theirs) <= 0.05 * theirs), (out["hidden_rel_err"], theirs)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_rank_oneshot_moe():
+    from golden_io import load
+
+    got = _spawn(_moe_worker)
+    assert all(v[0] == "ok" for v in got.values()), {r: v[0] for r, v in got.items()}
+    assert got[0][1]["same"] and got[1][1]["same"]
+    assert got[0][1]["stacked"] > 0
+    theirs = load("oneshot_c3tiny")["hidden_rel_err"]
+    ours = got[0][1]["hidden_rel_err"]
+    assert np.all(np.abs(ours - theirs) <= 0.05 * theirs), (ours, theirs)
