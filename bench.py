@@ -233,7 +233,7 @@ def run_ours(args, rank, world, device):
     }
     if args.e2e:
         out["e2e"] = run_e2e(args, rank, world, device)
-    if args.c3 and world == 1:
+    if args.c3:
         out["c3"] = run_c3(args, rank, world, device)
     return out
 

@@ -178,6 +178,48 @@ def _mlp_forward(self, x):
     return self.down_proj(self.act_fn(g) * u)
 
 
+# While a list is set here, decoder layers whose MLP can defer stop before
+# the down projection: they append (mlp, act, residual) and return None, and
+# the caller finishes them later with ``finish_deferred`` (the propagation
+# pass runs the layer's other GEMMs while the down projection is still being
+# quantized).
+_DEFER: list | None = None
+
+
+@contextlib.contextmanager
+def defer_down(store: list):
+    """Within the block, layers with fused forwards whose MLP can defer
+    (``deferrable_down``) put their down projection's input into ``store``
+    instead of finishing."""
+    global _DEFER
+    prev, _DEFER = _DEFER, store
+    try:
+        yield
+    finally:
+        _DEFER = prev
+
+
+def deferrable_down(layer: torch.nn.Module) -> torch.nn.Module | None:
+    """The down projection a decoder layer can defer (a Llama-family layer
+    and SiLU MLP the fused forwards take, no hooks on the MLP or the down
+    projection), else None."""
+    mlp = getattr(layer, "mlp", None)
+    if (mlp is None or not _module_classes(layer, LAYER_CLASSES) or not _module_classes(mlp, MLP_CLASSES)
+            or not _silu(getattr(mlp, "act_fn", None))):
+        return None
+    down = getattr(mlp, "down_proj", None)
+    if down is None or _hooked(mlp) or _hooked(down):
+        return None
+    return down
+
+
+def finish_deferred(item) -> torch.Tensor:
+    """The layer output of a deferred (mlp, act, residual): residual +
+    down_proj(act), as the decoder layer adds it."""
+    mlp, act, residual = item
+    return residual + mlp.down_proj(act)
+
+
 def _layer_forward(self, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
                    use_cache=False, position_embeddings=None, **kwargs):
     """LlamaDecoderLayer.forward with the post-attention residual add fused
@@ -193,7 +235,18 @@ def _layer_forward(self, hidden_states, attention_mask=None, position_ids=None, 
     else:
         residual = residual + h
         h = norm(residual)
-    h = self.mlp(h)
+    mlp = self.mlp
+    if _DEFER is not None and mlp.__dict__.get("forward") is not None and deferrable_down(self) is not None:
+        g = mlp.gate_proj(h)
+        u = mlp.up_proj(h)
+        if (g.dtype == u.dtype == torch.bfloat16 and g.shape == u.shape and g.is_contiguous()
+                and u.is_contiguous() and g.numel() % 8 == 0 and _aligned(g, u)):
+            act = silu_mul(g, u)
+        else:
+            act = mlp.act_fn(g) * u
+        _DEFER.append((mlp, act, residual))
+        return None
+    h = mlp(h)
     return residual + h
 
 

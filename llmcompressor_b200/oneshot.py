@@ -45,7 +45,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib, gptq, moe, ops
-from .layer_forward import fused_layer_ops
+from .layer_forward import deferrable_down, defer_down, finish_deferred, fused_layer_ops
 
 __all__ = ["oneshot", "GPTQModifier", "QuantizationModifier", "OneshotStats"]
 
@@ -502,10 +502,12 @@ class _GroupView:
         return self.H, torch.full((), float(self.parent.samples), dtype=torch.float32, device=self.H.device)
 
 
-def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, stats: OneshotStats) -> None:
+def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, stats: OneshotStats,
+                 defer: set | None = None) -> list:
     """Factor each group's Hessian once and quantize its modules; groups run
     concurrently on side streams (largest Hessian first), the caller's stream
-    waits for all of them."""
+    waits for all of them -- except the groups whose modules are all in
+    ``defer``: their completion events are returned instead."""
     from .pipeline import _side_streams
 
     dev = next(iter(cal.modules.values())).weight.device
@@ -513,7 +515,7 @@ def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, st
     jobs, singles = _expert_batches(cal, found)
     order = sorted(singles, key=lambda g: -cal.hess[g].d)
     streams = _side_streams(dev, max(1, min(MAX_SIDE_STREAMS, len(order) + len(jobs))))
-    done = []
+    done, deferred = [], []
     results = []
     for j, (gs, names, mods, qa) in enumerate(jobs):
         # experts' down projections: one batched solve over their Hessians
@@ -551,15 +553,17 @@ def _solve_layer(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, st
                 results.append((nm, loss, hinv))
             ev = torch.cuda.Event()
             ev.record(st)
-            done.append(ev)
+            (deferred if defer and set(names) <= defer else done).append(ev)
         cal.hess[g] = None  # release the Hessian buffers with the stream's work
     for ev in done:
         main.wait_event(ev)
     for nm, loss, hinv in results:
         stats.losses[nm] = (loss, hinv)
+    return deferred
 
 
 MAX_SIDE_STREAMS = 8  # concurrent solve streams (an MoE layer has one Hessian group per expert)
+DEFER_BYTES = 8 << 30  # down-projection inputs held while the down projection's solve finishes
 
 
 def _expert_batches(cal: _LayerCalibration, found: dict):
@@ -604,7 +608,7 @@ def _check_losses(stats: OneshotStats) -> None:
 
 # ------------------------------------------------------------------ multi-GPU solve
 def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifier, stats: OneshotStats,
-                      rank: int, ws: int) -> None:
+                      rank: int, ws: int, defer: set | None = None) -> list:
     """The multi-rank form of ``_solve_layer`` (the reference's
     ``compress_modules`` under DDP, S/modifiers/gptq/base.py:291-321,603-645,
     restructured): every shared Hessian is summed onto an owner rank chosen by
@@ -633,7 +637,7 @@ def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifie
     cal.hess = [cal.hess[g] for g in sorted(singles)]
     ng = len(cal.groups)
     if ng == 0:
-        return
+        return []
     # pinned staging: a pageable host-to-device copy would wait for the stream
     counts = torch.tensor([float(cal.hess[g].samples) for g in range(ng)], dtype=torch.float64).pin_memory()
     counts = counts.to(dev, non_blocking=True)
@@ -647,6 +651,7 @@ def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifie
     streams = _side_streams(dev, nst)
     red = {g: dist.reduce(Hs[g], dst=owners[keys[g]], async_op=True) for g in order}
     invs = {}
+    done, deferred = [], []
     for i, g in enumerate(order):
         st = streams[(ng - 1 - i) % nst]  # the largest Hessian (the critical path) gets the high-priority stream
         st.wait_stream(main)
@@ -670,9 +675,13 @@ def _solve_layer_dist(cal: _LayerCalibration, found: dict, modifier: GPTQModifie
                 inv.hinv_t = inv.hinv.t().contiguous()
             invs[g] = inv
             _solve_group_rows(cal, g, found, modifier, stats, inv, rank, ws, dev)
+            ev = torch.cuda.Event()
+            ev.record(st)
+            (deferred if defer and set(names) <= defer else done).append(ev)
         cal.hess[g] = None
-    for st in streams[:nst]:
-        main.wait_stream(st)
+    for ev in done:
+        main.wait_event(ev)
+    return deferred
 
 
 def _solve_experts_dist(cal, job, modifier, stats, rank: int, ws: int, dev) -> None:
@@ -866,6 +875,8 @@ class SequentialRunner:
                 phases.append((name, e))
 
         layer = self.layers[li]
+        will_propagate = propagate if propagate is not None else li + 1 < len(self.layers)
+        pending: list = []
         mark("start")
         if self.offload:
             self._onload(layer)
@@ -878,24 +889,50 @@ class SequentialRunner:
                     cal.run(layer, h, rest, kw)
             cal.remove()
             mark("calibrate")
+            # the down projection's solve may finish behind the first batches'
+            # propagation up to their down projections (deferred below)
+            down = deferrable_down(layer) if self.fused and will_propagate else None
+            defer = {self._name_of[id(down)]} if down is not None and id(down) in self._name_of else None
             if self.ws > 1:
-                _solve_layer_dist(cal, self.gptq_found, self.modifier, self.stats, self.rank, self.ws)
+                pending = _solve_layer_dist(cal, self.gptq_found, self.modifier, self.stats, self.rank, self.ws,
+                                            defer)
             else:
-                _solve_layer(cal, self.gptq_found, self.modifier, self.stats)
+                pending = _solve_layer(cal, self.gptq_found, self.modifier, self.stats, defer)
             mark("solve")
         mods = set(id(m) for m in layer.modules())
         rl = {n: v for n, v in self.rtn_found.items() if id(v[0]) in mods}
         if rl:
             _rtn(rl)
-        if propagate if propagate is not None else li + 1 < len(self.layers):
+        main = torch.cuda.current_stream()
+        if will_propagate:
             # propagate: the quantized layer's outputs are the next layer's inputs.
             # The reference keeps MoE layers in all-expert mode here too, whose
             # output keeps only the routed tokens' expert outputs: the routed
             # forward gives the same sum without the unrouted experts' work.
             all_ex = self.all_experts and not self.routed_propagation
             with moe.calibrate_all_experts(all_ex), fused_layer_ops(layer, enabled=self.fused):
-                for i, (h, kw, rest) in enumerate(self.cache):
+                start = 0
+                if pending:
+                    # the first batches up to the down projection while its
+                    # solve finishes, then their down projections
+                    h0 = self.cache[0][0]
+                    per = (h0.numel() // h0.shape[-1]) * down.in_features * h0.element_size()
+                    start = min(len(self.cache), max(1, DEFER_BYTES // per))
+                    store: list = []
+                    with defer_down(store):
+                        outs = [layer(h, *rest, **kw) for (h, kw, rest) in self.cache[:start]]
+                    for ev in pending:
+                        main.wait_event(ev)
+                    it = iter(store)
+                    for i, o in enumerate(outs):
+                        _, kw, rest = self.cache[i]
+                        self.cache[i] = (finish_deferred(next(it)) if o is None else _layer_out(o), kw, rest)
+                    del store, outs
+                for i in range(start, len(self.cache)):
+                    h, kw, rest = self.cache[i]
                     self.cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
+        for ev in pending:
+            main.wait_event(ev)
         mark("propagate")
         if self.offload:
             self._offload(layer)

@@ -149,3 +149,22 @@ def test_qwen3_moe_layer():
     ids = synthetic.calibration_tokens("c3tiny")[:4].cuda()
     with moe.calibrate_all_experts(True):
         _compare_layer(model, ids)
+
+
+def test_deferred_down_projection_is_the_same_output():
+    """The propagation pass may stop a layer before its down projection
+    (``defer_down``) and finish it later (``finish_deferred``): the same
+    bits as the whole fused forward."""
+    model = synthetic.random_llama("c1", device="cuda")
+    layer = model.model.layers[1]
+    ids = synthetic.calibration_tokens("c1")[:4].cuda()
+    args, kwargs = _layer_inputs(model, ids)
+    assert LF.deferrable_down(layer) is layer.mlp.down_proj
+    with torch.no_grad(), LF.fused_layer_ops(layer):
+        whole = layer(*args, **kwargs)
+        store = []
+        with LF.defer_down(store):
+            assert layer(*args, **kwargs) is None
+        late = LF.finish_deferred(store[0])
+    whole = whole[0] if isinstance(whole, tuple) else whole
+    assert torch.equal(late, whole)
