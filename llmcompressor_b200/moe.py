@@ -43,7 +43,8 @@ import contextlib
 import torch
 import torch.nn.functional as F
 
-__all__ = ["ExpertMLP", "LinearExperts", "linearize_experts", "calibrate_all_experts", "all_experts_enabled"]
+__all__ = ["ExpertMLP", "LinearExperts", "linearize_experts", "calibrate_all_experts", "all_experts_enabled",
+           "release_stacked"]
 
 _ALL_EXPERTS = False
 
@@ -82,6 +83,12 @@ class ExpertMLP(torch.nn.Module):
 # the stacked weights of one experts module at a time: (owner id, key, (Wg, Wu, Wd))
 _STACK: dict = {}
 STACKED_CALLS = 0  # forwards that took the stacked all-expert form (tests read it)
+
+
+def release_stacked() -> None:
+    """Drop the cached stacked expert weights (the pipeline calls it when a
+    layer is done)."""
+    _STACK.clear()
 
 
 def _hooked(m: torch.nn.Module) -> bool:

@@ -933,6 +933,7 @@ class SequentialRunner:
                     self.cache[i] = (_layer_out(layer(h, *rest, **kw)), kw, rest)
         for ev in pending:
             main.wait_event(ev)
+        moe.release_stacked()  # this layer's stacked expert weights, if any
         mark("propagate")
         if self.offload:
             self._offload(layer)
