@@ -135,7 +135,7 @@ def build_runner(args, rank, world, device, on_host: bool = False):
 
     layers = args.layers or CFG["layers"]
     model = synthetic.random_llama("llama3_8b", device=device, init_device=device, num_hidden_layers=layers)
-    ids = synthetic.calibration_tokens("llama3_8b", n=CFG["samples"], seq_len=CFG["seq"])
+    ids = synthetic.calibration_tokens("llama3_8b", n=args.samples or CFG["samples"], seq_len=CFG["seq"])
     s0, s1 = row_range(ids.shape[0], rank, world)
     batches = O._calibration_batches(ids[s0:s1], s1 - s0, CHUNK, device)
     if on_host:
@@ -676,6 +676,9 @@ def main():
     ap.add_argument("--c3-steps", type=int, default=2)
     ap.add_argument("--c3-warmup", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--samples", type=int, default=0,
+                    help="calibration samples of the C2 leg (0: 512); fewer only for profiling captures -- "
+                         "a value with fewer samples is not the benchmark's")
     ap.add_argument("--eager-forward", dest="fused", action="store_false",
                     help="run the decoder layers' HF forwards as they are (no fused elementwise kernels)")
     args = ap.parse_args()
@@ -735,9 +738,10 @@ def main():
         "data": "synthetic (seeded random weights and uniform random token ids)",
         "config": {
             "workload": "C2: oneshot GPTQ W4A16 g128 (actorder off, damp 0.01), Llama-3-8B shape, "
-                        "512x2048 calibration tokens, sequential pipeline incl. decoder forward passes",
+                        f"{args.samples or CFG['samples']}x2048 calibration tokens, sequential pipeline incl. "
+                        "decoder forward passes",
             "layers_in_model": L, "layers_timed": args.steps, "hidden": CFG["hidden"],
-            "intermediate": CFG["intermediate"], "calibration_tokens": CFG["samples"] * CFG["seq"],
+            "intermediate": CFG["intermediate"], "calibration_tokens": (args.samples or CFG["samples"]) * CFG["seq"],
             "forward_batch_tokens": CHUNK,
             "value_formula": "capture + layers x mean timed layer step",
             "capture_s": res["capture_ms"] * 1e-3,
