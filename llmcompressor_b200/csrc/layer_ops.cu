@@ -30,6 +30,22 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
   return (uint32_t)f_to_bf16(lo) | ((uint32_t)f_to_bf16(hi) << 16);
 }
 
+// bf16(silu(x)) = bf16(x / (1 + expf(-x))) for a bf16 value x, as the eager
+// op rounds it (float32 quotient, then bf16).  The quotient comes from the
+// approximate reciprocal (rcp.approx.f32, within one unit in the last place)
+// times x, within a few float32 units of the correctly rounded quotient; its bf16 rounding can differ from that of the correctly
+// rounded quotient only where the quotient lies within those few units of a
+// bf16 rounding midpoint (low 16 bits near 0x8000) -- there the IEEE
+// division decides.  Zeros, infinities and NaNs come out as the division's.
+__device__ __forceinline__ float silu_bf16(float x) {
+  const float d = 1.0f + expf(-x);
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
+  const float q = x * r;
+  if ((__float_as_uint(q) & 0xFFFFu) - 0x7FF8u < 16u) return rbf(__fdiv_rn(x, d));
+  return rbf(q);
+}
+
 // RMSNorm over rows of `cols` values (cols % 8 == 0); TPR threads per row
 // (a power of two <= 32; several rows per warp when TPR < 32).  With a
 // residual: h = bf16(residual + x) is written to res_out and normalised.
@@ -138,8 +154,7 @@ __global__ void __launch_bounds__(256) k_silu_mul(const uint4* __restrict__ g, c
   uint32_t o[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const float x0 = lo_f(A[k]), x1 = hi_f(A[k]);
-    const float s0 = rbf(x0 / (1.0f + expf(-x0))), s1 = rbf(x1 / (1.0f + expf(-x1)));
+    const float s0 = silu_bf16(lo_f(A[k])), s1 = silu_bf16(hi_f(A[k]));
     o[k] = pack_bf2(s0 * lo_f(B[k]), s1 * hi_f(B[k]));
   }
   out[i] = make_uint4(o[0], o[1], o[2], o[3]);
@@ -167,8 +182,7 @@ __global__ void __launch_bounds__(256) k_silu_mul_scaled(const uint4* __restrict
     uint32_t o[4], os[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float x0 = lo_f(A[k]), x1 = hi_f(A[k]);
-      const float s0 = rbf(x0 / (1.0f + expf(-x0))), s1 = rbf(x1 / (1.0f + expf(-x1)));
+      const float s0 = silu_bf16(lo_f(A[k])), s1 = silu_bf16(hi_f(A[k]));
       const float y0 = rbf(s0 * lo_f(B[k])), y1 = rbf(s1 * hi_f(B[k]));
       o[k] = pack_bf2(y0, y1);
       os[k] = s == 0.0f ? 0u : pack_bf2(y0 * s, y1 * s);

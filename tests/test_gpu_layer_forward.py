@@ -52,6 +52,27 @@ def test_rotary_bit_identical():
         assert torch.equal(fq, rq) and torch.equal(fk, rk), (B, S, H, D)
 
 
+def _same_bits_or_nan(ours, ref):
+    nan = torch.isnan(ref)
+    assert torch.equal(torch.isnan(ours), nan)
+    assert torch.equal(ours[~nan].view(torch.int16), ref[~nan].view(torch.int16))
+
+
+def test_silu_mul_every_bf16_gate():
+    """Every bf16 bit pattern as the gate (zeros, subnormals, infinities,
+    NaNs), times 1 and times random up values: the same bits as torch's
+    SiLU and product (NaN as NaN)."""
+    g = torch.arange(-32768, 32768, dtype=torch.int32, device="cuda").to(torch.int16).view(torch.bfloat16)
+    one = torch.ones_like(g)
+    _same_bits_or_nan(LF.silu_mul(g, one), torch.nn.functional.silu(g) * one)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    u = (torch.randn(g.numel(), device="cuda", generator=gen) * 3).to(torch.bfloat16)
+    _same_bits_or_nan(LF.silu_mul(g, u), torch.nn.functional.silu(g) * u)
+    # the stacked-expert kernel (act output) on the same values
+    act, _ = LF.silu_mul_scaled(g.view(256, 256), u.view(256, 256), 64, None, act=True, scaled=False)
+    _same_bits_or_nan(act.reshape(-1), torch.nn.functional.silu(g) * u)
+
+
 def test_silu_mul_bit_identical():
     g = torch.Generator(device="cuda").manual_seed(1)
     for n in (8, 4096 * 37, 14336 * 300):
