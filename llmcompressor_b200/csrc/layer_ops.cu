@@ -323,6 +323,13 @@ int llmc_silu_mul_scaled_bf16(const void* gate, const void* up, int64_t rows, in
   if (cols % 8 || group % 8 || cols % group || !al16(gate) || !al16(up) || (out && !al16(out)) ||
       (out_scaled && !al16(out_scaled)) || (weights && weights_ld < cols / group))
     return LLMC_EINVAL_SHAPE;
+  if (!out_scaled) {  // the plain product over the flat tensor
+    const int64_t n8 = rows * cols / 8;
+    k_silu_mul<<<(unsigned)((n8 + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint4*)gate, (const uint4*)up,
+                                                                              n8, (uint4*)out);
+    llmc::note_launch();
+    return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
+  }
   if (cols / 8 >= (1ll << 31)) return LLMC_EINVAL_SHAPE;
   const int cols8 = (int)(cols / 8);
   const dim3 grid((unsigned)((cols8 + 255) / 256), (unsigned)std::min<int64_t>(rows, 65535));
