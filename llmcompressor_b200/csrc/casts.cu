@@ -85,19 +85,6 @@ __device__ __forceinline__ uint32_t quant_code(float x, const ElemQ& e) {
   return (uint32_t)(int32_t)rintf(q);  // INT8 / PACK_INT32: signed code
 }
 
-// x / y correctly rounded from r = RN(1/y) (Markstein's correction: one fma
-// residual, one fma step) while the quotient stays in the normal range;
-// IEEE division otherwise (zeros, subnormals, huge values).
-__device__ __forceinline__ float div_by_recip(float x, float y, float r) {
-  const float q0 = __fmul_rn(x, r);
-  const float aq = fabsf(q0);
-  if (aq > 1.0e-30f && aq < 1.0e30f && fabsf(r) > 1.0e-30f && fabsf(r) < 1.0e30f) {
-    const float e = __fmaf_rn(-q0, y, x);
-    return __fmaf_rn(e, r, q0);
-  }
-  return __fdiv_rn(x, y);
-}
-
 // NVFP4 group scale (group_qparams for symmetric E2M1 with a float32 global
 // scale and FP8 scales): rbf(amax / 6) * gs rounded to E4M3 (0 -> 0.125),
 // with the division by 6 as a multiplication by RN(1/6) plus correction.
@@ -285,8 +272,17 @@ __device__ __forceinline__ Rect group_rect(const CastParams& p, int64_t gi) {
   if (a.strategy == LLMC_STRAT_TENSOR) { R.r0 = 0; R.r1 = p.rows; R.c0 = 0; R.c1 = p.cols; }
   else if (a.strategy == LLMC_STRAT_CHANNEL) { R.r0 = gi; R.r1 = gi + 1; R.c0 = 0; R.c1 = p.cols; }
   else if (a.strategy == LLMC_STRAT_BLOCK) {
-    int64_t bc_n = (p.cols + a.bw - 1) / a.bw;
-    int64_t br = gi / bc_n, bc = gi % bc_n;
+    int64_t br, bc;
+    if (gi < (1ll << 31) && p.cols < (1ll << 30) && a.bw < (1ll << 30)) {  // 32-bit divisions are far cheaper
+      const uint32_t bc_n = ((uint32_t)p.cols + (uint32_t)a.bw - 1u) / (uint32_t)a.bw;
+      const uint32_t q = (uint32_t)gi / bc_n;
+      br = q;
+      bc = (uint32_t)gi - q * bc_n;
+    } else {
+      const int64_t bc_n = (p.cols + a.bw - 1) / a.bw;
+      br = gi / bc_n;
+      bc = gi % bc_n;
+    }
     R.r0 = br * a.bh; R.r1 = min(p.rows, R.r0 + a.bh);
     R.c0 = bc * a.bw; R.c1 = min(p.cols, R.c0 + a.bw);
   } else {
@@ -462,6 +458,17 @@ __device__ __forceinline__ uint64_t quot2(uint32_t w, uint64_t nr2, uint64_t s2)
       : "=l"(q) : "r"(w), "l"(nr2), "l"(s2));
   return q;
 }
+// The same quotients for outputs where the sign of a zero code does not
+// matter (integer codes): q0 = x * r, e = q0 * (-s) + x, q = q0 + e * r
+// (the same correctly rounded quotient; x = -0 gives +0).  ns2 = (-s, -s).
+__device__ __forceinline__ uint64_t quot2_int(uint32_t w, uint64_t r2, uint64_t ns2) {
+  uint64_t q;
+  asm("{\n\t.reg .b32 lo, hi;\n\t.reg .b64 x, q0, e;\n\t"
+      "shl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xFFFF0000;\n\tmov.b64 x, {lo, hi};\n\t"
+      "mul.rn.f32x2 q0, x, %2;\n\tfma.rn.f32x2 e, q0, %3, x;\n\tfma.rn.f32x2 %0, e, %2, q0;\n\t}"
+      : "=l"(q) : "r"(w), "l"(r2), "l"(ns2));
+  return q;
+}
 __device__ __forceinline__ uint32_t bf2_of(uint64_t q) {
   uint32_t d;
   asm("{\n\t.reg .b32 lo, hi;\n\tmov.b64 {lo, hi}, %1;\n\tcvt.rn.bf16x2.f32 %0, hi, lo;\n\t}" : "=r"(d) : "l"(q));
@@ -523,6 +530,7 @@ __device__ __forceinline__ void st_v4(void* p, const uint32_t* w) {
 // Per-group divisor in the forms the pair routines take.
 struct GQ {
   uint64_t nr2, s2;  // (-r, -r), (s, s)
+  uint64_t r2, ns2;  // (r, r), (-s, -s)
   float s, zp;
   uint32_t zp2;      // zero point as bf16x2
   bool fast, has_zp, f32q;
@@ -533,6 +541,8 @@ __device__ __forceinline__ GQ to_gq(const ElemQ& e) {
   g.fast = e.fast && e.s > 0.0f;  // the pair form keeps zero signs for positive scales only
   g.nr2 = f2_pair(-e.r, -e.r);
   g.s2 = f2_pair(e.s, e.s);
+  g.r2 = f2_pair(e.r, e.r);
+  g.ns2 = f2_pair(-e.s, -e.s);
   g.zp2 = e.has_zp ? bf2_dup(e.zp) : 0u;
   return g;
 }
@@ -551,9 +561,11 @@ __device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, floa
   constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
   if (!F32Q) {
     uint32_t Q[NW];
+    constexpr bool INT_CODES = (FMT == LLMC_FMT_PACK_INT32 || FMT == LLMC_FMT_INT8);
     if (g.fast) {
 #pragma unroll
-      for (int k = 0; k < NW; ++k) Q[k] = bf2_of(quot2(w[k], g.nr2, g.s2));
+      for (int k = 0; k < NW; ++k)
+        Q[k] = bf2_of(INT_CODES ? quot2_int(w[k], g.r2, g.ns2) : quot2(w[k], g.nr2, g.s2));
       if (CHECK) {
 #pragma unroll
         for (int k = 0; k < NW; ++k)
@@ -678,6 +690,16 @@ __device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, floa
   }
 }
 
+// max |x| over the bf16 values in w[0..NW) (NaNs skipped; 0 for none): what
+// a symmetric scheme's scale needs of min(min, 0) and max(max, 0).
+template <int NW>
+__device__ __forceinline__ float absmax_words(const uint32_t* w) {
+  uint32_t M = 0u;
+#pragma unroll
+  for (int k = 0; k < NW; ++k) asm("max.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(M) : "r"(w[k]));
+  return fmaxf(fabsf(bf_lo(M)), fabsf(bf_hi(M)));
+}
+
 // min / max of the bf16 values in w[0..NW)
 template <int NW>
 __device__ __forceinline__ void minmax_words(const uint32_t* w, float& mn, float& mx) {
@@ -707,7 +729,16 @@ __device__ __forceinline__ void stream_span(const CastParams& p, int64_t e0, boo
   const int lane = threadIdx.x & 31;
   const int64_t g0 = GROUP ? e0 / (GROUP ? GROUP : 1) : 0;
   float mns[GPL], mxs[GPL];
-  if (MODE != MODE_GIVEN) {
+  if (MODE == MODE_FUSED && p.a.symmetric) {
+    // a symmetric scale reads max(|min(mn, 0)|, |max(mx, 0)|) = max |x| only
+#pragma unroll
+    for (int j = 0; j < GPL; ++j) {
+      mxs[j] = absmax_words<NW>(w + j * NW);
+#pragma unroll
+      for (int o = 1; o < LPG; o <<= 1) mxs[j] = fmaxf(mxs[j], __shfl_xor_sync(0xffffffffu, mxs[j], o));
+      mns[j] = 0.0f;
+    }
+  } else if (MODE != MODE_GIVEN) {
 #pragma unroll
     for (int j = 0; j < GPL; ++j) {
       minmax_words<NW>(w + j * NW, mns[j], mxs[j]);
@@ -1093,6 +1124,15 @@ struct CastJob {
   void* out;
   void* scale_out;
   int8_t* zp_out;
+  // k_stream_batch: the pointers rebased to the batch's global element
+  // numbering (moved back by the elements before the job, first * 1024), so
+  // global element e addresses the job's data directly; the job's elements
+  // end at lim.  Set on the host (launch_batch_fmt).
+  const uint16_t* w_rb;
+  void* out_rb;
+  void* scale_rb;
+  int8_t* zp_rb;
+  int64_t lim;
 };
 struct CastBatch {
   CastParams base;  // arguments, format and mode shared by the jobs
@@ -1121,25 +1161,31 @@ template <int FMT, int BITS, int GROUP>
 __global__ void __launch_bounds__(256, stream_ctas<GROUP, MODE_FUSED>()) k_stream_batch(const __grid_constant__ CastBatch b) {
   const int lane = threadIdx.x & 31;
   // job cursors: units arrive in increasing order, so the job index only
-  // moves forward (one comparison per unit instead of a search)
+  // moves forward; a warp compares each unit with the next job's first unit
+  // and otherwise reads the job's rebased pointers (no per-unit arithmetic)
   const int64_t u0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int j0 = u0 < b.units ? find_job(b, u0) : 0;
-  int js = j0, jp = j0;
-  auto advance = [&](int& j, int64_t u) {
-    while (j + 1 < b.njobs && b.job[j + 1].first <= u) ++j;
-  };
+  int js = u0 < b.units ? find_job(b, u0) : 0, jp = js;
+  auto next_first = [&](int j) { return j + 1 < b.njobs ? b.job[j + 1].first : INT64_MAX; };
+  int64_t snext = next_first(js), pnext = snext;
   auto src = [&](int64_t u, const uint16_t*& ptr) {
-    advance(js, u);
-    const CastJob& jb = b.job[js];
-    const int64_t e0 = ((u - jb.first) << 10) + lane * 32;
-    ptr = jb.w + e0;
-    return e0 < jb.rows * jb.cols;
+    if (u >= snext) {
+      while (js + 1 < b.njobs && b.job[js + 1].first <= u) ++js;
+      snext = next_first(js);
+    }
+    const int64_t e0 = (u << 10) + lane * 32;
+    ptr = b.job[js].w_rb + e0;
+    return e0 < b.job[js].lim;
   };
   auto proc = [&](int64_t u, const uint32_t* w) {
-    advance(jp, u);
-    const CastParams p = job_params(b, jp);
-    const int64_t e0 = ((u - b.job[jp].first) << 10) + lane * 32;
-    stream_span<FMT, BITS, GROUP, MODE_FUSED>(p, e0, e0 < p.rows * p.cols, w);
+    if (u >= pnext) {
+      while (jp + 1 < b.njobs && b.job[jp + 1].first <= u) ++jp;
+      pnext = next_first(jp);
+    }
+    const CastJob& jb = b.job[jp];
+    CastParams p = b.base;
+    p.gs = jb.gs; p.out = jb.out_rb; p.scale_out = jb.scale_rb; p.zp_out = jb.zp_rb;
+    const int64_t e0 = (u << 10) + lane * 32;
+    stream_span<FMT, BITS, GROUP, MODE_FUSED>(p, e0, e0 < jb.lim, w);
   };
   span_loop<GROUP>(b.units, src, proc);
 }
@@ -1256,16 +1302,30 @@ __global__ void __launch_bounds__(256, 3) k_block_tma(const __grid_constant__ Ca
     ElemQ e;
     float s_store = 0.f, zp_store = 0.f;
     if (MODE != MODE_GIVEN) {
-      uint32_t M = 0xFF80FF80u, mn2 = 0x7F807F80u;
+      float mx, mn;
+      if (MODE == MODE_FUSED && b.base.a.symmetric) {
+        // a symmetric scale reads max |x| only
+        uint32_t v8[8 * 4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint4 v = stage[j * 256];
-        M = hmax2(hmax2(M, v.x), hmax2(v.y, hmax2(v.z, v.w)));
-        mn2 = hmin2(hmin2(mn2, v.x), hmin2(v.y, hmin2(v.z, v.w)));
+        for (int j = 0; j < 8; ++j) {
+          const uint4 v = stage[j * 256];
+          v8[4 * j] = v.x; v8[4 * j + 1] = v.y; v8[4 * j + 2] = v.z; v8[4 * j + 3] = v.w;
+        }
+        mx = block_reduce(absmax_words<32>(v8), true, sh);
+        mn = 0.0f;
+      } else {
+        uint32_t M = 0xFF80FF80u, mn2 = 0x7F807F80u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 v = stage[j * 256];
+          M = hmax2(hmax2(M, v.x), hmax2(v.y, hmax2(v.z, v.w)));
+          mn2 = hmin2(hmin2(mn2, v.x), hmin2(v.y, hmin2(v.z, v.w)));
+        }
+        mx = fmaxf(bf_lo(M), bf_hi(M));
+        mn = fminf(bf_lo(mn2), bf_hi(mn2));
+        mn = block_reduce(mn, false, sh);
+        mx = block_reduce(mx, true, sh);
       }
-      float mx = fmaxf(bf_lo(M), bf_hi(M)), mn = fminf(bf_lo(mn2), bf_hi(mn2));
-      mn = block_reduce(mn, false, sh);
-      mx = block_reduce(mx, true, sh);
       if (MODE == MODE_STATS) {
         if (t == 0) { p.min_out[gi] = f_to_bf16(mn); p.max_out[gi] = f_to_bf16(mx); }
       } else {
@@ -1689,6 +1749,17 @@ static bool launch_batch_fmt(CastBatch& b, cudaStream_t st) {
     CastJob& j = b.job[i];
     j.first = units;
     if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
+      // rebased pointers for k_stream_batch (integer arithmetic on the
+      // addresses; a rebased pointer is only dereferenced at or past the
+      // job's own start)
+      constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+      constexpr int64_t SCALE_BYTES = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) ? 1 : 2;
+      const int64_t off = units * 1024, goff = a.group > 0 ? off / a.group : 0;
+      j.w_rb = (const uint16_t*)((uintptr_t)j.w - (uintptr_t)(off * 2));
+      j.out_rb = (void*)((uintptr_t)j.out - (uintptr_t)(OUT4 ? off / 2 : off));
+      j.scale_rb = (void*)((uintptr_t)j.scale_out - (uintptr_t)(goff * SCALE_BYTES));
+      j.zp_rb = j.zp_out ? (int8_t*)((uintptr_t)j.zp_out - (uintptr_t)goff) : nullptr;
+      j.lim = off + j.rows * j.cols;
       units += (j.rows * j.cols + 1023) / 1024;
     } else {
       CastParams p = b.base;

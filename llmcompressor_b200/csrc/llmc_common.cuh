@@ -50,6 +50,19 @@ __device__ __forceinline__ float bf16_quotient(float x, float s, float r, bool f
   return rbf(__fdiv_rn(x, s));
 }
 
+// x / y correctly rounded from r = RN(1/y) (Markstein's correction: one fma
+// residual, one fma step) while the quotient stays in the normal range;
+// IEEE division otherwise (zeros, subnormals, huge values).
+__device__ __forceinline__ float div_by_recip(float x, float y, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float aq = fabsf(q0);
+  if (aq > 1.0e-30f && aq < 1.0e30f && fabsf(r) > 1.0e-30f && fabsf(r) < 1.0e30f) {
+    const float e = __fmaf_rn(-q0, y, x);
+    return __fmaf_rn(e, r, q0);
+  }
+  return __fdiv_rn(x, y);
+}
+
 // Reciprocal and fast-path flag for a scale; the error bound above needs a
 // normal, finite reciprocal.
 __device__ __forceinline__ float scale_recip(float s, bool* fast) {
@@ -167,10 +180,11 @@ __device__ __forceinline__ float group_qparams(float mn, float mx, const QArgs& 
       uint32_t e = mx_e8m0_from_absmax(mvp, a.bits);
       scale = (float)e;  // the bf16 exponent value, converted below
     } else {
-      scale = R(__fdiv_rn(mvp, br * 0.5f));
+      const float half = br * 0.5f;  // the reciprocal depends on the args only: computed once per kernel
+      scale = R(div_by_recip(mvp, half, __frcp_rn(half)));
     }
   } else {
-    scale = R(__fdiv_rn(R(mx - mn), br));
+    scale = R(div_by_recip(R(mx - mn), br, __frcp_rn(br)));
     zp = R(qmin - R(__fdiv_rn(mn, scale)));
     if (!isnan(zp)) zp = fminf(fmaxf(zp, qmin), qmax);
   }
