@@ -115,7 +115,7 @@ def w4a16_args():
 # dram__bytes_write.sum) at the bench's batch size, and the algorithmic bytes
 # (X once + the lower triangle of H read and written):
 # profiles/k_hessian_pair__d4096_n16384.md, profiles/k_hessian_pair__d14336_n16384_traffic.md
-HESSIAN_TRAFFIC = {4096: 309.1e6 + 41.3e6, 14336: 5961.5e6 + 809.4e6}
+HESSIAN_TRAFFIC = {4096: 267.5e6 + 39.8e6, 14336: 4865.2e6 + 805.8e6}
 
 
 def hessian_algorithmic_bytes(d: int, tokens: int = CHUNK) -> float:
