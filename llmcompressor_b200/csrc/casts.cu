@@ -469,6 +469,12 @@ __device__ __forceinline__ uint64_t quot2_int(uint32_t w, uint64_t r2, uint64_t 
       : "=l"(q) : "r"(w), "l"(r2), "l"(ns2));
   return q;
 }
+// (lo + 0, hi + 0) rounded to nearest: -0 -> +0, everything else unchanged
+__device__ __forceinline__ uint64_t add2_zero(uint64_t v) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(v), "l"(0ull));
+  return d;
+}
 __device__ __forceinline__ uint32_t bf2_of(uint64_t q) {
   uint32_t d;
   asm("{\n\t.reg .b32 lo, hi;\n\tmov.b64 {lo, hi}, %1;\n\tcvt.rn.bf16x2.f32 %0, hi, lo;\n\t}" : "=r"(d) : "l"(q));
@@ -556,8 +562,13 @@ struct OutOf {
 // Codes of the 2*NW bf16 values in w (one parameter group) -> output words o
 // (NW/4 words for 4-bit outputs, NW/2 for 8-bit).  CHECK: scales come from
 // the caller, so a quotient may overflow.
+// sat (NVFP4): every value of the group is finite, so the saturating E2M1
+// conversion does the clamp to [-6, 6] by itself (it differs from fmin/fmax
+// only for NaN).  (For MXFP4 the finiteness test cost more than the clamp it
+// saves: measured 11% slower.)
 template <int FMT, int BITS, bool F32Q, bool CHECK, int NW>
-__device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, float qmin, float qmax, uint32_t* o) {
+__device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, float qmin, float qmax, uint32_t* o,
+                                            bool sat = false) {
   constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
   if (!F32Q) {
     uint32_t Q[NW];
@@ -618,7 +629,7 @@ __device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, floa
         float v[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          uint32_t a = hadd2(hmin2(hmax2(Q[4 * j + k], QMIN2), QMAX2), 0u);  // -0 -> +0
+          const uint32_t a = hadd2(hmin2(hmax2(Q[4 * j + k], QMIN2), QMAX2), 0u);  // -0 -> +0
           v[2 * k] = bf_lo(a);
           v[2 * k + 1] = bf_hi(a);
         }
@@ -630,7 +641,9 @@ __device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, floa
     if (g.fast) {
 #pragma unroll
       for (int k = 0; k < NW; ++k) pair_f2(quot2(w[k], g.nr2, g.s2), f[2 * k], f[2 * k + 1]);
-      if (CHECK) {
+      // an infinite value makes the correction step NaN: NVFP4 groups that are
+      // not all finite take the IEEE quotient there (as the general kernels do)
+      if (CHECK || (FMT == LLMC_FMT_NVFP4 && !sat)) {
 #pragma unroll
         for (int k = 0; k < NW; ++k)
           if (!(fabsf(f[2 * k]) <= 3.4028234663852886e38f && fabsf(f[2 * k + 1]) <= 3.4028234663852886e38f)) {
@@ -650,12 +663,22 @@ __device__ __forceinline__ void quant_group(const uint32_t* w, const GQ& g, floa
       for (int k = 0; k < 2 * NW; ++k) f[k] = f[k] + g.zp;
     }
     if (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) {
+      if (sat) {
 #pragma unroll
-      for (int j = 0; j < NW / 4; ++j) {
-        float v[8];
+        for (int j = 0; j < NW / 4; ++j) {
+          float v[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = fminf(fmaxf(__fadd_rn(f[8 * j + k], 0.0f), qmin), qmax);
-        o[j] = e2m1x8(v);
+          for (int k = 0; k < 4; ++k) pair_f2(add2_zero(f2_pair(f[8 * j + 2 * k], f[8 * j + 2 * k + 1])), v[2 * k], v[2 * k + 1]);
+          o[j] = e2m1x8(v);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < NW / 4; ++j) {
+          float v[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[k] = fminf(fmaxf(__fadd_rn(f[8 * j + k], 0.0f), qmin), qmax);
+          o[j] = e2m1x8(v);
+        }
       }
     } else if (FMT == LLMC_FMT_FP8) {
 #pragma unroll
@@ -700,6 +723,17 @@ __device__ __forceinline__ float absmax_words(const uint32_t* w) {
   return fmaxf(fabsf(bf_lo(M)), fabsf(bf_hi(M)));
 }
 
+// Largest magnitude bit pattern (bits & 0x7FFF) over the bf16 values in
+// w[0..NW): below 0x7F80 when every value is finite, and then the bf16 bits
+// of max |x| (magnitudes order like their bit patterns).
+template <int NW>
+__device__ __forceinline__ uint32_t absmax_bits(const uint32_t* w) {
+  uint32_t M = 0u;
+#pragma unroll
+  for (int k = 0; k < NW; ++k) asm("max.u16x2 %0, %0, %1;" : "+r"(M) : "r"(w[k] & 0x7FFF7FFFu));
+  return max(M & 0xFFFFu, M >> 16);
+}
+
 // min / max of the bf16 values in w[0..NW)
 template <int NW>
 __device__ __forceinline__ void minmax_words(const uint32_t* w, float& mn, float& mx) {
@@ -728,8 +762,25 @@ __device__ __forceinline__ void stream_span(const CastParams& p, int64_t e0, boo
   static_assert(GROUP != 0 || MODE == MODE_GIVEN, "whole-tensor spans take stored qparams");
   const int lane = threadIdx.x & 31;
   const int64_t g0 = GROUP ? e0 / (GROUP ? GROUP : 1) : 0;
+  constexpr bool FP4 = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4);
+  constexpr bool NV = (FMT == LLMC_FMT_NVFP4);
   float mns[GPL], mxs[GPL];
-  if (MODE == MODE_FUSED && p.a.symmetric) {
+  bool sat[GPL];
+#pragma unroll
+  for (int j = 0; j < GPL; ++j) sat[j] = false;
+  static_assert(!FP4 || LPG == 1, "FP4 groups (16 / 32 values) lie within one lane");
+  if (MODE == MODE_FUSED && p.a.symmetric && NV) {
+    // a symmetric scale reads max(|min(mn, 0)|, |max(mx, 0)|) = max |x| only;
+    // the magnitude bit patterns give it and tell whether the group is finite
+#pragma unroll
+    for (int j = 0; j < GPL; ++j) {
+      const uint32_t mb = absmax_bits<NW>(w + j * NW);
+      sat[j] = mb < 0x7F80u;
+      if (sat[j]) mxs[j] = bf16_to_f((uint16_t)mb);
+      else mxs[j] = absmax_words<NW>(w + j * NW);
+      mns[j] = 0.0f;
+    }
+  } else if (MODE == MODE_FUSED && p.a.symmetric) {
     // a symmetric scale reads max(|min(mn, 0)|, |max(mx, 0)|) = max |x| only
 #pragma unroll
     for (int j = 0; j < GPL; ++j) {
@@ -767,9 +818,9 @@ __device__ __forceinline__ void stream_span(const CastParams& p, int64_t e0, boo
     else e = make_elemq_given<FMT>(p, g0 + j);
     GQ g = to_gq(e);
     uint32_t* oj = o + j * (OUT4 ? NW / 4 : NW / 2);
-    if (FMT == LLMC_FMT_NVFP4) quant_group<FMT, BITS, true, MODE == MODE_GIVEN, NW>(w + j * NW, g, qmin, qmax, oj);
+    if (FMT == LLMC_FMT_NVFP4) quant_group<FMT, BITS, true, MODE == MODE_GIVEN, NW>(w + j * NW, g, qmin, qmax, oj, sat[j]);
     else if (MODE == MODE_GIVEN && g.f32q) quant_group<FMT, BITS, true, true, NW>(w + j * NW, g, qmin, qmax, oj);
-    else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, NW>(w + j * NW, g, qmin, qmax, oj);
+    else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, NW>(w + j * NW, g, qmin, qmax, oj, sat[j]);
     if (MODE == MODE_FUSED && (lane % LPG) == 0) store_scale<FMT>(p, g0 + j, s_store, zp_store);
   }
   if (OUT4) st_v4((uint8_t*)p.out + e0 / 2, o);
@@ -779,13 +830,12 @@ __device__ __forceinline__ void stream_span(const CastParams& p, int64_t e0, boo
 // Two ways to keep a warp's next spans in flight while it quantizes one.
 //
 // span_regs: the next span is loaded into registers (double buffer); one span
-// in flight per warp.  Cheapest when the per-group work is short (groups of
-// 64 or 128 values).
+// in flight per warp.  Used for the whole-tensor (TENSOR strategy) pass.
 //
 // span_ring: asynchronous copies into a per-warp ring of NBUF spans in shared
 // memory (2 KB each), NBUF - 1 spans in flight per warp without holding them
-// in registers.  Pays off for groups of 16 / 32 values, whose scale
-// arithmetic per span is longest.  A lane copies and later reads back only
+// in registers, and four CTAs per SM instead of three (measured faster for
+// every group size: W4A16 4.52 -> 4.67 TB/s batched).  A lane copies and later reads back only
 // its own 64 bytes (so no warp barrier is needed); its four 16-byte chunks
 // are stored in an order rotated by lane so that the reads are free of bank
 // conflicts.
@@ -807,7 +857,7 @@ __device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.w
 constexpr int SPAN_WORDS = 512;  // 1024 bf16 values
 constexpr int NBUF = 3;
 template <int GROUP>
-constexpr bool use_ring() { return GROUP == 16 || GROUP == 32; }
+constexpr bool use_ring() { return GROUP == 16 || GROUP == 32 || GROUP == 64 || GROUP == 128; }
 // resident CTAs per SM (the ring takes 48 KB of shared memory per CTA;
 // quantizing with stored qparams needs more than 64 registers a thread)
 template <int GROUP, int MODE>
@@ -1055,11 +1105,9 @@ __global__ void __launch_bounds__(THR, PF ? 2 : (THR == 128 ? (NP <= 4 ? 6 : 4) 
 // shuffles only, no CTA barrier, so many rows are in flight per SM.
 // ------------------------------------------------------------------------
 template <int FMT, int BITS, int MODE, int NPL>
-__global__ void __launch_bounds__(256) k_rowwarp(CastParams p) {
+__device__ __forceinline__ void rowwarp_row(const CastParams& p, int64_t row) {
   constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
   const int lane = threadIdx.x & 31;
-  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (row >= p.rows) return;  // whole warp
   const int64_t pieces = p.cols / 16;
   const uint16_t* src = p.w + row * p.cols;
   uint32_t w[NPL][8];
@@ -1107,6 +1155,13 @@ __global__ void __launch_bounds__(256) k_rowwarp(CastParams p) {
     if (OUT4) *(uint2*)((uint8_t*)p.out + el / 2) = make_uint2(o[0], o[1]);
     else st_v4((uint8_t*)p.out + el, o);
   }
+}
+
+template <int FMT, int BITS, int MODE, int NPL>
+__global__ void __launch_bounds__(256) k_rowwarp(CastParams p) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= p.rows) return;  // whole warp
+  rowwarp_row<FMT, BITS, MODE, NPL>(p, row);
 }
 
 // ------------------------------------------------------------------------
@@ -1188,6 +1243,121 @@ __global__ void __launch_bounds__(256, stream_ctas<GROUP, MODE_FUSED>()) k_strea
     stream_span<FMT, BITS, GROUP, MODE_FUSED>(p, e0, e0 < jb.lim, w);
   };
   span_loop<GROUP>(b.units, src, proc);
+}
+
+// CHANNEL rows of up to 4096 columns across the jobs of a batch: one warp
+// per row as in k_rowwarp (the whole row's loads issued at once, a
+// non-persistent grid); the warp finds its row's job by a search of the job
+// table.
+template <int FMT, int BITS, int NPL>
+__global__ void __launch_bounds__(256) k_rowwarp_batch(const __grid_constant__ CastBatch b) {
+  const int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (u >= b.units) return;  // whole warp
+  const int j = find_job(b, u);
+  rowwarp_row<FMT, BITS, MODE_FUSED, NPL>(job_params(b, j), u - b.job[j].first);
+}
+
+// Group strategies over the flat tensor, NS consecutive 1024-value spans per
+// warp: every load of the warp's spans is issued before the first is
+// quantized, and the grid is not persistent (a warp's 2 KB x NS stay in
+// flight while the SM's other warps compute), the structure of k_rowwarp.
+// Used for single FP4 tensors (groups of 16 / 32), where two spans per warp
+// measured faster than k_stream's ring (NVFP4 4.20 -> 4.57 TB/s on a
+// 28672 x 8192 weight); batches and the other groups measured faster with
+// k_stream / k_stream_batch.
+template <int FMT, int BITS, int GROUP, int MODE, int NS>
+__global__ void __launch_bounds__(256) k_spans(CastParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = p.rows * p.cols;
+  const int64_t u0 = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * NS;
+  uint32_t w[NS][16];
+#pragma unroll
+  for (int k = 0; k < NS; ++k) {
+    const int64_t e0 = ((u0 + k) << 10) + lane * 32;
+    if (e0 < n) {
+      ld_v8(p.w + e0, w[k]);
+      ld_v8(p.w + e0 + 16, w[k] + 8);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[k][i] = 0u;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NS; ++k) {
+    const int64_t e0 = ((u0 + k) << 10) + lane * 32;
+    if ((u0 + k) << 10 >= n) break;  // whole warp
+    stream_span<FMT, BITS, GROUP, MODE>(p, e0, e0 < n, w[k]);
+  }
+}
+
+// Groups of 64 / 128 values with one lane per group: a warp covers 32
+// consecutive groups (2048 / 4096 values), each lane loads its own group
+// (whole 32-byte sectors, so no DRAM bytes are wasted although a load
+// instruction spans 32 sectors) and computes its own group's scale, where the
+// span kernels compute every scale once per lane of the group (2 / 4 times)
+// and combine the statistics by shuffles.  All loads of a warp are issued
+// before the first value is quantized; the grid is not persistent (the
+// structure of k_rowwarp).  src_of(gi, ptr, p) gives group gi's values and
+// parameters (false past the end); FUSED mode only uses these for batches.
+template <int FMT, int BITS, int GROUP, int MODE, class Src>
+__device__ __forceinline__ void lane_group(int64_t gi, Src src_of) {
+  constexpr int NW = GROUP / 2;  // bf16x2 words per group
+  constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
+  static_assert(GROUP == 64 || GROUP == 128, "lane groups of 64 or 128 values");
+  const uint16_t* ptr = nullptr;
+  CastParams p;
+  const bool valid = src_of(gi, ptr, p);
+  uint32_t w[NW];
+  if (valid) {
+#pragma unroll
+    for (int k = 0; k < NW / 8; ++k) ld_v8(ptr + 16 * k, w + 8 * k);
+  }
+  if (!valid) return;
+  ElemQ e;
+  float s_store = 0.f, zp_store = 0.f;
+  if (MODE == MODE_FUSED) {
+    float mn, mx;
+    if (p.a.symmetric) {
+      mx = absmax_words<NW>(w);
+      mn = 0.0f;
+    } else {
+      minmax_words<NW>(w, mn, mx);
+    }
+    e = make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
+  } else {
+    e = make_elemq_given<FMT>(p, gi);
+  }
+  const GQ g = to_gq(e);
+  const float qmin = p.a.qmin(), qmax = p.a.qmax();
+  uint32_t o[OUT4 ? NW / 4 : NW / 2];
+  if (MODE == MODE_GIVEN && g.f32q) quant_group<FMT, BITS, true, true, NW>(w, g, qmin, qmax, o);
+  else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, NW>(w, g, qmin, qmax, o);
+  uint8_t* out = (uint8_t*)p.out + (OUT4 ? gi * (GROUP / 2) : gi * GROUP);
+#pragma unroll
+  for (int k = 0; k < (OUT4 ? NW / 4 : NW / 2) / 4; ++k) st_v4(out + 16 * k, o + 4 * k);
+  if (MODE == MODE_FUSED) store_scale<FMT>(p, gi, s_store, zp_store);
+}
+
+// Batches of groups of 64 / 128 values (W4A16 and other integer group
+// schemes), one lane per group; a unit is a group, numbered across the jobs
+// (CastJob::first counts groups here).  Measured against k_stream_batch on
+// 32 weights of 4096 x 4096: W4A16 4.67 -> 4.80 TB/s (single tensors stay
+// on k_stream, which measured the same).
+template <int FMT, int BITS, int GROUP>
+__global__ void __launch_bounds__(256) k_lanegroup_batch(const __grid_constant__ CastBatch b) {
+  const int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  lane_group<FMT, BITS, GROUP, MODE_FUSED>(gi, [&](int64_t u, const uint16_t*& ptr, CastParams& q) {
+    if (u >= b.units) return false;
+    const int j = find_job(b, u);
+    q = job_params(b, j);
+    const int64_t lg = u - b.job[j].first;  // the group within its job
+    ptr = q.w + lg * GROUP;
+    // rebase the outputs so that lane_group's global group index addresses them
+    q.out = (uint8_t*)q.out - (OutOf<FMT, BITS>::OUT4 ? b.job[j].first * (GROUP / 2) : b.job[j].first * GROUP);
+    q.scale_out = (uint8_t*)q.scale_out - b.job[j].first * ((FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4) ? 1 : 2);
+    if (q.zp_out) q.zp_out -= b.job[j].first;
+    return true;
+  });
 }
 
 // 128-thread CTAs, one group at a time without prefetch: several CTAs per SM
@@ -1580,7 +1750,11 @@ static bool launch_stream(const CastParams& p, int64_t group, cudaStream_t st) {
   const auto grid = [&](int ctas) { return dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>((steps + 7) / 8, 148 * ctas))); };
   const dim3 b(256);
   constexpr bool fp4 = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4);
-  if (group == 16) k_stream<FMT, BITS, 16, MODE><<<grid(stream_ctas<16, MODE>()), b, 0, st>>>(p);
+  constexpr int NS = 2;
+  const dim3 sg((unsigned)std::max<int64_t>(1, (steps + 8 * NS - 1) / (8 * NS)));
+  if (fp4 && group == 16) k_spans<FMT, BITS, 16, MODE, NS><<<sg, b, 0, st>>>(p);
+  else if (fp4 && group == 32) k_spans<FMT, BITS, 32, MODE, NS><<<sg, b, 0, st>>>(p);
+  else if (group == 16) k_stream<FMT, BITS, 16, MODE><<<grid(stream_ctas<16, MODE>()), b, 0, st>>>(p);
   else if (group == 32) k_stream<FMT, BITS, 32, MODE><<<grid(stream_ctas<32, MODE>()), b, 0, st>>>(p);
   else if constexpr (fp4) return false;
   else if (group == 64) k_stream<FMT, BITS, 64, MODE><<<grid(stream_ctas<64, MODE>()), b, 0, st>>>(p);
@@ -1772,17 +1946,25 @@ static bool launch_batch_fmt(CastBatch& b, cudaStream_t st) {
   }
   b.units = units;
   if (units == 0) return true;
+  if constexpr (!(FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4)) {
+    if ((a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) && (a.group == 64 || a.group == 128)) {
+      int64_t groups = 0;  // units are groups, one lane each (k_lanegroup_batch)
+      for (int i = 0; i < b.njobs; ++i) { b.job[i].first = groups; groups += b.job[i].rows * b.job[i].cols / a.group; }
+      b.units = groups;
+      const dim3 lg((unsigned)std::max<int64_t>(1, (groups + 255) / 256));
+      if (a.group == 64) k_lanegroup_batch<FMT, BITS, 64><<<lg, 256, 0, st>>>(b);
+      else k_lanegroup_batch<FMT, BITS, 128><<<lg, 256, 0, st>>>(b);
+      llmc::note_launch();
+      return true;
+    }
+  }
   if (a.strategy == LLMC_STRAT_GROUP || a.strategy == LLMC_STRAT_TENSOR_GROUP) {
     const auto grid = [&](int ctas) { return dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>((units + 7) / 8, 148 * ctas))); };
     const dim3 bl(256);
-    constexpr bool fp4 = (FMT == LLMC_FMT_NVFP4 || FMT == LLMC_FMT_MXFP4);
     const int64_t group = a.group;
     if (group == 16) k_stream_batch<FMT, BITS, 16><<<grid(stream_ctas<16, MODE_FUSED>()), bl, 0, st>>>(b);
     else if (group == 32) k_stream_batch<FMT, BITS, 32><<<grid(stream_ctas<32, MODE_FUSED>()), bl, 0, st>>>(b);
-    else if constexpr (fp4) return false;
-    else if (group == 64) k_stream_batch<FMT, BITS, 64><<<grid(stream_ctas<64, MODE_FUSED>()), bl, 0, st>>>(b);
-    else if (group == 128) k_stream_batch<FMT, BITS, 128><<<grid(stream_ctas<128, MODE_FUSED>()), bl, 0, st>>>(b);
-    else return false;
+    else return false;  // 64 / 128: k_lanegroup_batch above
     llmc::note_launch();
     return true;
   }
@@ -1800,6 +1982,15 @@ static bool launch_batch_fmt(CastBatch& b, cudaStream_t st) {
         all = tma_block_ok(p);
       }
       if (all) return launch_block_tma<FMT, BITS, MODE_FUSED>(b, st);
+    }
+    if (a.strategy == LLMC_STRAT_CHANNEL && pieces <= 256) {
+      const unsigned blocks = (unsigned)((units * 32 + 255) / 256);
+      if (pieces <= 32) k_rowwarp_batch<FMT, BITS, 1><<<blocks, 256, 0, st>>>(b);
+      else if (pieces <= 64) k_rowwarp_batch<FMT, BITS, 2><<<blocks, 256, 0, st>>>(b);
+      else if (pieces <= 128) k_rowwarp_batch<FMT, BITS, 4><<<blocks, 256, 0, st>>>(b);
+      else k_rowwarp_batch<FMT, BITS, 8><<<blocks, 256, 0, st>>>(b);
+      llmc::note_launch();
+      return true;
     }
     const unsigned g = (unsigned)std::min<int64_t>(units, 148 * 2);
     const unsigned g128 = (unsigned)std::min<int64_t>(units, 148 * 16);
@@ -1837,7 +2028,6 @@ static bool batchable(const CastParams& p) {
   if (a.strategy == LLMC_STRAT_CHANNEL || a.strategy == LLMC_STRAT_BLOCK) {
     if (p.cols % 16 || (uintptr_t)p.out % 16) return false;
     if (a.strategy == LLMC_STRAT_BLOCK && a.bw % 16) return false;
-    if (a.strategy == LLMC_STRAT_CHANNEL && p.cols <= 4096) return false;  // the warp-per-row kernel is faster
     const int64_t pc = a.strategy == LLMC_STRAT_CHANNEL ? p.cols / 16
                                                          : std::min<int64_t>(a.bh, p.rows) * (std::min<int64_t>(a.bw, p.cols) / 16);
     return pc <= 1024;
@@ -1989,6 +2179,8 @@ int llmc_modelfree_quantize_batch(const LlmcCastJob* jobs, int njobs, const Llmc
   b.base.mode = MODE_FUSED;
   b.base.fmt = fmt;
   if (int v = check_fmt(b.base.a, fmt)) return v;
+  CastBatch br;
+  memcpy(&br, &b, sizeof(b));
   for (int i = 0; i < njobs; ++i) {
     const LlmcCastJob& j = jobs[i];
     CastParams p = b.base;
@@ -2003,15 +2195,18 @@ int llmc_modelfree_quantize_batch(const LlmcCastJob* jobs, int njobs, const Llmc
       if (int v = launch(p, st)) return v;
       continue;
     }
-    CastJob& q = b.job[b.njobs++];
+    // CHANNEL rows of up to 4096 values go to their own batch (one warp per row)
+    CastBatch& t = (p.a.strategy == LLMC_STRAT_CHANNEL && p.cols <= 4096) ? br : b;
+    CastJob& q = t.job[t.njobs++];
     q.w = p.w; q.rows = p.rows; q.cols = p.cols; q.gs = p.gs;
     q.out = p.out; q.scale_out = p.scale_out; q.zp_out = p.zp_out;
-    if (b.njobs == kBatchMax) {
-      if (!launch_batch(b, st)) return LLMC_ENOSUPPORT;
-      b.njobs = 0;
+    if (t.njobs == kBatchMax) {
+      if (!launch_batch(t, st)) return LLMC_ENOSUPPORT;
+      t.njobs = 0;
     }
   }
   if (b.njobs > 0 && !launch_batch(b, st)) return LLMC_ENOSUPPORT;
+  if (br.njobs > 0 && !launch_batch(br, st)) return LLMC_ENOSUPPORT;
   return cudaGetLastError() == cudaSuccess ? LLMC_OK : LLMC_ECUDA;
 }
 

@@ -285,3 +285,40 @@ def test_repack_int4_int8_golden_and_large():
         np.testing.assert_array_equal(got.cpu().numpy(), ocasts.pack_int4_to_int8(t.numpy()))
     with pytest.raises(ValueError):
         ops.pack_int4_to_int8(torch.zeros(4, 3, dtype=torch.int8, device="cuda"))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("scheme", ["NVFP4A16", "MXFP4A16"])
+def test_fp4_groups_with_nonfinite_values_agree_across_kernels(scheme):
+    """FP4 groups whose values are all finite skip the explicit clamp to
+    [-6, 6] (the saturating E2M1 conversion clamps them); groups holding NaN
+    or +-inf keep it and take the IEEE quotient for the infinite values.  The
+    single-tensor kernel, the batched kernel and the general kernel (taken
+    for a weight that is not 32-byte aligned) must give the same bytes for
+    both kinds of group.  (For a group holding NaN or inf the reference's own
+    statistics are not finite; there is no reference value to hold the
+    kernels to, only their agreement.)"""
+    qa = preset_name_to_scheme(scheme, ["Linear"]).weights
+    rows, cols = 256, 1024
+    group = qa.group_size
+    g = torch.Generator().manual_seed(5)
+    w = 0.02 * torch.randn(rows, cols, generator=g)
+    w[0, 3] = 7.0  # one large value: its group's scale clamps the others
+    idx = torch.randperm(rows * cols, generator=g)[:48]
+    w.view(-1)[idx] = torch.tensor([float("nan"), float("inf"), -float("inf")]).repeat(16)
+    finite_groups = torch.isfinite(w).view(rows, cols // group, group).all(dim=-1)
+    w = w.to(torch.bfloat16).cuda()
+    store = torch.empty(rows * cols + 8, dtype=torch.bfloat16, device="cuda")
+    unaligned = store[8:].view(rows, cols)
+    unaligned.copy_(w)
+    finite = torch.nan_to_num(w, nan=0.0, posinf=0.0, neginf=0.0)
+    gs = ops.fused_global_scale([finite]) if scheme == "NVFP4A16" else None
+    single = ops.modelfree_quantize(w, qa, gs)
+    general = ops.modelfree_quantize(unaligned, qa, gs)
+    batched = ops.ModelfreeBatch([w, w], qa, [gs, gs]).run().results
+    for key in ("weight_packed", "weight_scale"):
+        ref = bits(single[key])
+        for r in batched:
+            np.testing.assert_array_equal(bits(r[key]), ref, err_msg=key)
+        np.testing.assert_array_equal(bits(general[key]), ref, err_msg=key)
+    assert not bool(finite_groups.all())  # both kinds of group were exercised
