@@ -1298,55 +1298,46 @@ __global__ void __launch_bounds__(256) k_spans(CastParams p) {
 // and combine the statistics by shuffles.  All loads of a warp are issued
 // before the first value is quantized; the grid is not persistent (the
 // structure of k_rowwarp).  src_of(gi, ptr, p) gives group gi's values and
-// parameters (false past the end); FUSED mode only uses these for batches.
-template <int FMT, int BITS, int GROUP, int MODE, class Src>
+// parameters (false past the end).
+template <int FMT, int BITS, int GROUP, class Src>
 __device__ __forceinline__ void lane_group(int64_t gi, Src src_of) {
   constexpr int NW = GROUP / 2;  // bf16x2 words per group
   constexpr bool OUT4 = OutOf<FMT, BITS>::OUT4;
   static_assert(GROUP == 64 || GROUP == 128, "lane groups of 64 or 128 values");
   const uint16_t* ptr = nullptr;
   CastParams p;
-  const bool valid = src_of(gi, ptr, p);
+  if (!src_of(gi, ptr, p)) return;
   uint32_t w[NW];
-  if (valid) {
 #pragma unroll
-    for (int k = 0; k < NW / 8; ++k) ld_v8(ptr + 16 * k, w + 8 * k);
-  }
-  if (!valid) return;
-  ElemQ e;
-  float s_store = 0.f, zp_store = 0.f;
-  if (MODE == MODE_FUSED) {
-    float mn, mx;
-    if (p.a.symmetric) {
-      mx = absmax_words<NW>(w);
-      mn = 0.0f;
-    } else {
-      minmax_words<NW>(w, mn, mx);
-    }
-    e = make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
+  for (int k = 0; k < NW / 8; ++k) ld_v8(ptr + 16 * k, w + 8 * k);
+  float mn, mx;
+  if (p.a.symmetric) {
+    mx = absmax_words<NW>(w);
+    mn = 0.0f;
   } else {
-    e = make_elemq_given<FMT>(p, gi);
+    minmax_words<NW>(w, mn, mx);
   }
+  float s_store = 0.f, zp_store = 0.f;
+  const ElemQ e = make_elemq_fused<FMT>(p, mn, mx, &s_store, &zp_store);
   const GQ g = to_gq(e);
   const float qmin = p.a.qmin(), qmax = p.a.qmax();
   uint32_t o[OUT4 ? NW / 4 : NW / 2];
-  if (MODE == MODE_GIVEN && g.f32q) quant_group<FMT, BITS, true, true, NW>(w, g, qmin, qmax, o);
-  else quant_group<FMT, BITS, false, MODE == MODE_GIVEN, NW>(w, g, qmin, qmax, o);
+  quant_group<FMT, BITS, false, false, NW>(w, g, qmin, qmax, o);
   uint8_t* out = (uint8_t*)p.out + (OUT4 ? gi * (GROUP / 2) : gi * GROUP);
 #pragma unroll
   for (int k = 0; k < (OUT4 ? NW / 4 : NW / 2) / 4; ++k) st_v4(out + 16 * k, o + 4 * k);
-  if (MODE == MODE_FUSED) store_scale<FMT>(p, gi, s_store, zp_store);
+  store_scale<FMT>(p, gi, s_store, zp_store);
 }
 
 // Batches of groups of 64 / 128 values (W4A16 and other integer group
 // schemes), one lane per group; a unit is a group, numbered across the jobs
 // (CastJob::first counts groups here).  Measured against k_stream_batch on
-// 32 weights of 4096 x 4096: W4A16 4.67 -> 4.80 TB/s (single tensors stay
-// on k_stream, which measured the same).
+// 32 weights of 4096 x 4096: W4A16 4.67 -> 4.80 TB/s, 5.75 in two-warp CTAs
+// (single tensors stay on k_stream, which measured the same as this layout).
 template <int FMT, int BITS, int GROUP>
 __global__ void __launch_bounds__(256) k_lanegroup_batch(const __grid_constant__ CastBatch b) {
   const int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  lane_group<FMT, BITS, GROUP, MODE_FUSED>(gi, [&](int64_t u, const uint16_t*& ptr, CastParams& q) {
+  lane_group<FMT, BITS, GROUP>(gi, [&](int64_t u, const uint16_t*& ptr, CastParams& q) {
     if (u >= b.units) return false;
     const int j = find_job(b, u);
     q = job_params(b, j);
